@@ -1,0 +1,236 @@
+/*
+ * twilight_b200.h — C ABI of the B200 (sm_100a) sparse decode-attention path.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL = legacy default stream) and returns an
+ * int status (TW_OK = 0).  Device buffers are owned by the caller; the library
+ * allocates nothing on the device except inside tw_host_alloc_mapped.
+ * All launches are asynchronous on the given stream.
+ *
+ * Layouts (D = head_dim = 128, E = cache entries = layers x kv_heads,
+ * entry = layer * kv_heads + kv_head, exactly as the reference):
+ *   slab K / V planes   [E][max_len][D]      K/V dtype, pinned + mapped host
+ *   page_min / page_max [E][page_cap][D]     K dtype (Quest metadata)
+ *   int4 codes          [E][max_len][D/2]    u8, byte j = code[2j] | code[2j+1] << 4
+ *   int4 scale / min    [E][max_len][D/gs]   K dtype, gs = quantisation group
+ *   queries             [G][R][D]            fp32 (the reference's q.float())
+ *
+ * Reference interfaces are cited as path:line inside the reference project
+ * (source/headinfer/headinfer/ abbreviated hi/).
+ */
+#ifndef TWILIGHT_B200_H
+#define TWILIGHT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  TW_ERR_INVALID_INDEX mirrors gather_kv's nonzero return for an
+ * out-of-range row (hi/cpu_kv_gather.cpp:9-10). */
+#define TW_OK 0
+#define TW_ERR_INVALID_INDEX 1
+#define TW_ERR_BAD_ARG 2
+#define TW_ERR_CAPACITY 3
+#define TW_ERR_ORDER 4
+#define TW_ERR_CUDA 5
+#define TW_ERR_TIMEOUT 6
+#define TW_ERR_UNSUPPORTED 7
+
+/* dtype codes */
+#define TW_F16 0
+#define TW_BF16 1
+#define TW_F32 2
+
+/* Human-readable status text; never NULL. */
+const char* tw_status_string(int status);
+/* cudaError_t recorded by the last call that returned TW_ERR_CUDA on this thread. */
+int tw_last_cuda_error(void);
+/* ABI version of this library. */
+int tw_abi_version(void);
+
+/* ---- host slab -------------------------------------------------------------
+ * Pinned, device-mapped host allocation for the K/V slab.  Replaces the
+ * reference's pin_memory slab (hi/quest_offload_cache.py:100-105) plus the
+ * cudaHostGetDevicePointer mapping of its zero-copy path
+ * (hi/resident_zero_copy.py:15-29).  *device_ptr is what kernels read. */
+int tw_host_alloc_mapped(size_t bytes, void** host_ptr, void** device_ptr);
+int tw_host_free(void* host_ptr);
+/* Device address of memory that is already pinned (e.g. torch pin_memory). */
+int tw_host_device_pointer(void* host_ptr, void** device_ptr);
+
+/* ---- Quest metadata ----------------------------------------------------------
+ * Page-wise channel min/max of K over complete block_size pages after the sink.
+ * Replaces QuestTopKOffloadedCache._build_metadata (hi/quest_offload_cache.py:276-289).
+ * keys: [n_entries][key_entry_stride] elements; page p of entry e covers rows
+ * sink + p*block_size .. +block_size of that entry.  Pages
+ * [first_page, first_page + n_pages) are written to
+ * page_min/page_max + e*meta_entry_stride + p*D. */
+int tw_quest_page_metadata(const void* keys, int64_t key_entry_stride, int n_entries,
+                           int sink, int block_size, int head_dim, int dtype,
+                           int first_page, int n_pages,
+                           void* page_min, void* page_max, int64_t meta_entry_stride,
+                           void* stream);
+
+/* ---- INT4 affine quantiser -----------------------------------------------------
+ * Group-wise asymmetric INT4 codes, bit-exact with affine_int4_pack
+ * (hi/twilight_offload_cache.py:25-37) applied to K.view(-1, group_size).
+ * keys: n_entries x n_tokens rows, row r of entry e at keys + (e*key_entry_stride + r)*D.
+ * Outputs row r of entry e at index (e*out_entry_stride + out_row_offset + r). */
+int tw_int4_pack(const void* keys, int64_t key_entry_stride, int n_entries, int64_t n_tokens,
+                 int head_dim, int group_size, int dtype,
+                 uint8_t* packed, void* scale, void* minimum,
+                 int64_t out_entry_stride, int64_t out_row_offset, void* stream);
+/* As tw_int4_pack with the rounding of the reference's `/ 15.0` made explicit:
+ * scale_div 0 = multiply by the fp32 reciprocal (torch executing it on CUDA,
+ * the reference's prefill device path; tw_int4_pack's mode), 1 = IEEE divide
+ * (torch executing it on CPU). */
+int tw_int4_pack_ex(const void* keys, int64_t key_entry_stride, int n_entries, int64_t n_tokens,
+                    int head_dim, int group_size, int dtype,
+                    uint8_t* packed, void* scale, void* minimum,
+                    int64_t out_entry_stride, int64_t out_row_offset, int scale_div,
+                    void* stream);
+
+/* ---- Quest upper-bound score ---------------------------------------------------
+ * score[g][r][p] = sum_d (q[g][r][d] > 0 ? max[g][p][d] : min[g][p][d]) * q[g][r][d],
+ * fp32, summed in the order of the reference's fused kernel
+ * (hi/twilight_fused_quest.py:13-46): lane l accumulates d = l, l+32, l+64, l+96,
+ * then a shfl-down tree 1,2,4,8,16.  page_min/max: [G][meta_group_stride] elements. */
+int tw_quest_score(const float* q, const void* page_min, const void* page_max,
+                   int groups, int heads_per_group, int n_pages, int64_t meta_group_stride,
+                   int head_dim, int dtype, float* scores, void* stream);
+
+/* ---- Top-k pages ----------------------------------------------------------------
+ * For each of `rows` rows of n scores: the k largest, written as ascending page
+ * ids [rows][k] (int32).  Replaces torch.topk(sorted=False) + sort
+ * (hi/twilight_offload_cache.py:1153-1155; hi/quest_offload_cache.py:373-374).
+ * Ties at the k-th value keep the lowest page ids.  Requires k <= n <= 16384. */
+int tw_topk_pages(const float* scores, int rows, int n, int k, int32_t* out_pages, void* stream);
+
+/* ---- INT4 QK estimate -------------------------------------------------------------
+ * logits[g][r][n] = (sum_d (code*scale + min) * q[g][r][d]) * (1/sqrt(D)) for the
+ * b0*block_size candidate tokens sink + pages[g][r][i]*block_size + j.
+ * Replaces fused_affine_int4_qk (hi/twilight_fused_qk.py:34-55) and the /sqrt(D)
+ * scaling (hi/twilight_offload_cache.py:1261).  packed/scale/minimum point at the
+ * layer's first entry; entry g is at +g*entry_stride_tokens rows. */
+int tw_int4_qk(const float* q, const uint8_t* packed, const void* scale, const void* minimum,
+               int64_t entry_stride_tokens, const int32_t* pages,
+               int groups, int heads_per_group, int b0_pages, int block_size, int sink,
+               int head_dim, int group_size, int dtype, float* logits, void* stream);
+
+/* ---- Top-p + GQA union ---------------------------------------------------------------
+ * Per (g, r) row: the smallest count c such that the c largest-logit candidates
+ * hold >= top_p of the softmax mass (the argsort/softmax/cumsum/searchsorted+1
+ * rule of hi/twilight_exact_top_p_graph.py:19-32, hi/twilight_offload_cache.py:1266-1310,
+ * budget_mode='dynamic').  Then per group g the sorted union of
+ * [0, sink_end) U [recent_start, old_length) U the R rows' selected positions
+ * (hi/twilight_offload_cache.py:1527-1549 + flatnonzero :1602-1614).
+ * union_pos: [G][pos_stride] int32 ascending, union_count: [G], head_count: [G][R].
+ * head_pos (nullable): [G][R][b0*block_size] each row's selected positions ascending.
+ * error_flag (nullable): set nonzero if a candidate position falls outside
+ * [0, old_length).  Launches G clusters of R CTAs (R <= 8). */
+int tw_top_p_union(const float* logits, const int32_t* pages,
+                   int groups, int heads_per_group, int b0_pages, int block_size, int sink,
+                   double top_p, int64_t old_length, int64_t sink_end, int64_t recent_start,
+                   int32_t* union_pos, int64_t pos_stride, int32_t* union_count,
+                   int32_t* head_count, int32_t* head_pos, int32_t* error_flag, void* stream);
+
+/* ---- whole-layer Twilight selection ----------------------------------------------------
+ * Quest score -> top-k pages -> INT4 QK -> top-p + union in one call (4 launches).
+ * Replaces TwilightMatchedBudgetOffloadedCache.prepare_layer_selection
+ * (hi/twilight_offload_cache.py:996-1843, gpu_compact_gqa_union path).
+ * workspace: >= tw_select_layer_workspace_size(...) bytes of device memory.
+ * pages_out: [G][R][b0] int32 (the Quest B0 pages, ascending). */
+size_t tw_select_layer_workspace_size(int groups, int heads_per_group, int n_pages, int b0_pages,
+                                      int block_size);
+int tw_select_layer(const float* q, const void* page_min, const void* page_max,
+                    int64_t meta_group_stride, int n_pages,
+                    const uint8_t* packed, const void* scale, const void* minimum,
+                    int64_t entry_stride_tokens,
+                    int groups, int heads_per_group, int b0_pages, int block_size, int sink,
+                    int head_dim, int group_size, int dtype, double top_p,
+                    int64_t old_length, int64_t sink_end, int64_t recent_start,
+                    int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
+                    int32_t* union_count, int32_t* head_count, int32_t* head_pos,
+                    int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- row gather ---------------------------------------------------------------------------
+ * out_k[i] = k[rows[i]], out_v[i] = v[rows[i]] for i < n, row_bytes each, read
+ * straight from (mapped host or device) memory by the GPU.  Same arguments and
+ * bounds contract as gather_kv (hi/cpu_kv_gather.cpp:3-16): an index outside
+ * [0, source_rows) is skipped and sets *error_flag (device int32) to 1.
+ * row_bytes must be a multiple of 16 and all pointers 16-byte aligned. */
+int tw_gather_kv(const void* k, const void* v, void* out_k, void* out_v,
+                 const int64_t* rows, int64_t n, int64_t source_rows, int64_t row_bytes,
+                 int32_t* error_flag, void* stream);
+
+/* ---- GQA union gather into the attention layout ----------------------------------------------
+ * Zero-copy gather of each group's union rows from the host slab, followed by
+ * the group's current-token row: out rows [cu[g], cu[g+1]) = slab rows of
+ * union_pos[g][0..count_g) then cur[g].  Writes cu_seqlens [G+1] int32.
+ * Replaces the flat CPU gather + chunked H2D + direct attention layout of
+ * update_layer_gqa_group_ragged (hi/twilight_offload_cache.py:2973-3101, :3307-3310)
+ * and the miss branch of assemble_zero_copy (hi/resident_zero_copy.cu:7-42).
+ * slab_k/slab_v: device-visible addresses of the K and V planes.
+ * Rows beyond rows_cap or positions outside [0, old_length) set *error_flag. */
+int tw_gather_union(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+                    int groups, int64_t old_length,
+                    const int32_t* union_pos, int64_t pos_stride, const int32_t* union_count,
+                    const void* cur_k, const void* cur_v, int head_dim, int dtype,
+                    void* out_k, void* out_v, int64_t rows_cap, int32_t* cu_seqlens,
+                    int32_t* error_flag, void* stream);
+
+/* ---- Quest per-query-head gather ------------------------------------------------------------------
+ * Per (g, r): rows [0, sink_end) U {sink + pages[g][r][i]*block_size + j} U
+ * [recent_start, old_length) then the group's current token, each head one
+ * segment of the flat layout (segment s = g*R + r, equal lengths
+ * seg_len = sink_end + k*block_size + (old_length - recent_start) + 1).
+ * Replaces _selected_positions + update_layer_flat_ragged packing
+ * (hi/quest_offload_cache.py:403-511, :724-987) and the per-entry pack of update
+ * (:578-630). */
+int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+                          int groups, int heads_per_group, int64_t old_length,
+                          int64_t sink_end, int64_t recent_start, int sink, int block_size,
+                          const int32_t* pages, int k_pages,
+                          const void* cur_k, const void* cur_v, int head_dim, int dtype,
+                          void* out_k, void* out_v, int32_t* error_flag, void* stream);
+
+/* ---- new-token append ------------------------------------------------------------------------------
+ * Writes each group's current K/V row to slab position `position`, folds it
+ * into the running Quest page min/max (page (position-sink)/block_size, when
+ * position >= sink) and INT4-packs it.  page_min/page_max/packed/scale/minimum
+ * may be NULL to skip that part.  Replaces the new-KV D2H
+ * (hi/quest_offload_cache.py:230-274, hi/twilight_offload_cache.py:551-794) and
+ * extends the prefill-only metadata (hi/quest_offload_cache.py:276-289,
+ * hi/twilight_offload_cache.py:925-936) to appended tokens. */
+int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int first_entry, int groups,
+                    int64_t position, const void* cur_k, const void* cur_v,
+                    int head_dim, int dtype, int sink, int block_size,
+                    void* page_min, void* page_max, int64_t meta_entry_stride,
+                    uint8_t* packed, void* scale, void* minimum, int group_size,
+                    void* stream);
+
+/* ---- sparse GQA decode attention -------------------------------------------------------------------------
+ * out[s][r] = softmax(q[s][r] . K[cu[s]:cu[s+1]]^T * softmax_scale) . V[cu[s]:cu[s+1]]
+ * for s < segments, r < heads_per_segment; q_len = 1 so every key is visible.
+ * Split-K flash-decode with a log-sum-exp merge, fp32 accumulation.
+ * Replaces flash_attn_varlen_func as called by hi/mp.py:258-279 (wrapper :21-52).
+ * q: [S][R][D] in `dtype`; k/v: [rows][D] in `dtype`; out: [S][R][D] in out_dtype
+ * (dtype or TW_F32); lse (nullable): [S][R] fp32 natural-log sum-exp.
+ * max_seqlen_k: an upper bound of cu[s+1]-cu[s] (sizes the split grid).
+ * workspace: >= tw_decode_attention_workspace_size(...) bytes; its counter area
+ * must be zero before the first call (the kernel leaves it zero). */
+size_t tw_decode_attention_workspace_size(int segments, int heads_per_segment, int max_seqlen_k,
+                                          int head_dim);
+int tw_decode_attention(const void* q, const void* k, const void* v, const int32_t* cu_seqlens,
+                        int segments, int heads_per_segment, int max_seqlen_k, int head_dim,
+                        int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TWILIGHT_B200_H */

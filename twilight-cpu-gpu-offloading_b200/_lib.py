@@ -1,0 +1,111 @@
+"""ctypes binding of the C ABI (include/twilight_b200.h).
+
+The library is the only compute path: there is no CPU fallback.  Loading
+fails loudly when libtwilight_b200.so is absent.  Status codes map to the
+exception types the reference raises: ValueError for bad shapes/arguments and
+invalid row indices (hi/cpu_kv_gather.py:35-36), RuntimeError for CUDA and
+capacity errors (hi/quest_offload_cache.py:104-106).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libtwilight_b200.so"
+
+TW_OK = 0
+TW_ERR_INVALID_INDEX = 1
+TW_ERR_BAD_ARG = 2
+TW_ERR_CAPACITY = 3
+TW_ERR_ORDER = 4
+TW_ERR_CUDA = 5
+TW_ERR_TIMEOUT = 6
+TW_ERR_UNSUPPORTED = 7
+
+TW_F16 = 0
+TW_BF16 = 1
+TW_F32 = 2
+
+P = ctypes.c_void_p
+I32 = ctypes.c_int
+I64 = ctypes.c_int64
+SZ = ctypes.c_size_t
+DBL = ctypes.c_double
+FLT = ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/twilight_b200.h
+SIGNATURES = {
+    "tw_status_string": (ctypes.c_char_p, [I32]),
+    "tw_last_cuda_error": (I32, []),
+    "tw_abi_version": (I32, []),
+    "tw_host_alloc_mapped": (I32, [SZ, ctypes.POINTER(P), ctypes.POINTER(P)]),
+    "tw_host_free": (I32, [P]),
+    "tw_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
+    "tw_quest_page_metadata": (I32, [P, I64, I32, I32, I32, I32, I32, I32, I32, P, P, I64, P]),
+    "tw_int4_pack": (I32, [P, I64, I32, I64, I32, I32, I32, P, P, P, I64, I64, P]),
+    "tw_int4_pack_ex": (I32, [P, I64, I32, I64, I32, I32, I32, P, P, P, I64, I64, I32, P]),
+    "tw_quest_score": (I32, [P, P, P, I32, I32, I32, I64, I32, I32, P, P]),
+    "tw_topk_pages": (I32, [P, I32, I32, I32, P, P]),
+    "tw_int4_qk": (I32, [P, P, P, P, I64, P, I32, I32, I32, I32, I32, I32, I32, I32, P, P]),
+    "tw_top_p_union": (I32, [P, P, I32, I32, I32, I32, I32, DBL, I64, I64, I64, P, I64, P, P, P,
+                             P, P]),
+    "tw_select_layer_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
+    "tw_select_layer": (I32, [P, P, P, I64, I32, P, P, P, I64, I32, I32, I32, I32, I32, I32, I32,
+                              I32, DBL, I64, I64, I64, P, P, I64, P, P, P, P, P, SZ, P]),
+    "tw_gather_kv": (I32, [P, P, P, P, P, I64, I64, I64, P, P]),
+    "tw_gather_union": (I32, [P, P, I64, I32, I32, I64, P, I64, P, P, P, I32, I32, P, P, I64, P,
+                              P, P]),
+    "tw_gather_quest_heads": (I32, [P, P, I64, I32, I32, I32, I64, I64, I64, I32, I32, P, I32, P,
+                                    P, I32, I32, P, P, P, P]),
+    "tw_append_token": (I32, [P, P, I64, I32, I32, I64, P, P, I32, I32, I32, I32, P, P, I64, P, P,
+                              P, I32, P]),
+    "tw_decode_attention_workspace_size": (SZ, [I32, I32, I32, I32]),
+    "tw_decode_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P, SZ, P]),
+}
+
+_lib = None
+
+
+class TwilightError(RuntimeError):
+    pass
+
+
+def load():
+    """Load the extension or raise (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH.name} is missing: build it with "
+            "`python twilight-cpu-gpu-offloading_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def status_string(status: int) -> str:
+    return load().tw_status_string(status).decode()
+
+
+def check(status: int, what: str = "") -> None:
+    if status == TW_OK:
+        return
+    msg = f"{what}: {status_string(status)}" if what else status_string(status)
+    if status == TW_ERR_CUDA:
+        msg += f" (cudaError {load().tw_last_cuda_error()})"
+        raise TwilightError(msg)
+    if status in (TW_ERR_INVALID_INDEX, TW_ERR_BAD_ARG, TW_ERR_ORDER, TW_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    if status == TW_ERR_TIMEOUT:
+        raise TimeoutError(msg)
+    raise RuntimeError(msg)
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)

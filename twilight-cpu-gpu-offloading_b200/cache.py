@@ -1,0 +1,851 @@
+"""Drop-in offload caches: the reference's operator API over the sm_100a kernels.
+
+QuestTopKOffloadedCache mirrors hi/quest_offload_cache.py:23 (per-query-head
+Quest pages) and TwilightMatchedBudgetOffloadedCache mirrors
+hi/twilight_offload_cache.py:133 (Quest B0 -> INT4 QK -> top-p -> GQA union,
+dynamic budget).  Same constructor keywords, method names, return tuples and
+exception types; the full K/V history lives in a pinned, device-mapped host
+slab and every selection, gather and attention step runs as CUDA kernels of
+libtwilight_b200.so on the caller's current stream.  Selections stay on the
+device: the only host synchronisation on the reference-compatible path is
+the read of the G union lengths that update_layer_gqa_group_ragged must
+return as Python ints; attend_layer needs none.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import math
+import time
+from collections import defaultdict
+from typing import Any, Optional
+
+import torch
+
+from . import _lib, ops
+from .slab import MappedHostSlab, SequentialCacheState, SlabGeometry
+
+HEAD_DIM = ops.HEAD_DIM
+
+
+def _contiguous_entries(entries: list[int]) -> int:
+    first = entries[0]
+    if list(entries) != list(range(first, first + len(entries))):
+        raise ValueError("layer entries must be contiguous (layer * kv_heads + kv_head)")
+    return first
+
+
+class QuestTopKOffloadedCache:
+    """Pinned-host full cache with per-query-head Quest top-k pages.
+
+    hi/quest_offload_cache.py:23-1055.  Extra keyword (not in the reference):
+    ``incremental_page_metadata`` (default False = the reference's candidate
+    window capped at the prompt's pages, hi/twilight_offload_cache.py:1062-1069;
+    True = pages completed by appended tokens become candidates).
+    """
+
+    def __init__(self, *, num_cache_entries: int, max_cache_len: int, head_dim: int,
+                 num_query_heads_per_kv: int, dtype: torch.dtype, device: torch.device | str,
+                 sink_tokens: int = 64, recent_tokens: int = 256, block_size: int = 16,
+                 budget_fraction: float = 0.05, selection_interval: int = 1,
+                 max_selected_history_fraction: Optional[float] = None,
+                 layer_batched_selection: bool = False, layer_flat_ragged_execution: bool = False,
+                 sparse_gather_stabilized: bool = False,
+                 per_head_varlen_attention_reference: bool = False,
+                 incremental_page_metadata: bool = False, **ignored: Any) -> None:
+        device = torch.device(device)
+        if device.type != "cuda" or not torch.cuda.is_available():
+            raise ValueError("an operational CUDA device is required")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        if sink_tokens < 0 or recent_tokens <= 0 or block_size <= 0:
+            raise ValueError("invalid sink/recent/block configuration")
+        if not 0.0 < budget_fraction <= 1.0:
+            raise ValueError("budget_fraction must be in (0, 1]")
+        if selection_interval <= 0:
+            raise ValueError("selection_interval must be positive")
+        if max_selected_history_fraction is None:
+            max_selected_history_fraction = budget_fraction
+        if not 0.0 < max_selected_history_fraction <= 1.0:
+            raise ValueError("max_selected_history_fraction must be in (0, 1]")
+        if num_query_heads_per_kv <= 0:
+            raise ValueError("num_query_heads_per_kv must be positive")
+        if head_dim != HEAD_DIM:
+            raise ValueError(f"head_dim must be {HEAD_DIM} (the sm_100a kernels' tile)")
+        if num_query_heads_per_kv > 8:
+            raise ValueError("at most 8 query heads per KV head are supported")
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("K/V dtype must be float16 or bfloat16")
+        if layer_flat_ragged_execution and not layer_batched_selection:
+            raise ValueError("layer-flat ragged execution requires layer-batched selection")
+        if sparse_gather_stabilized and not layer_flat_ragged_execution:
+            raise ValueError("stabilized sparse gather requires layer-flat ragged execution")
+        _lib.load()  # fail loudly without the extension
+        self.geometry = SlabGeometry(num_entries=num_cache_entries, batch_size=1,
+                                     max_cache_len=max_cache_len, head_dim=head_dim)
+        self.dtype = dtype
+        self.device = device
+        self.allocated_capacity = max_cache_len
+        self.num_query_heads_per_kv = num_query_heads_per_kv
+        self.sink_tokens = sink_tokens
+        self.recent_tokens = recent_tokens
+        self.block_size = block_size
+        self.budget_fraction = budget_fraction
+        self.selection_interval = int(selection_interval)
+        self.layer_batched_selection = bool(layer_batched_selection)
+        self.layer_flat_ragged_execution = bool(layer_flat_ragged_execution)
+        self.sparse_gather_stabilized = bool(sparse_gather_stabilized)
+        self.per_head_varlen_attention_reference = bool(per_head_varlen_attention_reference)
+        self.max_selected_history_fraction = max_selected_history_fraction
+        self.incremental_page_metadata = bool(incremental_page_metadata)
+        self.ignored_options = dict(ignored)
+        self._bookkeeping = SequentialCacheState(num_cache_entries, max_cache_len)
+        self._logical_lengths = self._bookkeeping.logical_lengths
+        self._initialized = [False] * num_cache_entries
+        self._seen_tokens = 0
+        self._prompt_length: Optional[int] = None
+
+        self._slab = MappedHostSlab(self.geometry, dtype)
+        self.page_capacity = max(1, math.ceil(max(0, max_cache_len - sink_tokens) / block_size))
+        E, D = num_cache_entries, head_dim
+        self._page_min = torch.empty((E, self.page_capacity, D), dtype=dtype, device=device)
+        self._page_max = torch.empty_like(self._page_min)
+        self._meta_pages = [0] * E  # prompt pages with metadata per entry
+        max_pages = math.ceil(max(0, max_cache_len - sink_tokens) / block_size)
+        self.max_selected_tokens_per_query_head = min(
+            max_cache_len,
+            sink_tokens + recent_tokens
+            + max(1, math.ceil(max_selected_history_fraction * max_pages)) * block_size)
+        self._error_flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._quest_pages: dict[int, tuple[Optional[torch.Tensor], int, int]] = {}
+        self._quest_prepared: set[int] = set()
+        self._last_query_head_lengths: list[Optional[tuple[int, ...]]] = [None] * E
+        self._quest_pack: Optional[torch.Tensor] = None
+        self._layer_bufs: dict[int, dict[str, Any]] = {}
+        self._capture_selection_trace = False
+        self._selection_trace: list[dict[str, Any]] = []
+        self.metrics_enabled = False
+        self.metrics: dict[str, float] = defaultdict(float)
+        self._timing_events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    # ------------------------------------------------------------ construction --
+    @classmethod
+    def from_llama_model(cls, model: torch.nn.Module, **kwargs: Any):
+        """hi/quest_offload_cache.py:175-190."""
+        config = model.config
+        parameter = next(model.parameters())
+        return cls(
+            num_cache_entries=config.num_hidden_layers * config.num_key_value_heads,
+            head_dim=getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads,
+            num_query_heads_per_kv=config.num_attention_heads // config.num_key_value_heads,
+            dtype=parameter.dtype, device=parameter.device, **kwargs)
+
+    # ------------------------------------------------------------------ views --
+    def _host_tensor(self, kind: str, entry: int) -> torch.Tensor:
+        return self._slab.entry(kind, entry)
+
+    @property
+    def _host_key_rows(self) -> torch.Tensor:
+        return self._slab.rows[0].reshape(-1, self.geometry.head_dim)
+
+    @property
+    def _host_value_rows(self) -> torch.Tensor:
+        return self._slab.rows[1].reshape(-1, self.geometry.head_dim)
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    # ---------------------------------------------------------------- metrics --
+    def reset_metrics(self) -> None:
+        self.metrics = defaultdict(float)
+        self._timing_events = []
+
+    def enable_metrics(self, enabled: bool = True) -> None:
+        self.metrics_enabled = enabled
+        if enabled:
+            self.reset_metrics()
+
+    def _phase_start(self) -> Optional[torch.cuda.Event]:
+        if not self.metrics_enabled:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        return ev
+
+    def _phase_end(self, name: str, start: Optional[torch.cuda.Event]) -> None:
+        if start is None:
+            return
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(torch.cuda.current_stream(self.device))
+        self._timing_events.append((name, start, end))
+
+    def resolve_metrics(self) -> dict[str, float]:
+        self.synchronize()
+        for name, start, end in self._timing_events:
+            self.metrics[f"{name}_cuda_seconds"] += start.elapsed_time(end) / 1000.0
+            self.metrics[f"{name}_event_intervals"] += 1
+        self._timing_events = []
+        return dict(self.metrics)
+
+    def enable_selection_trace(self, enabled: bool = True) -> None:
+        self._capture_selection_trace = bool(enabled)
+        self._selection_trace = []
+
+    def selection_trace(self) -> list[dict[str, Any]]:
+        return list(self._selection_trace)
+
+    # ------------------------------------------------------------ bookkeeping --
+    def _check_error_flag(self) -> None:
+        flag = int(self._error_flag.item())
+        if flag:
+            self._error_flag.zero_()
+            _lib.check(flag, "device-side check")
+
+    def _window(self, old_length: int) -> dict[str, int]:
+        sink_end = min(self.sink_tokens, old_length)
+        recent_start = max(sink_end, old_length - max(0, self.recent_tokens - 1))
+        eligible = max(0, recent_start - sink_end)
+        return dict(sink_end=sink_end, recent_start=recent_start, eligible=eligible,
+                    candidate_pages=eligible // self.block_size)
+
+    def _metadata_pages(self, entries: list[int], old_length: int) -> int:
+        if self.incremental_page_metadata:
+            return max(0, old_length - self.sink_tokens) // self.block_size if old_length > self.sink_tokens else 0
+        return min(self._meta_pages[e] for e in entries)
+
+    def _build_metadata(self, entry: int, key_states: torch.Tensor) -> None:
+        """Quest page min/max of the prompt (hi/quest_offload_cache.py:276-289) plus
+        the running min/max of the trailing partial page, continued on append."""
+        keys = key_states[0, 0].contiguous()
+        S = int(keys.shape[0])
+        complete = max(0, S - self.sink_tokens) // self.block_size if S > self.sink_tokens else 0
+        if complete:
+            _lib.check(_lib.load().tw_quest_page_metadata(
+                keys.data_ptr(), S * HEAD_DIM, 1, self.sink_tokens, self.block_size, HEAD_DIM,
+                ops._kv_code(self.dtype), 0, complete,
+                self._page_min[entry].data_ptr(), self._page_max[entry].data_ptr(),
+                self.page_capacity * HEAD_DIM, self._stream()), "quest_page_metadata")
+        partial = S - self.sink_tokens - complete * self.block_size if S > self.sink_tokens else 0
+        if partial > 0 and complete < self.page_capacity:
+            off = complete * HEAD_DIM * keys.element_size()
+            _lib.check(_lib.load().tw_quest_page_metadata(
+                keys.data_ptr(), S * HEAD_DIM, 1, self.sink_tokens + complete * self.block_size,
+                partial, HEAD_DIM, ops._kv_code(self.dtype), 0, 1,
+                self._page_min[entry].data_ptr() + off, self._page_max[entry].data_ptr() + off,
+                self.page_capacity * HEAD_DIM, self._stream()), "quest_page_metadata")
+        self._meta_pages[entry] = complete
+
+    def _schedule_d2h(self, entry: int, start: int, key_states, value_states) -> None:
+        n = int(key_states.shape[-2])
+        self._host_tensor("key", entry)[0, 0, start:start + n].copy_(key_states[0, 0], non_blocking=True)
+        self._host_tensor("value", entry)[0, 0, start:start + n].copy_(value_states[0, 0], non_blocking=True)
+
+    def _append_rows(self, first_entry: int, groups: int, position: int, k_new: torch.Tensor,
+                     v_new: torch.Tensor) -> None:
+        """Current token -> slab row `position`, running page min/max, INT4 codes."""
+        packed = getattr(self, "_packed", None)
+        lib = _lib.load()
+        _lib.check(lib.tw_append_token(
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            first_entry, groups, position, k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM,
+            ops._kv_code(self.dtype), self.sink_tokens, self.block_size,
+            self._page_min.data_ptr(), self._page_max.data_ptr(), self.page_capacity * HEAD_DIM,
+            None if packed is None else packed.data_ptr(),
+            None if packed is None else self._scale.data_ptr(),
+            None if packed is None else self._minimum.data_ptr(),
+            getattr(self, "int4_group_size", 128), self._stream()), "append_token")
+
+    # ---------------------------------------------------------------- prefill --
+    def _prefill(self, key_states, value_states, layer_idx: int, append_length: int,
+                 old_length: int) -> None:
+        if old_length != 0:
+            raise ValueError("chunked/multiple prefill updates are unsupported")
+        if self._prompt_length is None:
+            self._prompt_length = append_length
+        elif self._prompt_length != append_length:
+            raise RuntimeError("cache entries received unequal prompt lengths")
+        self._build_metadata(layer_idx, key_states)
+        self._schedule_d2h(layer_idx, 0, key_states, value_states)
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs: Optional[dict[str, Any]] = None):
+        """hi/quest_offload_cache.py:513-665.  Prefill: metadata + slab copy, returns the
+        inputs.  Decode: per-query-head pack [1, R, T, D] for K and V."""
+        if key_states.shape != value_states.shape or key_states.shape[:2] != (1, 1):
+            raise ValueError("expected identical head-wise [1, 1, seq, dim] K/V")
+        if not key_states.is_cuda or key_states.device != self.device:
+            raise ValueError("K/V must be on the cache device")
+        append_length = int(key_states.shape[-2])
+        old_length, _ = self._bookkeeping.preview(layer_idx, append_length)
+        if append_length > 1:
+            self._bookkeeping.advance(layer_idx, append_length)
+            self._seen_tokens = self._bookkeeping.seen_tokens
+            self._initialized[layer_idx] = True
+            self._prefill(key_states, value_states, layer_idx, append_length, old_length)
+            return key_states, value_states
+        query = None if cache_kwargs is None else cache_kwargs.get("query_states")
+        R = self.num_query_heads_per_kv
+        if query is None or tuple(query.shape) != (1, R, 1, HEAD_DIM):
+            raise ValueError("decode requires post-RoPE query_states")
+        self._bookkeeping.advance(layer_idx, 1)
+        self._seen_tokens = self._bookkeeping.seen_tokens
+        self._initialized[layer_idx] = True
+        return self._quest_decode_entry(layer_idx, query, key_states, value_states, old_length)
+
+    # ---------------------------------------------------------- Quest per-Q path --
+    def _quest_select(self, entries: list[int], queries: list[torch.Tensor], old_length: int):
+        w = self._window(old_length)
+        budget = min(w["candidate_pages"],
+                     max(1, math.ceil(self.budget_fraction * w["eligible"] / self.block_size)))
+        candidate_pages = min(w["candidate_pages"], self._metadata_pages(entries, old_length))
+        budget = min(budget, candidate_pages)
+        first = _contiguous_entries(entries)
+        if budget == 0:
+            return None, 0, w
+        q = torch.stack([query[0, :, 0] for query in queries], dim=0).float().contiguous()
+        G = len(entries)
+        start = self._phase_start()
+        scores = ops.quest_score(q, self._page_min[first:first + G], self._page_max[first:first + G],
+                                 candidate_pages)
+        pages = ops.topk_pages(scores, budget)
+        self._phase_end("selector", start)
+        if self._capture_selection_trace:
+            decode_step = old_length - (self._prompt_length or 0) + 1
+            cpu = pages.cpu()
+            for g, entry in enumerate(entries):
+                for r in range(self.num_query_heads_per_kv):
+                    self._selection_trace.append({
+                        "decode_step": decode_step, "entry": entry, "query_head_in_group": r,
+                        "selected_page_indices": tuple(int(v) for v in cpu[g, r].tolist())})
+        return pages, budget, w
+
+    def prepare_layer_selection(self, *, entries: list[int], queries: list[torch.Tensor]) -> None:
+        """hi/quest_offload_cache.py:299-401 (pages stay on the device).  With
+        selection_interval > 1 the cached pages are reused between refreshes."""
+        if not self.layer_batched_selection:
+            return
+        self._validate_layer(entries, queries)
+        old_length = self._layer_old_length(entries)
+        if self._prompt_length is None:
+            raise RuntimeError("prompt length is missing")
+        if not self._refresh_due(entries, old_length):
+            self._quest_prepared.update(entries)
+            return
+        pages, budget, _ = self._quest_select(entries, queries, old_length)
+        for g, entry in enumerate(entries):
+            self._quest_pages[entry] = (pages, g, budget)
+        self._quest_prepared.update(entries)
+
+    def _refresh_due(self, entries, old_length: int) -> bool:
+        decode_step = old_length - (self._prompt_length or 0) + 1
+        return (any(e not in self._quest_pages for e in entries)
+                or (decode_step - 1) % self.selection_interval == 0)
+
+    def _quest_pages_for(self, entries: list[int], queries, old_length: int):
+        """Pages [G,R,k] for the entries: prepared or cached, else selected now."""
+        prepared = all(e in self._quest_prepared for e in entries)
+        for e in entries:
+            self._quest_prepared.discard(e)
+        if not prepared and self._refresh_due(entries, old_length):
+            pages, budget, w = self._quest_select(entries, queries, old_length)
+            for g, entry in enumerate(entries):
+                self._quest_pages[entry] = (pages, g, budget)
+            return pages, budget, w
+        items = [self._quest_pages[e] for e in entries]
+        budget = items[0][2]
+        w = self._window(old_length)
+        if budget == 0:
+            return None, 0, w
+        base = items[0][0]
+        if all(it[0] is base for it in items) and [it[1] for it in items] == list(
+                range(items[0][1], items[0][1] + len(entries))):
+            g0 = items[0][1]
+            return base[g0:g0 + len(entries)], budget, w
+        return torch.cat([it[0][it[1]:it[1] + 1] for it in items], dim=0), budget, w
+
+    def _validate_layer(self, entries, queries) -> None:
+        if len(entries) != len(queries) or not entries:
+            raise ValueError("entries and queries must be non-empty and aligned")
+        if len(set(entries)) != len(entries):
+            raise ValueError("layer entries must be unique")
+        shape = (1, self.num_query_heads_per_kv, 1, HEAD_DIM)
+        if any(tuple(q.shape) != shape for q in queries):
+            raise ValueError("unexpected layer Query shape")
+        _contiguous_entries(entries)
+
+    def _layer_old_length(self, entries) -> int:
+        lengths = [self._logical_lengths[e] for e in entries]
+        if len(set(lengths)) != 1:
+            raise AssertionError("layer KV entries have unequal logical lengths")
+        return lengths[0]
+
+    def _quest_pack_buffers(self, rows: int) -> tuple[torch.Tensor, torch.Tensor]:
+        if self._quest_pack is None or self._quest_pack.shape[1] < rows:
+            self._quest_pack = torch.empty((2, rows, HEAD_DIM), dtype=self.dtype, device=self.device)
+        return self._quest_pack[0, :rows], self._quest_pack[1, :rows]
+
+    def _quest_gather(self, first: int, groups: int, pages, k_pages: int, w, old_length: int,
+                      k_new: torch.Tensor, v_new: torch.Tensor):
+        R = self.num_query_heads_per_kv
+        seg_len = w["sink_end"] + k_pages * self.block_size + (old_length - w["recent_start"]) + 1
+        total = seg_len * groups * R
+        out_k, out_v = self._quest_pack_buffers(total)
+        start = self._phase_start()
+        _lib.check(_lib.load().tw_gather_quest_heads(
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            first, groups, R, old_length, w["sink_end"], w["recent_start"], self.sink_tokens,
+            self.block_size, None if pages is None else pages.data_ptr(), k_pages,
+            k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM, ops._kv_code(self.dtype),
+            out_k.data_ptr(), out_v.data_ptr(), self._error_flag.data_ptr(), self._stream()),
+            "gather_quest_heads")
+        self._phase_end("h2d", start)
+        if self.metrics_enabled:
+            self.metrics["h2d_bytes"] += 2 * (seg_len - 1) * groups * R * HEAD_DIM * k_new.element_size()
+            self.metrics["h2d_copy_calls"] += 1
+        return out_k, out_v, seg_len
+
+    def _quest_decode_entry(self, entry: int, query, key_states, value_states, old_length: int):
+        pages, budget, w = self._quest_pages_for([entry], [query], old_length)
+        k_new = key_states[0, 0].contiguous()
+        v_new = value_states[0, 0].contiguous()
+        out_k, out_v, seg_len = self._quest_gather(entry, 1, pages, budget, w, old_length, k_new, v_new)
+        self._append_rows(entry, 1, old_length, k_new, v_new)
+        R = self.num_query_heads_per_kv
+        self._last_query_head_lengths[entry] = tuple([seg_len] * R)
+        return out_k.view(1, R, seg_len, HEAD_DIM), out_v.view(1, R, seg_len, HEAD_DIM)
+
+    def update_layer_flat_ragged(self, *, key_states: list[torch.Tensor],
+                                 value_states: list[torch.Tensor], queries: list[torch.Tensor],
+                                 entries: list[int]):
+        """hi/quest_offload_cache.py:724-987: per-query-head segments of one layer in
+        one flat ragged batch.  Returns (K [sum_T,1,D], V, cu_seqlens int32, max, lengths)."""
+        if not self.layer_flat_ragged_execution:
+            raise RuntimeError("layer-flat ragged execution is disabled")
+        if not (len(entries) == len(key_states) == len(value_states) == len(queries) and entries):
+            raise ValueError("layer entries, K/V, and Queries must be aligned")
+        self._validate_layer(entries, queries)
+        for k, v in zip(key_states, value_states):
+            if k.shape != v.shape or tuple(k.shape) != (1, 1, 1, HEAD_DIM):
+                raise ValueError("layer-flat decode expects [1, 1, 1, dim] K/V")
+        old_length = self._advance_layer(entries)
+        first = entries[0]
+        G = len(entries)
+        pages, budget, w = self._quest_pages_for(entries, queries, old_length)
+        k_new = torch.cat([k[0, 0] for k in key_states], dim=0)
+        v_new = torch.cat([v[0, 0] for v in value_states], dim=0)
+        out_k, out_v, seg_len = self._quest_gather(first, G, pages, budget, w, old_length, k_new, v_new)
+        self._append_rows(first, G, old_length, k_new, v_new)
+        R = self.num_query_heads_per_kv
+        total = seg_len * G * R
+        cu = torch.arange(0, G * R + 1, dtype=torch.int32, device=self.device) * seg_len
+        lengths = tuple([seg_len] * (G * R))
+        for g, entry in enumerate(entries):
+            self._last_query_head_lengths[entry] = tuple([seg_len] * R)
+        return out_k.view(total, 1, HEAD_DIM), out_v.view(total, 1, HEAD_DIM), cu, seg_len, lengths
+
+    def _advance_layer(self, entries: list[int]) -> int:
+        olds = []
+        for entry in entries:
+            self._bookkeeping.preview(entry, 1)
+            old, _ = self._bookkeeping.advance(entry, 1)
+            self._initialized[entry] = True
+            olds.append(old)
+        self._seen_tokens = self._bookkeeping.seen_tokens
+        if len(set(olds)) != 1:
+            raise AssertionError("layer KV entries have unequal logical lengths")
+        return olds[0]
+
+    # ------------------------------------------------------------------- misc --
+    def get_last_query_head_lengths(self, entry: int) -> Optional[tuple[int, ...]]:
+        return self._last_query_head_lengths[entry]
+
+    def synchronize(self) -> None:
+        torch.cuda.current_stream(self.device).synchronize()
+        self._check_error_flag()
+
+    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
+        return self._logical_lengths[0 if layer_idx is None else layer_idx]
+
+    def get_max_length(self) -> Optional[int]:
+        return self.allocated_capacity
+
+    def reorder_cache(self, beam_idx: torch.LongTensor) -> None:
+        del beam_idx
+        raise NotImplementedError("batch-size-1 cache does not support reordering")
+
+    def _device_bytes(self) -> int:
+        tensors = [self._page_min, self._page_max, self._error_flag]
+        if self._quest_pack is not None:
+            tensors.append(self._quest_pack)
+        for bufs in self._layer_bufs.values():
+            tensors.extend(t for t in bufs.values() if isinstance(t, torch.Tensor))
+        return sum(t.numel() * t.element_size() for t in tensors)
+
+    def state_snapshot(self) -> dict[str, Any]:
+        return {
+            "logical_length": self.get_seq_length(),
+            "allocated_capacity": self.allocated_capacity,
+            "initialized_entries": sum(self._initialized),
+            "host_slab_bytes": self._slab.nbytes,
+            "host_slab_pinned": True,
+            "host_slab_device_mapped": True,
+            "metadata_gpu_bytes": 2 * self._page_min.numel() * self._page_min.element_size(),
+            "execution_buffer_gpu_bytes": self._device_bytes(),
+            "block_size": self.block_size,
+            "budget_fraction": self.budget_fraction,
+            "selection_interval": self.selection_interval,
+            "layer_batched_selection": self.layer_batched_selection,
+            "layer_flat_ragged_execution": self.layer_flat_ragged_execution,
+            "sparse_gather_stabilized": self.sparse_gather_stabilized,
+            "max_selected_history_fraction": self.max_selected_history_fraction,
+            "sink_tokens": self.sink_tokens,
+            "recent_tokens": self.recent_tokens,
+            "num_query_heads_per_kv": self.num_query_heads_per_kv,
+            "incremental_page_metadata": self.incremental_page_metadata,
+            "backend": "sm_100a",
+        }
+
+    def close(self) -> None:
+        self._slab.close()
+
+
+class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
+    """Quest B0 + INT4 QK + top-p with the dynamic budget, GQA-group execution.
+
+    hi/twilight_offload_cache.py:133-3743.  budget_mode must be 'dynamic' (the
+    deployed profile); 'matched' raises ValueError.  qk_backend values of the
+    reference are accepted and all run the CUDA INT4 estimator.  Extra keyword:
+    ``int4_group_size`` (128 = the reference's per-token scale, or 32/64).
+    """
+
+    def __init__(self, *, candidate_token_budget: int = 8192, top_p: float = 0.95,
+                 matched_budget_fraction: float = 0.05, budget_mode: str = "dynamic",
+                 gqa_groupwise_execution: bool = False, qk_backend: str = "pytorch",
+                 int4_group_size: int = 128, **kwargs: Any) -> None:
+        if candidate_token_budget <= 0:
+            raise ValueError("candidate_token_budget must be positive")
+        if not 0.0 < top_p <= 1.0:
+            raise ValueError("top_p must be in (0, 1]")
+        if not 0.0 < matched_budget_fraction <= 1.0:
+            raise ValueError("matched_budget_fraction must be in (0, 1]")
+        if budget_mode not in {"matched", "dynamic"}:
+            raise ValueError("budget_mode must be 'matched' or 'dynamic'")
+        if budget_mode == "matched":
+            raise ValueError("budget_mode='matched' is not implemented by the sm_100a path; "
+                             "use budget_mode='dynamic'")
+        if qk_backend not in {"pytorch", "triton", "triton_prepare", "cuda"}:
+            raise ValueError("unknown Twilight QK backend")
+        layer_batched = bool(kwargs.get("layer_batched_selection", False))
+        if qk_backend != "pytorch" and not layer_batched:
+            raise ValueError("fused QK requires layer-batched selection")
+        if gqa_groupwise_execution and not layer_batched:
+            raise ValueError("GQA group-wise execution requires layer-batched selection")
+        if gqa_groupwise_execution and kwargs.get("layer_flat_ragged_execution", False):
+            raise ValueError("GQA group-wise and per-Query-head flat execution are exclusive")
+        if int4_group_size not in (32, 64, 128):
+            raise ValueError("int4_group_size must be 32, 64 or 128")
+        max_cache_len = int(kwargs["max_cache_len"])
+        sink = int(kwargs.get("sink_tokens", 64))
+        block = int(kwargs.get("block_size", 16))
+        max_pages = math.ceil(max(0, max_cache_len - sink) / block)
+        required = min(max_pages, math.ceil(candidate_token_budget / block))
+        kwargs["budget_fraction"] = matched_budget_fraction
+        kwargs["max_selected_history_fraction"] = required / max_pages if max_pages else 1.0
+        super().__init__(**kwargs)
+        self.candidate_token_budget = int(candidate_token_budget)
+        self.top_p = float(top_p)
+        self.matched_budget_fraction = float(matched_budget_fraction)
+        self.budget_mode = budget_mode
+        self.gqa_groupwise_execution = bool(gqa_groupwise_execution)
+        self.qk_backend = qk_backend
+        self.int4_group_size = int(int4_group_size)
+        E, L = self.geometry.num_entries, self.geometry.max_cache_len
+        ng = HEAD_DIM // self.int4_group_size
+        self._packed = torch.empty((E, L, HEAD_DIM // 2), dtype=torch.uint8, device=self.device)
+        self._scale = torch.empty((E, L, ng), dtype=self.dtype, device=self.device)
+        self._minimum = torch.empty_like(self._scale)
+        self.b0_page_capacity = max(1, min(self.page_capacity, math.ceil(candidate_token_budget / block)))
+        self._prepared: dict[int, dict[str, Any]] = {}
+        self._capture_budget_trace = False
+        self._budget_trace: list[dict[str, Any]] = []
+        self._group_union_trace: list[dict[str, Any]] = []
+        self._cached_group_positions: dict[int, torch.Tensor] = {}
+        self._cached_per_q_positions: dict[int, tuple[torch.Tensor, ...]] = {}
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs: Optional[dict[str, Any]] = None):
+        """Prefill as the reference (metadata + INT4 codes + slab copy).  Decode runs
+        through update_layer_gqa_group_ragged / attend_layer (the GQA group path)."""
+        if int(key_states.shape[-2]) == 1:
+            raise NotImplementedError(
+                "Twilight decode runs per layer: use update_layer_gqa_group_ragged or attend_layer")
+        return super().update(key_states, value_states, layer_idx, cache_kwargs)
+
+    # --------------------------------------------------------------- metadata --
+    def _build_metadata(self, entry: int, key_states: torch.Tensor) -> None:
+        """Quest metadata + INT4 codes of the prompt (hi/twilight_offload_cache.py:925-936)."""
+        super()._build_metadata(entry, key_states)
+        keys = key_states[0, 0].contiguous()
+        S = int(keys.shape[0])
+        _lib.check(_lib.load().tw_int4_pack(
+            keys.data_ptr(), S * HEAD_DIM, 1, S, HEAD_DIM, self.int4_group_size,
+            ops._kv_code(self.dtype), self._packed[entry].data_ptr(), self._scale[entry].data_ptr(),
+            self._minimum[entry].data_ptr(), self.geometry.max_cache_len, 0, self._stream()),
+            "int4_pack")
+
+    # ---------------------------------------------------------------- buffers --
+    def _buffers(self, first: int, groups: int) -> dict[str, Any]:
+        bufs = self._layer_bufs.get(groups)
+        if bufs is not None:
+            return bufs
+        R = self.num_query_heads_per_kv
+        L = self.geometry.max_cache_len
+        dev = self.device
+        n_cap = self.b0_page_capacity * self.block_size
+        per_group = min(L, self.sink_tokens + self.recent_tokens + R * n_cap) + 1
+        rows_cap = groups * per_group
+        ws = ops.select_layer_workspace_bytes(groups, R, self.page_capacity, self.b0_page_capacity,
+                                              self.block_size)
+        attn_ws = ops.decode_attention_workspace_bytes(groups, R, per_group)
+        bufs = {
+            "pages": torch.empty((groups, R, self.b0_page_capacity), dtype=torch.int32, device=dev),
+            "union_pos": torch.empty((groups, L), dtype=torch.int32, device=dev),
+            # union_count [G] | error flag slot is separate
+            "union_count": torch.zeros(groups, dtype=torch.int32, device=dev),
+            "head_count": torch.zeros((groups, R), dtype=torch.int32, device=dev),
+            "head_pos": torch.empty((groups, R, n_cap), dtype=torch.int32, device=dev),
+            "workspace": torch.empty(max(ws, 256), dtype=torch.uint8, device=dev),
+            "attn_workspace": torch.zeros(max(attn_ws, 256), dtype=torch.uint8, device=dev),
+            "flat": torch.empty((2, 2, rows_cap, HEAD_DIM), dtype=self.dtype, device=dev),
+            "cu": torch.zeros((2, groups + 1), dtype=torch.int32, device=dev),
+            "rows_cap": rows_cap,
+            "per_group_cap": per_group,
+            "slot": 0,
+        }
+        self._layer_bufs[groups] = bufs
+        return bufs
+
+    # -------------------------------------------------------------- selection --
+    def prepare_layer_selection(self, *, entries: list[int], queries: list[torch.Tensor]) -> None:
+        """Both Twilight selection stages for one layer on the device
+        (hi/twilight_offload_cache.py:996-1843, gpu_compact_gqa_union semantics)."""
+        if not self.layer_batched_selection:
+            return
+        self._validate_layer(entries, queries)
+        old_length = self._layer_old_length(entries)
+        if self._prompt_length is None:
+            raise RuntimeError("Twilight prompt metadata is missing")
+        q = torch.stack([query[0, :, 0] for query in queries], dim=0).float().contiguous()
+        self._select(entries, q, old_length)
+
+    def _select(self, entries: list[int], q: torch.Tensor, old_length: int) -> None:
+        first = entries[0]
+        G = len(entries)
+        R = self.num_query_heads_per_kv
+        bufs = self._buffers(first, G)
+        w = self._window(old_length)
+        candidate_pages = min(w["candidate_pages"], self._metadata_pages(entries, old_length))
+        b0_pages = min(candidate_pages, max(1, math.ceil(self.candidate_token_budget / self.block_size)),
+                       self.b0_page_capacity)
+        start = self._phase_start()
+        if candidate_pages == 0 or b0_pages == 0:
+            protected = torch.cat((torch.arange(w["sink_end"], device=self.device, dtype=torch.int32),
+                                   torch.arange(w["recent_start"], old_length, device=self.device,
+                                                dtype=torch.int32)))
+            bufs["union_pos"][:, : protected.numel()] = protected
+            bufs["union_count"].fill_(protected.numel())
+            bufs["head_count"].zero_()
+        else:
+            lib = _lib.load()
+            _lib.check(lib.tw_select_layer(
+                q.data_ptr(), self._page_min[first].data_ptr(), self._page_max[first].data_ptr(),
+                self.page_capacity * HEAD_DIM, candidate_pages, self._packed[first].data_ptr(),
+                self._scale[first].data_ptr(), self._minimum[first].data_ptr(),
+                self.geometry.max_cache_len, G, R, b0_pages, self.block_size, self.sink_tokens,
+                HEAD_DIM, self.int4_group_size, ops._kv_code(self.dtype), self.top_p, old_length,
+                w["sink_end"], w["recent_start"], bufs["pages"].data_ptr(),
+                bufs["union_pos"].data_ptr(), self.geometry.max_cache_len,
+                bufs["union_count"].data_ptr(), bufs["head_count"].data_ptr(),
+                bufs["head_pos"].data_ptr() if self._tracing() else None,
+                self._error_flag.data_ptr(), bufs["workspace"].data_ptr(),
+                bufs["workspace"].numel(), self._stream()), "select_layer")
+        self._phase_end("twilight_selection_core", start)
+        self._prepared[first] = dict(old_length=old_length, window=w, b0_pages=b0_pages,
+                                     candidate_pages=candidate_pages, entries=list(entries))
+        if self._tracing():
+            self._record_traces(entries, old_length, w, b0_pages, bufs)
+
+    def _tracing(self) -> bool:
+        return self._capture_selection_trace or self._capture_budget_trace
+
+    def _record_traces(self, entries, old_length, w, b0_pages, bufs) -> None:
+        R = self.num_query_heads_per_kv
+        counts = bufs["head_count"].cpu()
+        head_pos = bufs["head_pos"].cpu()
+        decode_step = old_length - (self._prompt_length or 0) + 1
+        protected = w["sink_end"] + (old_length - w["recent_start"])
+        for g, entry in enumerate(entries):
+            rows = []
+            for r in range(R):
+                c = int(counts[g, r]) if b0_pages else 0
+                sel = head_pos[g, r, :c].to(torch.int64) if b0_pages else torch.empty(0, dtype=torch.int64)
+                rows.append(sel)
+                if self._capture_budget_trace:
+                    self._budget_trace.append({
+                        "decode_step": decode_step, "entry": entry, "kv_head": g,
+                        "query_head_in_group": r, "budget_mode": self.budget_mode,
+                        "b0_tokens": b0_pages * self.block_size, "raw_b1_tokens": c,
+                        "selected_adaptive_tokens": c, "protected_tokens": protected,
+                        "selected_history_tokens": protected + c,
+                        "eligible_history_tokens": w["eligible"], "full_history_tokens": old_length})
+            self._cached_per_q_positions[entry] = tuple(rows)
+            if self._capture_selection_trace:
+                for r, sel in enumerate(rows):
+                    self._selection_trace.append({
+                        "decode_step": decode_step, "entry": entry, "query_head_in_group": r,
+                        "selected_positions": tuple(int(v) for v in sel.tolist())})
+
+    def enable_budget_trace(self, enabled: bool = True) -> None:
+        self._capture_budget_trace = bool(enabled)
+        self._budget_trace = []
+
+    def budget_trace(self) -> list[dict[str, Any]]:
+        return list(self._budget_trace)
+
+    def group_union_trace(self) -> list[dict[str, Any]]:
+        return list(self._group_union_trace)
+
+    # --------------------------------------------------------- GQA group path --
+    def _begin_group_step(self, key_states, value_states, queries, entries):
+        if not self.gqa_groupwise_execution:
+            raise RuntimeError("Twilight GQA group-wise execution is disabled")
+        if not (len(entries) == len(key_states) == len(value_states) == len(queries) and entries):
+            raise ValueError("layer entries, K/V, and Queries must be aligned")
+        if len(set(entries)) != len(entries):
+            raise ValueError("layer entries must be unique")
+        _contiguous_entries(entries)
+        for k, v in zip(key_states, value_states):
+            if k.shape != v.shape or tuple(k.shape) != (1, 1, 1, HEAD_DIM):
+                raise ValueError("GQA group decode expects [1, 1, 1, dim] K/V")
+        old_length = self._advance_layer(entries)
+        prepared = self._prepared.pop(entries[0], None)
+        if prepared is None or prepared["old_length"] != old_length:
+            raise AssertionError("prepared GPU GQA union is missing")
+        k_new = torch.cat([k[0, 0] for k in key_states], dim=0)
+        v_new = torch.cat([v[0, 0] for v in value_states], dim=0)
+        return old_length, k_new, v_new
+
+    def _gather_union(self, first: int, G: int, old_length: int, k_new, v_new):
+        bufs = self._buffers(first, G)
+        slot = bufs["slot"]
+        bufs["slot"] = 1 - slot
+        out_k = bufs["flat"][slot, 0]
+        out_v = bufs["flat"][slot, 1]
+        cu = bufs["cu"][slot]
+        start = self._phase_start()
+        _lib.check(_lib.load().tw_gather_union(
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            first, G, old_length, bufs["union_pos"].data_ptr(), self.geometry.max_cache_len,
+            bufs["union_count"].data_ptr(), k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM,
+            ops._kv_code(self.dtype), out_k.data_ptr(), out_v.data_ptr(), bufs["rows_cap"],
+            cu.data_ptr(), self._error_flag.data_ptr(), self._stream()), "gather_union")
+        self._phase_end("h2d", start)
+        return bufs, out_k, out_v, cu
+
+    def update_layer_gqa_group_ragged(self, *, key_states: list[torch.Tensor],
+                                      value_states: list[torch.Tensor],
+                                      queries: list[torch.Tensor], entries: list[int]):
+        """hi/twilight_offload_cache.py:2610-3602.  Returns (K [sum_T,1,D], V, cu_seqlens_k
+        int32 [G+1] (device), max_seqlen_k, group_total_lengths); group g's rows are its
+        sorted union followed by its current token.  K/V are views into cache-owned
+        double-buffered storage, valid until the next layer reuses the slot."""
+        old_length, k_new, v_new = self._begin_group_step(key_states, value_states, queries, entries)
+        first, G = entries[0], len(entries)
+        bufs, out_k, out_v, cu = self._gather_union(first, G, old_length, k_new, v_new)
+        self._append_rows(first, G, old_length, k_new, v_new)
+        host = torch.cat((bufs["union_count"], self._error_flag)).cpu()
+        flag = int(host[-1])
+        if flag:
+            self._error_flag.zero_()
+            _lib.check(flag, "device-side check")
+        counts = [int(c) for c in host[:-1].tolist()]
+        lengths = tuple(c + 1 for c in counts)
+        total = sum(lengths)
+        for g, entry in enumerate(entries):
+            self._last_query_head_lengths[entry] = tuple([lengths[g]] * self.num_query_heads_per_kv)
+        self._record_group_step(entries, old_length, counts)
+        return (out_k[:total].view(total, 1, HEAD_DIM), out_v[:total].view(total, 1, HEAD_DIM), cu,
+                max(lengths), lengths)
+
+    def _record_group_step(self, entries, old_length, counts) -> None:
+        decode_step = old_length - (self._prompt_length or 0) + 1
+        if self._capture_selection_trace:
+            bufs = self._layer_bufs[len(entries)]
+            for g, entry in enumerate(entries):
+                union = bufs["union_pos"][g, : counts[g]].to(torch.int64).cpu()
+                self._cached_group_positions[entry] = union
+                self._group_union_trace.append({
+                    "decode_step": decode_step, "entry": entry, "kv_head": g,
+                    "group_union_history_tokens": counts[g],
+                    "positions_sha256": hashlib.sha256(union.numpy().tobytes()).hexdigest()})
+        if self.metrics_enabled:
+            self.metrics["h2d_bytes"] += 2 * sum(counts) * HEAD_DIM * torch.tensor([], dtype=self.dtype).element_size()
+            self.metrics["h2d_copy_calls"] += 1
+            self.metrics["group_union_history_tokens_total"] += sum(counts)
+            self.metrics["cache_update_calls"] += len(entries)
+
+    def attend_layer(self, *, key_states, value_states, queries, entries,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Fused extension of the GQA group step: gather + sparse GQA decode attention
+        + append, with no host synchronisation.  Returns the attention output
+        [G, R, D] in the K/V dtype (what hi/mp.py:258-279 feeds to o_proj)."""
+        old_length, k_new, v_new = self._begin_group_step(key_states, value_states, queries, entries)
+        first, G = entries[0], len(entries)
+        bufs, out_k, out_v, cu = self._gather_union(first, G, old_length, k_new, v_new)
+        q = torch.stack([query[0, :, 0] for query in queries], dim=0).to(self.dtype).contiguous()
+        start = self._phase_start()
+        out = ops.decode_attention(q, out_k, out_v, cu, min(bufs["per_group_cap"], old_length + 1),
+                                   workspace=bufs["attn_workspace"], out=out)
+        self._phase_end("attention", start)
+        self._append_rows(first, G, old_length, k_new, v_new)
+        return out
+
+    # ------------------------------------------------------------- hashes ----
+    def selected_positions_sha256(self) -> str:
+        digest = hashlib.sha256()
+        for entry in sorted(self._cached_per_q_positions):
+            positions = self._cached_per_q_positions[entry]
+            digest.update(entry.to_bytes(4, byteorder="little", signed=False))
+            digest.update(len(positions).to_bytes(4, byteorder="little", signed=False))
+            for selected in positions:
+                arr = selected.to(torch.int64).contiguous()
+                digest.update(arr.numel().to_bytes(8, byteorder="little", signed=False))
+                digest.update(arr.numpy().tobytes())
+        return digest.hexdigest()
+
+    def group_positions_sha256(self) -> Optional[str]:
+        digest = hashlib.sha256()
+        for entry in sorted(self._cached_group_positions):
+            arr = self._cached_group_positions[entry].to(torch.int64).contiguous()
+            digest.update(entry.to_bytes(4, byteorder="little", signed=False))
+            digest.update(arr.numel().to_bytes(8, byteorder="little", signed=False))
+            digest.update(arr.numpy().tobytes())
+        return digest.hexdigest()
+
+    def state_snapshot(self) -> dict[str, Any]:
+        snap = super().state_snapshot()
+        quant = sum(t.numel() * t.element_size() for t in (self._packed, self._scale, self._minimum))
+        snap.update({
+            "policy": "twilight_inspired_int4_top_p_dynamic",
+            "candidate_token_budget": self.candidate_token_budget,
+            "top_p": self.top_p,
+            "matched_budget_fraction": self.matched_budget_fraction,
+            "budget_mode": self.budget_mode,
+            "quantized_key_metadata_gpu_bytes": quant,
+            "int4_group_size": self.int4_group_size,
+            "qk_backend": self.qk_backend,
+            "twilight_gqa_groupwise_execution": self.gqa_groupwise_execution,
+            "twilight_gqa_group_semantics": "exact union of the original per-Query-head selected token sets",
+            "selection_boundary": "device-resident union; host reads only the union lengths",
+        })
+        return snap

@@ -1,0 +1,273 @@
+// Zero-copy row gathers: the GPU reads the selected K/V rows straight from the
+// pinned, device-mapped host slab (or from device memory) with 16-byte loads
+// and writes them into the flat attention layout.
+//
+// Reference: gather_kv (hi/cpu_kv_gather.cpp:3-16), assemble_zero_copy miss
+// branch (hi/resident_zero_copy.cu:7-42), the flat CPU gather + chunked H2D +
+// direct attention layout of update_layer_gqa_group_ragged
+// (hi/twilight_offload_cache.py:2973-3101, :3307-3310), and the per-query-head
+// packing of QuestTopKOffloadedCache (hi/quest_offload_cache.py:403-511, :724-987).
+#include "tw_common.cuh"
+
+namespace tw {
+
+// Each thread moves one 16-byte vector of a row; kUnroll rows are loaded
+// before any is stored so that many host-link reads are in flight.
+constexpr int kGatherThreads = 256;
+constexpr int kGatherUnroll = 4;
+
+__global__ void __launch_bounds__(kGatherThreads)
+gather_kv_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v, uint4* __restrict__ ok,
+                 uint4* __restrict__ ov, const int64_t* __restrict__ rows, int64_t n,
+                 int64_t source_rows, int vec_per_row, int32_t* error_flag) {
+  const int rows_per_cta = kGatherThreads / vec_per_row;
+  const int sub_row = threadIdx.x / vec_per_row;
+  const int col = threadIdx.x % vec_per_row;
+  if (sub_row >= rows_per_cta) return;
+  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+  for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + sub_row; base < n;
+       base += stride * kGatherUnroll) {
+    uint4 kv[kGatherUnroll], vv[kGatherUnroll];
+    int64_t idx[kGatherUnroll];
+    bool ok_row[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      idx[u] = base + u * stride;
+      ok_row[u] = false;
+      if (idx[u] < n) {
+        const int64_t r = rows[idx[u]];
+        if (r >= 0 && r < source_rows) {
+          ok_row[u] = true;
+          kv[u] = __ldcs(k + r * vec_per_row + col);
+          vv[u] = __ldcs(v + r * vec_per_row + col);
+        } else if (error_flag) {
+          atomicExch(error_flag, TW_ERR_INVALID_INDEX);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      if (ok_row[u]) {
+        ok[idx[u] * vec_per_row + col] = kv[u];
+        ov[idx[u] * vec_per_row + col] = vv[u];
+      }
+    }
+  }
+}
+
+// Group offsets in the flat layout: off[g] = sum_{g' < g} (count[g'] + 1).
+constexpr int kMaxGroups = 64;
+
+// Rows of the union layout: group g occupies [off[g], off[g] + count[g] + 1);
+// its last row is the current token.
+template <int kVec>
+__global__ void __launch_bounds__(kGatherThreads)
+gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
+                    int64_t max_len, int first_entry, int groups, int64_t old_length,
+                    const int32_t* __restrict__ union_pos, int64_t pos_stride,
+                    const int32_t* __restrict__ union_count, const uint4* __restrict__ cur_k,
+                    const uint4* __restrict__ cur_v, uint4* __restrict__ out_k,
+                    uint4* __restrict__ out_v, int64_t rows_cap, int32_t* __restrict__ cu_seqlens,
+                    int32_t* error_flag) {
+  __shared__ int64_t off[kMaxGroups + 1];
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    for (int g = 0; g < groups; ++g) {
+      off[g] = acc;
+      acc += (int64_t)union_count[g] + 1;
+    }
+    off[groups] = acc;
+    if (blockIdx.x == 0) {
+      for (int g = 0; g <= groups; ++g) cu_seqlens[g] = (int32_t)off[g];
+      if (acc > rows_cap && error_flag) atomicExch(error_flag, TW_ERR_CAPACITY);
+    }
+  }
+  __syncthreads();
+  const int64_t total = min(off[groups], rows_cap);
+  constexpr int rows_per_cta = kGatherThreads / kVec;
+  const int sub_row = threadIdx.x / kVec;
+  const int col = threadIdx.x % kVec;
+  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+  for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + sub_row; base < total;
+       base += stride * kGatherUnroll) {
+    uint4 kv[kGatherUnroll], vv[kGatherUnroll];
+    int64_t t[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      t[u] = base + u * stride;
+      if (t[u] >= total) continue;
+      int g = 0;
+      while (g + 1 < groups && off[g + 1] <= t[u]) ++g;
+      const int64_t i = t[u] - off[g];
+      const int32_t cnt = union_count[g];
+      if (i < cnt) {
+        const int64_t pos = union_pos[(int64_t)g * pos_stride + i];
+        if (pos < 0 || pos >= old_length) {
+          if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
+          kv[u] = make_uint4(0, 0, 0, 0);
+          vv[u] = kv[u];
+        } else {
+          const int64_t src = ((int64_t)(first_entry + g) * max_len + pos) * kVec + col;
+          kv[u] = __ldcs(slab_k + src);
+          vv[u] = __ldcs(slab_v + src);
+        }
+      } else {
+        kv[u] = cur_k[(int64_t)g * kVec + col];
+        vv[u] = cur_v[(int64_t)g * kVec + col];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      if (t[u] >= total) continue;
+      out_k[t[u] * kVec + col] = kv[u];
+      out_v[t[u] * kVec + col] = vv[u];
+    }
+  }
+}
+
+// Quest per-query-head layout: segment s = g*R + r has seg_len rows:
+// [0, sink_end) then the k pages' rows then [recent_start, old_length) then the
+// current token of group g.
+template <int kVec>
+__global__ void __launch_bounds__(kGatherThreads)
+gather_quest_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
+                    int64_t max_len, int first_entry, int R, int64_t old_length, int64_t sink_end,
+                    int64_t recent_start, int sink, int block, const int32_t* __restrict__ pages,
+                    int k_pages, const uint4* __restrict__ cur_k, const uint4* __restrict__ cur_v,
+                    uint4* __restrict__ out_k, uint4* __restrict__ out_v, int64_t seg_len,
+                    int64_t total, int32_t* error_flag) {
+  constexpr int rows_per_cta = kGatherThreads / kVec;
+  const int sub_row = threadIdx.x / kVec;
+  const int col = threadIdx.x % kVec;
+  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+  const int64_t sel = (int64_t)k_pages * block;
+  for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + sub_row; base < total;
+       base += stride * kGatherUnroll) {
+    uint4 kv[kGatherUnroll], vv[kGatherUnroll];
+    int64_t t[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      t[u] = base + u * stride;
+      if (t[u] >= total) continue;
+      const int64_t s = t[u] / seg_len;
+      const int64_t i = t[u] - s * seg_len;
+      const int g = (int)(s / R);
+      int64_t pos;
+      if (i < sink_end) {
+        pos = i;
+      } else if (i < sink_end + sel) {
+        const int64_t j = i - sink_end;
+        pos = (int64_t)sink + (int64_t)pages[s * k_pages + j / block] * block + (j % block);
+      } else if (i < seg_len - 1) {
+        pos = recent_start + (i - sink_end - sel);
+      } else {
+        pos = -1;  // current token
+      }
+      if (pos < 0) {
+        kv[u] = cur_k[(int64_t)g * kVec + col];
+        vv[u] = cur_v[(int64_t)g * kVec + col];
+      } else if (pos >= old_length) {
+        if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
+        kv[u] = make_uint4(0, 0, 0, 0);
+        vv[u] = kv[u];
+      } else {
+        const int64_t src = ((int64_t)(first_entry + g) * max_len + pos) * kVec + col;
+        kv[u] = __ldcs(slab_k + src);
+        vv[u] = __ldcs(slab_v + src);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      if (t[u] >= total) continue;
+      out_k[t[u] * kVec + col] = kv[u];
+      out_v[t[u] * kVec + col] = vv[u];
+    }
+  }
+}
+
+int gather_grid(int64_t rows, int rows_per_cta) {
+  int device = 0, sms = 148;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const int64_t want = (rows + (int64_t)rows_per_cta * kGatherUnroll - 1) /
+                       ((int64_t)rows_per_cta * kGatherUnroll);
+  const int64_t cap = (int64_t)sms * 8;
+  const int64_t g = want < cap ? want : cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace tw
+
+using namespace tw;
+
+extern "C" int tw_gather_kv(const void* k, const void* v, void* out_k, void* out_v,
+                            const int64_t* rows, int64_t n, int64_t source_rows,
+                            int64_t row_bytes, int32_t* error_flag, void* stream) {
+  if (n < 0 || source_rows < 0 || row_bytes <= 0 || (row_bytes % 16) != 0 ||
+      row_bytes / 16 > kGatherThreads)
+    return TW_ERR_BAD_ARG;
+  if (n == 0) return TW_OK;
+  if (!k || !v || !out_k || !out_v || !rows) return TW_ERR_BAD_ARG;
+  if (!aligned16(k) || !aligned16(v) || !aligned16(out_k) || !aligned16(out_v))
+    return TW_ERR_BAD_ARG;
+  const int vec = (int)(row_bytes / 16);
+  const int grid = gather_grid(n, kGatherThreads / vec);
+  gather_kv_kernel<<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
+      (const uint4*)k, (const uint4*)v, (uint4*)out_k, (uint4*)out_v, rows, n, source_rows, vec,
+      error_flag);
+  return check_launch();
+}
+
+extern "C" int tw_gather_union(const void* slab_k, const void* slab_v, int64_t max_len,
+                               int first_entry, int groups, int64_t old_length,
+                               const int32_t* union_pos, int64_t pos_stride,
+                               const int32_t* union_count, const void* cur_k, const void* cur_v,
+                               int head_dim, int dtype, void* out_k, void* out_v,
+                               int64_t rows_cap, int32_t* cu_seqlens, int32_t* error_flag,
+                               void* stream) {
+  if (head_dim != kHeadDim || (dtype != TW_F16 && dtype != TW_BF16)) return TW_ERR_UNSUPPORTED;
+  if (!slab_k || !slab_v || !union_pos || !union_count || !cur_k || !cur_v || !out_k || !out_v ||
+      !cu_seqlens || groups <= 0 || groups > kMaxGroups || first_entry < 0 || old_length < 0 ||
+      old_length > max_len || rows_cap <= 0)
+    return TW_ERR_BAD_ARG;
+  if (!aligned16(slab_k) || !aligned16(slab_v) || !aligned16(cur_k) || !aligned16(cur_v) ||
+      !aligned16(out_k) || !aligned16(out_v))
+    return TW_ERR_BAD_ARG;
+  constexpr int kVec = kHeadDim * 2 / 16;  // 16 vectors per 256-byte row
+  const int grid = gather_grid(rows_cap, kGatherThreads / kVec);
+  gather_union_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
+      (const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, groups, old_length,
+      union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
+      (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens, error_flag);
+  return check_launch();
+}
+
+extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int64_t max_len,
+                                     int first_entry, int groups, int heads_per_group,
+                                     int64_t old_length, int64_t sink_end, int64_t recent_start,
+                                     int sink, int block_size, const int32_t* pages, int k_pages,
+                                     const void* cur_k, const void* cur_v, int head_dim,
+                                     int dtype, void* out_k, void* out_v, int32_t* error_flag,
+                                     void* stream) {
+  if (head_dim != kHeadDim || (dtype != TW_F16 && dtype != TW_BF16)) return TW_ERR_UNSUPPORTED;
+  if (!slab_k || !slab_v || !cur_k || !cur_v || !out_k || !out_v || groups <= 0 ||
+      heads_per_group <= 0 || first_entry < 0 || old_length < 0 || old_length > max_len ||
+      sink_end < 0 || sink_end > old_length || recent_start < sink_end ||
+      recent_start > old_length || k_pages < 0 || (k_pages > 0 && !pages) || block_size <= 0)
+    return TW_ERR_BAD_ARG;
+  if (!aligned16(slab_k) || !aligned16(slab_v) || !aligned16(cur_k) || !aligned16(cur_v) ||
+      !aligned16(out_k) || !aligned16(out_v))
+    return TW_ERR_BAD_ARG;
+  const int64_t seg_len =
+      sink_end + (int64_t)k_pages * block_size + (old_length - recent_start) + 1;
+  const int64_t total = seg_len * groups * heads_per_group;
+  constexpr int kVec = kHeadDim * 2 / 16;
+  const int grid = gather_grid(total, kGatherThreads / kVec);
+  gather_quest_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
+      (const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, heads_per_group,
+      old_length, sink_end, recent_start, sink, block_size, pages, k_pages, (const uint4*)cur_k,
+      (const uint4*)cur_v, (uint4*)out_k, (uint4*)out_v, seg_len, total, error_flag);
+  return check_launch();
+}

@@ -1,0 +1,305 @@
+// Twilight INT4 stage: group-wise affine INT4 quantiser and the INT4 QK estimate.
+//
+// Reference: affine_int4_pack / affine_int4_dequantize
+// (hi/twilight_offload_cache.py:25-47), fused_affine_int4_qk
+// (hi/twilight_fused_qk.py:13-55), logits /= sqrt(D) (hi/twilight_offload_cache.py:1261).
+#include "tw_common.cuh"
+
+namespace tw {
+
+// Rounding of the `/ 15.0` in affine_int4_pack.  torch on CUDA multiplies by
+// the fp32 reciprocal of a CPU-scalar divisor; torch on CPU divides.
+enum ScaleDiv : int { kScaleReciprocal = 0, kScaleDivide = 1 };
+
+// Quantise the 4 channels 4*lane .. 4*lane+3 of one row held by a warp.
+// group_size in {32, 64, 128}: lanes 0..31 split into groups of group_size/4.
+// Returns the two packed bytes for this lane (low byte = channels 0,1).
+template <typename T>
+__device__ __forceinline__ uint16_t quantize_lane(const T (&raw)[4], int group_size, int scale_div,
+                                                  T* scale_out, T* min_out) {
+  const int lanes_per_group = group_size >> 2;
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = to_f32(raw[i]);
+  float mn = fminf(fminf(x[0], x[1]), fminf(x[2], x[3]));
+  float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+  for (int off = 1; off < lanes_per_group; off <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  }
+  // (maximum - minimum) is computed in the K dtype, then widened.
+  const float diff = to_f32(from_f32<T>(__fsub_rn(mx, mn)));
+  const float clamped = fmaxf(diff, 1e-9f);
+  const float sc32 = scale_div == kScaleDivide ? __fdiv_rn(clamped, 15.0f)
+                                               : __fmul_rn(clamped, __fdiv_rn(1.0f, 15.0f));
+  const T sc_t = from_f32<T>(sc32);
+  const float sc = to_f32(sc_t);
+  const T mn_t = from_f32<T>(mn);  // exact: mn is a K-dtype value
+  uint32_t codes[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float c = rintf(__fdiv_rn(__fsub_rn(x[i], mn), sc));
+    if (!(c >= 0.0f)) c = 0.0f;  // negatives and NaN (0/0) -> 0, as clamp + uint8 cast
+    if (c > 15.0f) c = 15.0f;
+    codes[i] = (uint32_t)c;
+  }
+  if ((threadIdx.x & (lanes_per_group - 1)) == 0) {
+    *scale_out = sc_t;
+    *min_out = mn_t;
+  }
+  return (uint16_t)((codes[0] | (codes[1] << 4)) | ((codes[2] | (codes[3] << 4)) << 8));
+}
+
+// Warp per row.  keys rows: entry e, row t at keys + (e*key_entry_stride + t)*D.
+template <typename T>
+__global__ void int4_pack_kernel(const T* __restrict__ keys, int64_t key_entry_stride,
+                                 int64_t n_tokens, int group_size, int scale_div,
+                                 uint8_t* __restrict__ packed, T* __restrict__ scale,
+                                 T* __restrict__ minimum, int64_t out_entry_stride,
+                                 int64_t out_row_offset) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int64_t t = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int e = blockIdx.y;
+  if (t >= n_tokens) return;
+  const T* row = keys + (e * key_entry_stride + t) * kHeadDim;
+  T raw[4];
+  const uint2 v = *reinterpret_cast<const uint2*>(row + 4 * lane);
+  memcpy(raw, &v, sizeof(v));
+  const int ngroups = kHeadDim / group_size;
+  const int64_t orow = e * out_entry_stride + out_row_offset + t;
+  const int grp = (4 * lane) / group_size;
+  const uint16_t bytes = quantize_lane<T>(raw, group_size, scale_div, scale + orow * ngroups + grp,
+                                          minimum + orow * ngroups + grp);
+  reinterpret_cast<uint16_t*>(packed + orow * (kHeadDim / 2))[lane] = bytes;
+}
+
+// INT4 QK estimate.  4 lanes per candidate token, lane j covers channels
+// 32j .. 32j+31 (16 code bytes, one uint4 load).  Per channel k = code*s + m
+// (separately rounded), acc += k*q in channel order, then (a0+a1)+(a2+a3).
+template <typename T>
+__global__ void __launch_bounds__(256)
+int4_qk_kernel(const float* __restrict__ q, const uint8_t* __restrict__ packed,
+               const T* __restrict__ scale, const T* __restrict__ minimum,
+               int64_t entry_stride, const int32_t* __restrict__ pages, int R, int b0,
+               int block, int sink, int group_size, float inv_sqrt_d,
+               float* __restrict__ logits, int tokens_per_cta) {
+  const int row = blockIdx.y;  // g*R + r
+  const int g = row / R;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  const int sub = lane & 3;
+  const int tok = lane >> 2;
+  const int n_cand = b0 * block;
+  float qr[32];
+  const float* qrow = q + (int64_t)row * kHeadDim + 32 * sub;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(qrow + i);
+    qr[i] = v.x; qr[i + 1] = v.y; qr[i + 2] = v.z; qr[i + 3] = v.w;
+  }
+  const int ngroups = kHeadDim / group_size;
+  const int grp = (32 * sub) / group_size;
+  const int32_t* prow = pages + (int64_t)row * b0;
+  const int64_t ebase = (int64_t)g * entry_stride;
+  const int cta_begin = blockIdx.x * tokens_per_cta;
+  const int cta_end = min(n_cand, cta_begin + tokens_per_cta);
+  for (int base = cta_begin + warp * 8; base < cta_end; base += warps * 8) {
+    const int n = base + tok;
+    const bool valid = n < cta_end;
+    float acc = 0.0f;
+    if (valid) {
+      const int page = prow[n / block];
+      const int64_t pos = (int64_t)sink + (int64_t)page * block + (n % block);
+      const int64_t tr = ebase + pos;
+      const uint4 c = __ldg(reinterpret_cast<const uint4*>(packed + tr * (kHeadDim / 2)) + sub);
+      const float s = to_f32(scale[tr * ngroups + grp]);
+      const float m = to_f32(minimum[tr * ngroups + grp]);
+      const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t byte = (words[w] >> (8 * b)) & 0xffu;
+          const int i = 8 * w + 2 * b;
+          const float k0 = __fadd_rn(__fmul_rn((float)(byte & 15u), s), m);
+          acc = __fadd_rn(acc, __fmul_rn(k0, qr[i]));
+          const float k1 = __fadd_rn(__fmul_rn((float)(byte >> 4), s), m);
+          acc = __fadd_rn(acc, __fmul_rn(k1, qr[i + 1]));
+        }
+      }
+    }
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    if (valid && sub == 0) logits[(int64_t)row * n_cand + n] = __fmul_rn(acc, inv_sqrt_d);
+  }
+}
+
+// New-token append: one CTA (128 threads) per group.  Copies the row to the
+// slab (mapped host or device memory), folds it into the running page min/max
+// and INT4-packs it.
+template <typename T>
+__global__ void append_token_kernel(uint4* __restrict__ slab_k, uint4* __restrict__ slab_v,
+                                    int64_t max_len, int first_entry, int64_t position,
+                                    const T* __restrict__ cur_k, const T* __restrict__ cur_v,
+                                    int sink, int block, T* __restrict__ pmin, T* __restrict__ pmax,
+                                    int64_t meta_entry_stride, uint8_t* __restrict__ packed,
+                                    T* __restrict__ scale, T* __restrict__ minimum, int group_size,
+                                    int scale_div) {
+  const int g = blockIdx.x;
+  const int entry = first_entry + g;
+  const int d = threadIdx.x;
+  const T* krow = cur_k + (int64_t)g * kHeadDim;
+  const T* vrow = cur_v + (int64_t)g * kHeadDim;
+  const int64_t slab_row = (int64_t)entry * max_len + position;
+  constexpr int kVecPerRow = kHeadDim * sizeof(T) / 16;
+  if (slab_k != nullptr) {
+    if (d < kVecPerRow) {
+      slab_k[slab_row * kVecPerRow + d] = reinterpret_cast<const uint4*>(krow)[d];
+    } else if (d < 2 * kVecPerRow) {
+      const int j = d - kVecPerRow;
+      slab_v[slab_row * kVecPerRow + j] = reinterpret_cast<const uint4*>(vrow)[j];
+    }
+  }
+  if (pmin != nullptr && position >= sink) {
+    const int64_t rel = position - sink;
+    const int64_t page = rel / block;
+    const int64_t off = rel % block;
+    const int64_t idx = (int64_t)entry * meta_entry_stride + page * kHeadDim + d;
+    const T x = krow[d];
+    if (off == 0) {
+      pmin[idx] = x;
+      pmax[idx] = x;
+    } else {
+      const float fx = to_f32(x);
+      if (fx < to_f32(pmin[idx])) pmin[idx] = x;
+      if (fx > to_f32(pmax[idx])) pmax[idx] = x;
+    }
+  }
+  if (packed != nullptr && threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    T raw[4];
+    const uint2 v = *reinterpret_cast<const uint2*>(krow + 4 * lane);
+    memcpy(raw, &v, sizeof(v));
+    const int ngroups = kHeadDim / group_size;
+    const int64_t orow = (int64_t)entry * max_len + position;
+    const int grp = (4 * lane) / group_size;
+    const uint16_t bytes = quantize_lane<T>(raw, group_size, scale_div,
+                                            scale + orow * ngroups + grp,
+                                            minimum + orow * ngroups + grp);
+    reinterpret_cast<uint16_t*>(packed + orow * (kHeadDim / 2))[lane] = bytes;
+  }
+}
+
+bool valid_group_size(int gs) { return gs == 32 || gs == 64 || gs == 128; }
+
+}  // namespace tw
+
+using namespace tw;
+
+int tw_int4_pack_mode(const void* keys, int64_t key_entry_stride, int n_entries, int64_t n_tokens,
+                      int head_dim, int group_size, int dtype, uint8_t* packed, void* scale,
+                      void* minimum, int64_t out_entry_stride, int64_t out_row_offset,
+                      int scale_div, void* stream) {
+  if (head_dim != kHeadDim || !valid_group_size(group_size)) return TW_ERR_UNSUPPORTED;
+  if (!keys || !packed || !scale || !minimum || n_entries < 0 || n_tokens < 0 ||
+      n_entries > 65535 || (scale_div != kScaleReciprocal && scale_div != kScaleDivide))
+    return TW_ERR_BAD_ARG;
+  if (n_entries == 0 || n_tokens == 0) return TW_OK;
+  constexpr int kThreads = 256;
+  const int64_t blocks = (n_tokens + (kThreads / 32) - 1) / (kThreads / 32);
+  if (blocks > 0x7fffffff) return TW_ERR_BAD_ARG;
+  dim3 grid((unsigned)blocks, n_entries);
+  TW_DISPATCH_KV_DTYPE(dtype, T, {
+    int4_pack_kernel<T><<<grid, kThreads, 0, (cudaStream_t)stream>>>(
+        (const T*)keys, key_entry_stride, n_tokens, group_size, scale_div, packed, (T*)scale,
+        (T*)minimum, out_entry_stride, out_row_offset);
+    return check_launch();
+  });
+}
+
+extern "C" int tw_int4_pack(const void* keys, int64_t key_entry_stride, int n_entries,
+                            int64_t n_tokens, int head_dim, int group_size, int dtype,
+                            uint8_t* packed, void* scale, void* minimum,
+                            int64_t out_entry_stride, int64_t out_row_offset, void* stream) {
+  return tw_int4_pack_mode(keys, key_entry_stride, n_entries, n_tokens, head_dim, group_size,
+                           dtype, packed, scale, minimum, out_entry_stride, out_row_offset,
+                           kScaleReciprocal, stream);
+}
+
+// Same as tw_int4_pack with an explicit rounding mode of the `/ 15` step:
+// 0 = multiply by the fp32 reciprocal (torch on CUDA), 1 = IEEE divide (torch on CPU).
+extern "C" int tw_int4_pack_ex(const void* keys, int64_t key_entry_stride, int n_entries,
+                               int64_t n_tokens, int head_dim, int group_size, int dtype,
+                               uint8_t* packed, void* scale, void* minimum,
+                               int64_t out_entry_stride, int64_t out_row_offset, int scale_div,
+                               void* stream) {
+  return tw_int4_pack_mode(keys, key_entry_stride, n_entries, n_tokens, head_dim, group_size,
+                           dtype, packed, scale, minimum, out_entry_stride, out_row_offset,
+                           scale_div, stream);
+}
+
+// 1/sqrt(D) as torch on CUDA applies `logits /= math.sqrt(D)`: the double
+// divisor is narrowed to fp32 and its fp32 reciprocal multiplies.
+float inv_sqrt_head_dim(int head_dim) {
+  const float d = (float)sqrt((double)head_dim);
+  return 1.0f / d;
+}
+
+int launch_int4_qk(const float* q, const uint8_t* packed, const void* scale, const void* minimum,
+                   int64_t entry_stride_tokens, const int32_t* pages, int groups, int R,
+                   int b0_pages, int block_size, int sink, int group_size, int dtype,
+                   float* logits, cudaStream_t stream) {
+  const int n_cand = b0_pages * block_size;
+  constexpr int kThreads = 256;
+  constexpr int kTokensPerCta = 256;
+  dim3 grid((n_cand + kTokensPerCta - 1) / kTokensPerCta, groups * R);
+  const float inv = inv_sqrt_head_dim(kHeadDim);
+  TW_DISPATCH_KV_DTYPE(dtype, T, {
+    int4_qk_kernel<T><<<grid, kThreads, 0, stream>>>(
+        q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages, R, b0_pages,
+        block_size, sink, group_size, inv, logits, kTokensPerCta);
+    return check_launch();
+  });
+}
+
+extern "C" int tw_int4_qk(const float* q, const uint8_t* packed, const void* scale,
+                          const void* minimum, int64_t entry_stride_tokens, const int32_t* pages,
+                          int groups, int heads_per_group, int b0_pages, int block_size,
+                          int sink, int head_dim, int group_size, int dtype, float* logits,
+                          void* stream) {
+  if (head_dim != kHeadDim || !valid_group_size(group_size)) return TW_ERR_UNSUPPORTED;
+  if (!q || !packed || !scale || !minimum || !pages || !logits || groups <= 0 ||
+      heads_per_group <= 0 || b0_pages < 0 || block_size <= 0 || sink < 0 ||
+      (int64_t)groups * heads_per_group > 65535)
+    return TW_ERR_BAD_ARG;
+  if (b0_pages == 0) return TW_OK;
+  return launch_int4_qk(q, packed, scale, minimum, entry_stride_tokens, pages, groups,
+                        heads_per_group, b0_pages, block_size, sink, group_size, dtype, logits,
+                        (cudaStream_t)stream);
+}
+
+extern "C" int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int first_entry,
+                               int groups, int64_t position, const void* cur_k, const void* cur_v,
+                               int head_dim, int dtype, int sink, int block_size, void* page_min,
+                               void* page_max, int64_t meta_entry_stride, uint8_t* packed,
+                               void* scale, void* minimum, int group_size, void* stream) {
+  if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
+  if (!cur_k || !cur_v || groups <= 0 || first_entry < 0 || position < 0 ||
+      position >= max_len || block_size <= 0 || sink < 0)
+    return TW_ERR_BAD_ARG;
+  if ((slab_k == nullptr) != (slab_v == nullptr)) return TW_ERR_BAD_ARG;
+  if ((page_min == nullptr) != (page_max == nullptr)) return TW_ERR_BAD_ARG;
+  if (packed != nullptr && (!scale || !minimum || !valid_group_size(group_size)))
+    return TW_ERR_BAD_ARG;
+  if ((slab_k && ((uintptr_t)slab_k & 15)) || ((uintptr_t)cur_k & 15) || ((uintptr_t)cur_v & 15))
+    return TW_ERR_BAD_ARG;
+  TW_DISPATCH_KV_DTYPE(dtype, T, {
+    append_token_kernel<T><<<groups, kHeadDim, 0, (cudaStream_t)stream>>>(
+        (uint4*)slab_k, (uint4*)slab_v, max_len, first_entry, position, (const T*)cur_k,
+        (const T*)cur_v, sink, block_size, (T*)page_min, (T*)page_max, meta_entry_stride,
+        packed, (T*)scale, (T*)minimum, packed ? group_size : 128, kScaleReciprocal);
+    return check_launch();
+  });
+}

@@ -1,0 +1,138 @@
+// Shared device helpers for the sm_100a sparse decode-attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/twilight_b200.h"
+
+namespace tw {
+
+constexpr int kHeadDim = 128;          // the only head_dim the path supports
+constexpr int kMaxHeadsPerGroup = 8;   // R <= 8 (one cluster of R CTAs per group)
+
+// Thread-local record of the last CUDA error (tw_last_cuda_error).
+void set_last_cuda_error(cudaError_t err);
+
+inline int check_launch() {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+
+// Order-preserving map of an fp32 value to uint32 (larger float -> larger key).
+// -0.0 is folded onto +0.0 so that equal values compare equal, as in torch.topk.
+__device__ __forceinline__ uint32_t float_key(float f) {
+  if (f == 0.0f) f = 0.0f;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// Deterministic e^x for x <= 0 in IEEE double, written from the Taylor series
+// of e^r on |r| <= ln2/2 after the reduction x = k*ln2 + r.  Every operation is
+// an explicitly rounded add or multiply, so the same sequence in the C oracle
+// (compiled without contraction) gives bit-identical results.
+// Inputs below -700 return 0 (their fixed-point mass is 0 either way), which
+// keeps 2^k a normal double built from its bit pattern.
+__device__ __forceinline__ double det_exp(double x) {
+  if (!(x >= -700.0)) return 0.0;
+  const double log2e = 1.4426950408889634;   // log2(e)
+  const double ln2 = 0.6931471805599453;     // ln(2)
+  double t = __dmul_rn(x, log2e);
+  double k = floor(__dadd_rn(t, 0.5));
+  double r = __dadd_rn(x, -__dmul_rn(k, ln2));
+  // Horner on 1/n!, n = 0..13
+  double p = 1.0 / 6227020800.0;                 // 1/13!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 479001600.0);   // 1/12!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 39916800.0);    // 1/11!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 3628800.0);     // 1/10!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 362880.0);      // 1/9!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 40320.0);       // 1/8!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 5040.0);        // 1/7!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 720.0);         // 1/6!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 120.0);         // 1/5!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 24.0);          // 1/4!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0 / 6.0);           // 1/3!
+  p = __dadd_rn(__dmul_rn(p, r), 0.5);                 // 1/2!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0);                 // 1/1!
+  p = __dadd_rn(__dmul_rn(p, r), 1.0);                 // 1/0!
+  const long long biased = (long long)k + 1023;
+  const double two_k = __longlong_as_double(biased << 52);
+  return __dmul_rn(p, two_k);
+}
+
+// Fixed-point softmax mass: e * 2^48 truncated.  Sums of up to 65536 masses
+// fit in 64 bits and are exact, hence order-independent.
+constexpr double kMassScale = 281474976710656.0;  // 2^48
+__device__ __forceinline__ unsigned long long mass_of(double e) {
+  return __double2ull_rz(__dmul_rn(e, kMassScale));
+}
+
+// Block-wide exclusive scan of one uint32 per thread (blockDim.x <= 1024).
+// `scratch` needs 32 words.  Returns the exclusive prefix; *total gets the sum.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* scratch,
+                                                         uint32_t* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = (lane < nwarps) ? scratch[lane] : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      uint32_t y = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += y;
+    }
+    scratch[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  uint32_t warp_base = (warp > 0) ? scratch[warp - 1] : 0u;
+  *total = scratch[nwarps - 1];
+  __syncthreads();
+  return warp_base + x - v;
+}
+
+}  // namespace tw
+
+#define TW_DISPATCH_KV_DTYPE(dtype, T, ...)                 \
+  do {                                                      \
+    if ((dtype) == TW_F16) {                                \
+      using T = __half;                                     \
+      __VA_ARGS__;                                          \
+    } else if ((dtype) == TW_BF16) {                        \
+      using T = __nv_bfloat16;                              \
+      __VA_ARGS__;                                          \
+    } else {                                                \
+      return TW_ERR_BAD_ARG;                                \
+    }                                                       \
+  } while (0)
