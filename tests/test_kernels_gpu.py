@@ -1,0 +1,351 @@
+"""GPU parity of each sm_100a kernel (called through the C ABI via ops.py).
+
+Integer / index / code outputs must equal oracle/exact.c bit for bit; the
+arithmetic order of the fp32 stages (Quest score, INT4 QK) is also restated
+there, so those are compared bit for bit too.  Where the reference's own
+torch expression runs on CUDA (oracle/torch_ref.py) it pins the CUDA
+semantics (INT4 reciprocal division, Quest score order).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import exact, synth, torch_ref
+from pipeline import DTYPE_CODE, bits, twilight_oracle
+from tolerance import ATTN_TOL_16BIT, ATTN_TOL_FP32
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float16, torch.bfloat16]
+
+
+def _rand_keys(E, S, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    k = torch.randn(E, S, 128, generator=g)
+    k[..., 5] *= 4.0
+    return k.to(dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("group", [32, 64, 128])
+@pytest.mark.parametrize("scale_div", [0, 1])
+def test_int4_pack_bitexact(tw, cuda, dtype, group, scale_div):
+    E, S, cap = 2, 777, 800
+    keys = _rand_keys(E, S, dtype, 1 + group)
+    keys[0, 3] = 1.0                       # constant row
+    keys[1, 7, :64] = -3.0                 # two-valued row
+    keys[1, 7, 64:] = 5.0
+    ng = 128 // group
+    packed = torch.zeros((E, cap, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((E, cap, ng), dtype=dtype, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys.to(cuda), group_size=group, packed=packed, scale=scale, minimum=minimum,
+                     out_row_offset=10, scale_div=scale_div)
+    torch.cuda.synchronize()
+    for e in range(E):
+        p, s, m = exact.int4_pack(bits(keys[e]), group, DTYPE_CODE[dtype], scale_div)
+        np.testing.assert_array_equal(packed[e, 10:10 + S].cpu().numpy(), p)
+        np.testing.assert_array_equal(scale[e, 10:10 + S].cpu().float().numpy(),
+                                      torch.from_numpy(s.view(np.int16)).view(dtype).float().numpy())
+        np.testing.assert_array_equal(minimum[e, 10:10 + S].cpu().float().numpy(),
+                                      torch.from_numpy(m.view(np.int16)).view(dtype).float().numpy())
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_int4_pack_matches_reference_expression_on_cuda(tw, cuda, dtype):
+    """tw_int4_pack (reciprocal mode) == the reference's affine_int4_pack run by torch on CUDA."""
+    keys = _rand_keys(1, 4096, dtype, 7)[0].to(cuda)
+    p_ref, s_ref, m_ref = torch_ref.affine_int4_pack(keys)
+    packed = torch.zeros((1, 4096, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((1, 4096, 1), dtype=dtype, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys[None], group_size=128, packed=packed, scale=scale, minimum=minimum)
+    torch.cuda.synchronize()
+    assert torch.equal(packed[0], p_ref)
+    assert torch.equal(scale[0, :, 0].float(), s_ref.float())
+    assert torch.equal(minimum[0, :, 0].float(), m_ref.float())
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_quest_metadata_bitexact(tw, cuda, dtype):
+    E, S, sink, block = 3, 64 + 16 * 40 + 5, 64, 16
+    keys = _rand_keys(E, S, dtype, 3)
+    cap = 50
+    pmin = torch.zeros((E, cap, 128), dtype=dtype, device=cuda)
+    pmax = torch.zeros_like(pmin)
+    n = tw.ops.quest_page_metadata(keys.to(cuda), sink=sink, block_size=block, page_min=pmin,
+                                   page_max=pmax)
+    torch.cuda.synchronize()
+    assert n == 40
+    for e in range(E):
+        a, b = exact.quest_page_metadata(bits(keys[e]), sink, block, DTYPE_CODE[dtype])
+        ta, tb = torch_ref.quest_page_metadata(keys[e], sink, block)
+        assert torch.equal(pmin[e, :40].cpu(), ta) and torch.equal(pmax[e, :40].cpu(), tb)
+        np.testing.assert_array_equal(bits(pmin[e, :40].cpu()), a)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("R", [1, 3, 4, 8])
+def test_quest_score_bitexact(tw, cuda, dtype, R):
+    G, P, cap = 4, 1000, 1024
+    g = torch.Generator().manual_seed(R)
+    a = torch.randn(G, cap, 128, generator=g).to(dtype)
+    b = torch.randn(G, cap, 128, generator=g).to(dtype)
+    lo, hi = torch.minimum(a, b), torch.maximum(a, b)
+    q = torch.randn(G, R, 128, generator=g)
+    q[0, 0] = q[0, 0].bfloat16().float()
+    q[-1, -1] *= torch.exp2(torch.randint(-12, 12, (128,), generator=g).float())
+    scores = tw.ops.quest_score(q.to(cuda), lo.to(cuda), hi.to(cuda), P)
+    torch.cuda.synchronize()
+    ref = exact.quest_score(q.numpy(), bits(lo[:, :P]), bits(hi[:, :P]), DTYPE_CODE[dtype])
+    np.testing.assert_array_equal(scores.cpu().numpy(), ref)
+    # the reference's torch expression on CUDA (pinned bit-equal to its fused
+    # kernel by the reference's own test under torch 2.7): agreement to fp32 rounding
+    tref = torch_ref.quest_scores(q.to(cuda), lo[:, :P].to(cuda), hi[:, :P].to(cuda)).cpu().numpy()
+    assert np.max(np.abs(tref - ref)) <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("n,k", [(17, 1), (186, 64), (2028, 256), (2048, 2048), (8188, 256), (16384, 1000)])
+def test_topk_pages_bitexact(tw, cuda, n, k):
+    g = torch.Generator().manual_seed(n)
+    scores = torch.randn(6, n, generator=g)
+    scores[1] = torch.round(scores[1] * 4) / 4        # many ties
+    scores[2] = 0.0                                   # all tied
+    scores[3, : n // 2] = -0.0
+    scores[4] = torch.arange(n, dtype=torch.float32)  # distinct ascending
+    out = tw.ops.topk_pages(scores.to(cuda), k)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), exact.topk_pages(scores.numpy(), k))
+    # set equality with torch.topk wherever the k-th value is not tied
+    ref = torch.topk(scores, k, dim=-1).indices.sort(dim=-1).values
+    assert torch.equal(out[0].cpu().long(), ref[0]) and torch.equal(out[4].cpu().long(), ref[4])
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("group", [32, 128])
+@pytest.mark.parametrize("R,block", [(4, 16), (3, 1), (8, 16)])
+def test_int4_qk_bitexact(tw, cuda, dtype, group, R, block):
+    G, S, sink = 2, 1200, 64
+    keys = _rand_keys(G, S, dtype, 11)
+    ng = 128 // group
+    packed = torch.zeros((G, S, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((G, S, ng), dtype=dtype, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys.to(cuda), group_size=group, packed=packed, scale=scale, minimum=minimum)
+    P = (S - sink - 255) // block
+    b0 = min(P, 512 // block)
+    g = torch.Generator().manual_seed(5)
+    pages = torch.stack([torch.stack([torch.randperm(P, generator=g)[:b0].sort().values
+                                      for _ in range(R)]) for _ in range(G)]).int()
+    q = torch.randn(G, R, 128, generator=g)
+    logits = tw.ops.int4_qk(q.to(cuda), packed, scale, minimum, pages.to(cuda), block_size=block,
+                            sink=sink)
+    torch.cuda.synchronize()
+    ref = exact.int4_qk(q.numpy(), packed.cpu().numpy(), bits(scale.cpu()), bits(minimum.cpu()),
+                        pages.numpy(), block, sink, group, DTYPE_CODE[dtype])
+    np.testing.assert_array_equal(logits.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("case", ["random", "ties", "peaked", "p_one", "tiny"])
+def test_top_p_union_bitexact(tw, cuda, case):
+    G, R, block, sink, top_p = 3, 4, 16, 64, 0.95
+    b0 = 64
+    L = 64 + 16 * 300 + 255
+    g = torch.Generator().manual_seed(["random", "ties", "peaked", "p_one", "tiny"].index(case))
+    if case == "tiny":
+        R, block, sink, b0, L, top_p = 3, 1, 1, 8, 16, 0.85
+    n = b0 * block
+    P = (max(sink, L - 255 if case != "tiny" else L - 1) - sink) // block
+    pages = torch.stack([torch.stack([torch.randperm(P, generator=g)[:b0].sort().values
+                                      for _ in range(R)]) for _ in range(G)]).int()
+    logits = torch.randn(G, R, n, generator=g)
+    if case == "ties":
+        logits = torch.round(logits * 2) / 2
+    elif case == "peaked":
+        logits = logits * 10
+    elif case == "p_one":
+        top_p = 1.0
+    recent = 256 if case != "tiny" else 2
+    sink_end = min(sink, L)
+    recent_start = max(sink_end, L - (recent - 1))
+    union_pos = torch.full((G, L), -7, dtype=torch.int32, device=cuda)
+    union_count = torch.zeros(G, dtype=torch.int32, device=cuda)
+    head_count = torch.zeros((G, R), dtype=torch.int32, device=cuda)
+    head_pos = torch.full((G, R, n), -7, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    tw.ops.top_p_union(logits.to(cuda), pages.to(cuda), block_size=block, sink=sink, top_p=top_p,
+                       old_length=L, sink_end=sink_end, recent_start=recent_start,
+                       union_pos=union_pos, union_count=union_count, head_count=head_count,
+                       head_pos=head_pos, error_flag=err)
+    torch.cuda.synchronize()
+    unions, hc, hp, bad = exact.top_p_union(logits.numpy(), pages.numpy(), block, sink, top_p, L,
+                                            sink_end, recent_start)
+    assert int(err.item()) == 0 and bad == 0
+    np.testing.assert_array_equal(head_count.cpu().numpy(), hc)
+    for gi in range(G):
+        np.testing.assert_array_equal(union_pos[gi, : int(union_count[gi])].cpu().numpy(), unions[gi])
+        for r in range(R):
+            np.testing.assert_array_equal(head_pos[gi, r, : hc[gi, r]].cpu().numpy(), hp[gi][r])
+
+
+@pytest.mark.parametrize("name,cfg", [
+    ("twilight_outliers", dict(groups=2, heads=4, length=2048, dtype="float16", seed=11,
+                               workload="outliers", sink=64, recent=256, block=16, b0_tokens=512,
+                               top_p=0.95, n_needles=0)),
+    ("twilight_needles", dict(groups=2, heads=4, length=1536, dtype="bfloat16", seed=12,
+                              workload="needles", sink=64, recent=256, block=16, b0_tokens=256,
+                              top_p=0.9, n_needles=8)),
+])
+def test_select_layer_matches_reference_golden(tw, cuda, name, cfg):
+    """Whole-layer selection on the GPU (INT4 packed in the CPU rounding mode the
+    golden run used) reproduces the reference's unions and per-head counts."""
+    from pathlib import Path
+    golden = np.load(Path(__file__).resolve().parent / "golden" / f"{name}.npz")
+    layer = synth.make_layer(groups=cfg["groups"], heads_per_group=cfg["heads"], length=cfg["length"],
+                             dtype=cfg["dtype"], seed=cfg["seed"], workload=cfg["workload"],
+                             sink=cfg["sink"], recent=cfg["recent"], block=cfg["block"],
+                             n_needles=cfg["n_needles"])
+    G, R, L = cfg["groups"], cfg["heads"], cfg["length"]
+    dt = layer.keys.dtype
+    keys = layer.keys.to(cuda)
+    cap = (L - cfg["sink"]) // cfg["block"] + 1
+    pmin = torch.zeros((G, cap, 128), dtype=dt, device=cuda)
+    pmax = torch.zeros_like(pmin)
+    P_built = tw.ops.quest_page_metadata(keys, sink=cfg["sink"], block_size=cfg["block"],
+                                         page_min=pmin, page_max=pmax)
+    packed = torch.zeros((G, L, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((G, L, 1), dtype=dt, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys, group_size=128, packed=packed, scale=scale, minimum=minimum,
+                     scale_div=tw.ops.SCALE_DIVIDE)
+    w = torch_ref.window(L, sink=cfg["sink"], recent=cfg["recent"], block=cfg["block"],
+                         candidate_token_budget=cfg["b0_tokens"], metadata_pages=P_built)
+    q = layer.queries.float().to(cuda)
+    scores = tw.ops.quest_score(q, pmin, pmax, w.candidate_pages)
+    pages = tw.ops.topk_pages(scores, w.b0_pages)
+    logits = tw.ops.int4_qk(q, packed, scale, minimum, pages, block_size=cfg["block"], sink=cfg["sink"])
+    union_pos = torch.zeros((G, L), dtype=torch.int32, device=cuda)
+    union_count = torch.zeros(G, dtype=torch.int32, device=cuda)
+    head_count = torch.zeros((G, R), dtype=torch.int32, device=cuda)
+    tw.ops.top_p_union(logits, pages, block_size=cfg["block"], sink=cfg["sink"], top_p=cfg["top_p"],
+                       old_length=L, sink_end=w.sink_end, recent_start=w.recent_start,
+                       union_pos=union_pos, union_count=union_count, head_count=head_count)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(head_count.cpu().numpy(), golden["desired"])
+    for gi in range(G):
+        n = int(union_count[gi])
+        np.testing.assert_array_equal(union_pos[gi, :n].cpu().numpy(),
+                                      golden["unions"][gi][: golden["union_counts"][gi]])
+
+
+def test_gather_kv_contract(tw, cuda):
+    """hi/cpu_kv_gather.cpp contract on the GPU, from device and from mapped host memory."""
+    g = torch.Generator().manual_seed(123)
+    k = torch.randn(10000, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(10000, 128, generator=g).to(torch.bfloat16)
+    geom = tw.SlabGeometry(num_entries=1, batch_size=1, max_cache_len=10000, head_dim=128)
+    slab = tw.MappedHostSlab(geom, torch.bfloat16)
+    slab.entry("key", 0)[0, 0].copy_(k)
+    slab.entry("value", 0)[0, 0].copy_(v)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for source in ("device", "mapped"):
+        for n in (0, 1, 8192):
+            rows = torch.randint(10000, (n,), generator=g)
+            a = torch.zeros(n, 128, dtype=k.dtype, device=cuda)
+            b = torch.zeros_like(a)
+            src_k = k.to(cuda) if source == "device" else (slab.entry("key", 0)[0, 0], slab.key_device_ptr)
+            src_v = v.to(cuda) if source == "device" else (slab.entry("value", 0)[0, 0], slab.value_device_ptr)
+            tw.ops.gather_kv(src_k, src_v, rows.to(cuda), a, b, err)
+            torch.cuda.synchronize()
+            assert torch.equal(a.cpu(), k[rows]) and torch.equal(b.cpu(), v[rows])
+            assert int(err.item()) == 0
+    for bad in (-1, 10000):
+        out = torch.full((2, 128), 7.0, dtype=k.dtype, device=cuda)
+        rows = torch.tensor([bad, 3], device=cuda)
+        tw.ops.gather_kv(k.to(cuda), v.to(cuda), rows, out, out.clone(), err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == tw._lib.TW_ERR_INVALID_INDEX
+        assert torch.equal(out[0].cpu(), torch.full((128,), 7.0, dtype=k.dtype))  # skipped
+        assert torch.equal(out[1].cpu(), k[3])
+        err.zero_()
+    slab.close()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("S,R,lengths", [
+    (8, 4, [1, 2, 129, 300, 4400, 1, 4096, 257]),
+    (4, 8, [1000, 1, 128, 8193]),
+    (32, 1, [1300] * 32),
+    (3, 3, [17, 0, 5]),
+])
+def test_decode_attention(tw, cuda, dtype, S, R, lengths):
+    g = torch.Generator().manual_seed(S * 100 + R)
+    total = sum(lengths)
+    q = (torch.randn(S, R, 128, generator=g) * 2).to(dtype)
+    k = torch.randn(total, 128, generator=g).to(dtype)
+    v = torch.randn(total, 128, generator=g).to(dtype)
+    cu = torch.tensor([0] + list(np.cumsum(lengths)), dtype=torch.int32)
+    max_len = max(lengths)
+    ws = torch.zeros(tw.ops.decode_attention_workspace_bytes(S, R, max_len), dtype=torch.uint8, device=cuda)
+    lse = torch.zeros(S, R, device=cuda)
+    out32 = tw.ops.decode_attention(q.to(cuda), k.to(cuda), v.to(cuda), cu.to(cuda), max_len,
+                                    workspace=ws, out_dtype=torch.float32, lse=lse)
+    out16 = tw.ops.decode_attention(q.to(cuda), k.to(cuda), v.to(cuda), cu.to(cuda), max_len,
+                                    workspace=ws)
+    torch.cuda.synchronize()
+    for s in range(S):
+        a, b = int(cu[s]), int(cu[s + 1])
+        if b == a:
+            assert torch.all(out32[s].cpu() == 0)
+            continue
+        ref = torch_ref.decode_attention(q[s], k[a:b], v[a:b])
+        np.testing.assert_allclose(out32[s].cpu().double().numpy(), ref.numpy(), atol=ATTN_TOL_FP32, rtol=0)
+        np.testing.assert_allclose(out16[s].cpu().double().numpy(), ref.numpy(), atol=ATTN_TOL_16BIT, rtol=0)
+        sc = (q[s].double() @ k[a:b].double().T) / math.sqrt(128)
+        np.testing.assert_allclose(lse[s].cpu().double().numpy(), torch.logsumexp(sc, -1).numpy(),
+                                   atol=1e-3, rtol=0)
+    # the workspace counters are left at zero for the next call
+    assert int(ws[:4 * S].view(torch.int32).abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_append_token_running_metadata(tw, cuda, dtype):
+    """Appending rows one by one gives the slab rows, the bulk page min/max and
+    the INT4 codes of those rows."""
+    E, max_len, sink, block, G = 2, 160, 4, 16, 2
+    keys = _rand_keys(E, max_len, dtype, 9)
+    vals = _rand_keys(E, max_len, dtype, 10)
+    geom = tw.SlabGeometry(num_entries=E, batch_size=1, max_cache_len=max_len, head_dim=128)
+    slab = tw.MappedHostSlab(geom, dtype)
+    cap = math.ceil((max_len - sink) / block)
+    pmin = torch.zeros((E, cap, 128), dtype=dtype, device=cuda)
+    pmax = torch.zeros_like(pmin)
+    packed = torch.zeros((E, max_len, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((E, max_len, 4), dtype=dtype, device=cuda)
+    minimum = torch.zeros_like(scale)
+    lib = tw.load_library()
+    kd, vd = keys.to(cuda), vals.to(cuda)
+    for pos in range(max_len):
+        kn = kd[:, pos].contiguous()
+        vn = vd[:, pos].contiguous()
+        tw._lib.check(lib.tw_append_token(
+            slab.key_device_ptr, slab.value_device_ptr, max_len, 0, G, pos, kn.data_ptr(),
+            vn.data_ptr(), 128, DTYPE_CODE[dtype], sink, block, pmin.data_ptr(), pmax.data_ptr(),
+            cap * 128, packed.data_ptr(), scale.data_ptr(), minimum.data_ptr(), 32,
+            torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(slab.rows[0, :, :], keys) and torch.equal(slab.rows[1, :, :], vals)
+    full = (max_len - sink) // block
+    for e in range(E):
+        a, b = exact.quest_page_metadata(bits(keys[e]), sink, block, DTYPE_CODE[dtype])
+        np.testing.assert_array_equal(bits(pmin[e, :full].cpu()), a)
+        np.testing.assert_array_equal(bits(pmax[e, :full].cpu()), b)
+        p, s, m = exact.int4_pack(bits(keys[e]), 32, DTYPE_CODE[dtype], 0)
+        np.testing.assert_array_equal(packed[e].cpu().numpy(), p)
+        np.testing.assert_array_equal(bits(scale[e].cpu()), s)
+    slab.close()

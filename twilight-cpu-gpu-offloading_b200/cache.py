@@ -727,10 +727,11 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         for k, v in zip(key_states, value_states):
             if k.shape != v.shape or tuple(k.shape) != (1, 1, 1, HEAD_DIM):
                 raise ValueError("GQA group decode expects [1, 1, 1, dim] K/V")
-        old_length = self._advance_layer(entries)
-        prepared = self._prepared.pop(entries[0], None)
-        if prepared is None or prepared["old_length"] != old_length:
+        prepared = self._prepared.get(entries[0])
+        if prepared is None or prepared["old_length"] != self._layer_old_length(entries):
             raise AssertionError("prepared GPU GQA union is missing")
+        del self._prepared[entries[0]]
+        old_length = self._advance_layer(entries)
         k_new = torch.cat([k[0, 0] for k in key_states], dim=0)
         v_new = torch.cat([v[0, 0] for v in value_states], dim=0)
         return old_length, k_new, v_new

@@ -89,7 +89,9 @@ decode_attention_kernel(const T* __restrict__ q, const T* __restrict__ k, const 
   const int s = blockIdx.y;
   const int split = blockIdx.x;
   const int seg_begin = cu[s];
-  const int seg_len = cu[s + 1] - seg_begin;
+  // Rows beyond max_splits * kAttnChunk (a caller's max_seqlen_k below the real
+  // segment length) are not read: the split count is clamped to the grid.
+  const int seg_len = min(cu[s + 1] - seg_begin, max_splits * kAttnChunk);
   const int nsplit = (seg_len + kAttnChunk - 1) / kAttnChunk;
   if (split >= max(nsplit, 1)) return;
   const int lane = threadIdx.x & 31;
