@@ -338,7 +338,7 @@ def run_ours(args) -> int:
     if rank == 0:
         pinned = pinned_h2d_peak_gbs(device)
         mapped = mapped_read_peak_gbs(tw, step, device)
-        e2e = run_e2e(tw, layer, queries, device, K, W)
+        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W)
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
     if world > 1:
@@ -620,6 +620,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
