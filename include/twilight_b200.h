@@ -229,6 +229,33 @@ int tw_decode_attention(const void* q, const void* k, const void* v, const int32
                         int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- allocation-free decode attention ---------------------------------------------------------------
+ * No counterpart in the reference: an addition of this library.  Same
+ * computation, arguments and result as tw_decode_attention, but the caller
+ * passes no workspace.  It is for callers that cannot allocate device memory:
+ * a serving runtime that has reserved all device memory for its own arena, or
+ * a host written in another language that is handed device buffers but has no
+ * CUDA allocator to call.  The split-K scratch (merge counters and per-split
+ * partials) lives in one fixed array of TW_NOALLOC_SCRATCH_BYTES inside this
+ * library; every GPU that loads the library holds its own copy until the
+ * process exits.  The call allocates nothing and calls no allocating routine.
+ *   - Capacity: returns TW_ERR_CAPACITY (nothing launched) when the scratch
+ *     needed exceeds the array: about segments * heads * ceil(max_seqlen_k/128)
+ *     * 520 bytes (e.g. 8 segments x 4 heads up to max_seqlen_k ~ 31 000).
+ *     A call with max_seqlen_k <= 128 uses no scratch.
+ *   - Set-up: the first call on each device looks up the array's device
+ *     address (cudaGetSymbolAddress) with that device current; make that
+ *     first call before any stream capture.
+ *   - Sharing: every call on a device uses the same array, which keeps the
+ *     last call's contents (the call clears the counters it needs).  Calls
+ *     whose executions overlap on the GPU (e.g. on two streams at once) race
+ *     on the array and corrupt each other's results: serialise them. */
+#define TW_NOALLOC_SCRATCH_BYTES (4u << 20)
+int tw_decode_attention_noalloc(const void* q, const void* k, const void* v,
+                                const int32_t* cu_seqlens, int segments, int heads_per_segment,
+                                int max_seqlen_k, int head_dim, int dtype, float softmax_scale,
+                                void* out, int out_dtype, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

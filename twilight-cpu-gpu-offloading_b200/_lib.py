@@ -62,6 +62,7 @@ SIGNATURES = {
                               P, I32, P]),
     "tw_decode_attention_workspace_size": (SZ, [I32, I32, I32, I32]),
     "tw_decode_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P, SZ, P]),
+    "tw_decode_attention_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P]),
 }
 
 _lib = None

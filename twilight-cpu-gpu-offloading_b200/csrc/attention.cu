@@ -8,6 +8,8 @@
 // heads each) and G*R (Quest per-query-head segments, 1 head each).
 #include <math_constants.h>
 
+#include <mutex>
+
 #include "tw_common.cuh"
 
 namespace tw {
@@ -300,4 +302,92 @@ extern "C" int tw_decode_attention(const void* q, const void* k, const void* v,
                                                           scale_log2, ws, out, lse, st);
   }
   return TW_ERR_UNSUPPORTED;
+}
+
+// ---- allocation-free variant ----------------------------------------------------
+// Some callers cannot allocate device memory: a serving runtime that has
+// reserved all device memory for its own arena, or a foreign-language host
+// that is handed device buffers but has no CUDA allocator to call.  For them
+// tw_decode_attention_noalloc keeps the split-K scratch (merge counters and
+// per-split partials) in this fixed array.  Each GPU that loads the library
+// holds its own copy until the process exits.  Host code must not pass the
+// symbol itself to a kernel (on the host it is only a stand-in, not a device
+// address); its device address comes from cudaGetSymbolAddress, looked up
+// once per device on that device's first call.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[TW_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+void* g_noalloc_ptr[kNoAllocMaxDevices];
+cudaError_t g_noalloc_err[kNoAllocMaxDevices];
+
+// Device address of this device's scratch array (set up on first use).
+int noalloc_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return TW_ERR_UNSUPPORTED;
+  std::call_once(g_noalloc_once[dev], [dev]() {
+    void* p = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_ptr[dev] = p;
+  });
+  if (g_noalloc_err[dev] != cudaSuccess) {
+    set_last_cuda_error(g_noalloc_err[dev]);
+    return TW_ERR_CUDA;
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return TW_OK;
+}
+}  // namespace
+
+extern "C" int tw_decode_attention_noalloc(const void* q, const void* k, const void* v,
+                                           const int32_t* cu_seqlens, int segments,
+                                           int heads_per_segment, int max_seqlen_k, int head_dim,
+                                           int dtype, float softmax_scale, void* out,
+                                           int out_dtype, float* lse, void* stream) {
+  if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !cu_seqlens || !out || segments <= 0 || segments > 65535 ||
+      heads_per_segment <= 0 || max_seqlen_k < 0 || !(softmax_scale > 0.0f))
+    return TW_ERR_BAD_ARG;
+  if (heads_per_segment > kMaxHeadsPerGroup) return TW_ERR_UNSUPPORTED;
+  if (out_dtype != dtype && out_dtype != TW_F32) return TW_ERR_BAD_ARG;
+  if (dtype != TW_F16 && dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
+  const int max_splits = attn_max_splits(max_seqlen_k);
+  const size_t need = attn_ws_bytes(segments, heads_per_segment, max_splits, nullptr, nullptr);
+  if (max_splits > 1 && need > (size_t)TW_NOALLOC_SCRATCH_BYTES) return TW_ERR_CAPACITY;
+  cudaStream_t st = (cudaStream_t)stream;
+  AttnWorkspace ws{};
+  if (max_splits > 1) {
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != TW_OK) return rc;
+    attn_ws_bytes(segments, heads_per_segment, max_splits, &ws, reinterpret_cast<char*>(scratch));
+    // The array keeps the previous call's contents: the merge counters must
+    // start at zero.
+    cudaError_t err = cudaMemsetAsync(ws.counters, 0, (size_t)segments * sizeof(unsigned int), st);
+    if (err != cudaSuccess) {
+      set_last_cuda_error(err);
+      return TW_ERR_CUDA;
+    }
+  }
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  if (dtype == TW_F16) {
+    if (out_dtype == TW_F32)
+      return launch_attention<__half, float>(q, k, v, cu_seqlens, segments, heads_per_segment,
+                                             max_splits, scale_log2, ws, out, lse, st);
+    return launch_attention<__half, __half>(q, k, v, cu_seqlens, segments, heads_per_segment,
+                                            max_splits, scale_log2, ws, out, lse, st);
+  }
+  if (out_dtype == TW_F32)
+    return launch_attention<__nv_bfloat16, float>(q, k, v, cu_seqlens, segments,
+                                                  heads_per_segment, max_splits, scale_log2, ws,
+                                                  out, lse, st);
+  return launch_attention<__nv_bfloat16, __nv_bfloat16>(q, k, v, cu_seqlens, segments,
+                                                        heads_per_segment, max_splits, scale_log2,
+                                                        ws, out, lse, st);
 }
