@@ -149,8 +149,9 @@ def build_workload(tw, device: torch.device, seed: int, n_queries: int):
 class DeviceStep:
     """The hot path launched through the C ABI on fixed device buffers."""
 
-    def __init__(self, tw, layer, device: torch.device) -> None:
+    def __init__(self, tw, layer, device: torch.device, fused: bool = True) -> None:
         self.tw = tw
+        self.fused = fused
         self.lib = tw.load_library()
         G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
         self.G, self.R, self.L = G, R, L
@@ -199,7 +200,7 @@ class DeviceStep:
         self.q16 = torch.empty((G, R, 128), dtype=torch.float16, device=device)
         self.k_new = layer.key_new.to(device)
         self.v_new = layer.value_new.to(device)
-        self.launches_per_step = 7
+        self.launches_per_step = 6 if fused else 7
 
     def load_query(self, q16: torch.Tensor) -> None:
         self.q16.copy_(q16)
@@ -222,20 +223,30 @@ class DeviceStep:
             self.ws.numel(), st), "select_layer")
         if "select" in ev:
             ev["select"][1].record()
-            ev["gather"][0].record()
-        tw._lib.check(lib.tw_gather_union(
-            self.slab.key_device_ptr, self.slab.value_device_ptr, self.max_len, 0, G, self.L,
-            self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
-            self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, self.flat_k.data_ptr(),
-            self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), st),
-            "gather_union")
-        if "gather" in ev:
-            ev["gather"][1].record()
-            ev["attention"][0].record()
-        tw.ops.decode_attention(self.q16, self.flat_k, self.flat_v, self.cu, self.per_group_cap,
-                                workspace=self.attn_ws, out=self.out)
-        if "attention" in ev:
-            ev["attention"][1].record()
+        if self.fused:
+            if "attention" in ev:
+                ev["attention"][0].record()
+            tw.ops.attend_union(self.slab, 0, self.L, self.union_pos, self.union_count, self.k_new,
+                                self.v_new, self.q16, self.per_group_cap, workspace=self.attn_ws,
+                                error_flag=self.err, out=self.out)
+            if "attention" in ev:
+                ev["attention"][1].record()
+        else:
+            if "gather" in ev:
+                ev["gather"][0].record()
+            tw._lib.check(lib.tw_gather_union(
+                self.slab.key_device_ptr, self.slab.value_device_ptr, self.max_len, 0, G, self.L,
+                self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
+                self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, self.flat_k.data_ptr(),
+                self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), st),
+                "gather_union")
+            if "gather" in ev:
+                ev["gather"][1].record()
+                ev["attention"][0].record()
+            tw.ops.decode_attention(self.q16, self.flat_k, self.flat_v, self.cu, self.per_group_cap,
+                                    workspace=self.attn_ws, out=self.out)
+            if "attention" in ev:
+                ev["attention"][1].record()
         # new token written at position L (the step is repeated at a fixed length)
         tw._lib.check(lib.tw_append_token(
             self.slab.key_device_ptr, self.slab.value_device_ptr, self.max_len, 0, G, self.L,
@@ -255,7 +266,7 @@ class DeviceStep:
         hbm = (2 * self.G * self.cand_pages * 128 * 2      # Quest min/max, read once per group
                + cand_tokens * (64 + ng * 2 * 2)           # INT4 codes + scale/min of unique candidates
                + 3 * 4 * self.G * self.R * self.b0 * CFG["block"]  # fp32 logits write/read + scores
-               + 2 * 512 * (rows + self.G))                # staged K/V rows written then read
+               + (0 if self.fused else 2 * 512 * (rows + self.G)))  # staged K/V written then read
         return {"union_rows": rows, "host_bytes": host, "hbm_bytes": hbm,
                 "gather_bytes": host, "unique_candidate_tokens": cand_tokens}
 
@@ -278,7 +289,7 @@ def run_ours(args) -> int:
     tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
     K, W = args.steps, args.warmup
     layer, queries = build_workload(tw, device, seed=rank, n_queries=K + W)
-    step = DeviceStep(tw, layer, device)
+    step = DeviceStep(tw, layer, device, fused=not args.staged)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     torch.cuda.synchronize()
 
@@ -288,7 +299,7 @@ def run_ours(args) -> int:
     torch.cuda.synchronize()
     step.err.zero_()
 
-    names = ("select", "gather", "attention")
+    names = ("select", "attention") if step.fused else ("select", "gather", "attention")
     per_step, kern = [], {n: [] for n in names}
     byte_log = []
     q_dev = queries[W:].to(device)
@@ -351,7 +362,8 @@ def run_ours(args) -> int:
         hbm_src = "measured" if peaks.get("hbm_gbs") else "fallback"
         ms_per_step = max_total_ms / K
         value = world * K / (max_total_ms * 1e-3)
-        gather_ms = float(np.mean(kern_ms["gather"]))
+        dom = "attention" if step.fused else "gather"
+        gather_ms = float(np.mean(kern_ms[dom]))
         gather_gbs = avg["gather_bytes"] / (gather_ms * 1e-3) / 1e9
         t_roof_ms = max(avg["hbm_bytes"] / (hbm_peak * 1e9), avg["host_bytes"] / (pinned * 1e9)) * 1e3
         line = {
@@ -376,6 +388,7 @@ def run_ours(args) -> int:
                             "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
                 "l2": "flushed before every timed step (512 MiB device write, outside the events)",
                 "parallelism": f"request-sharded replicas x{world}",
+                "path": "fused gather+attention" if step.fused else "staged gather then attention",
                 "mean_union_rows": avg["union_rows"],
             },
             "clocks": clocks,
@@ -383,7 +396,8 @@ def run_ours(args) -> int:
             "kernel_ms": {n: round(float(np.mean(v)), 5) for n, v in kern_ms.items()},
             "roofline": {
                 "bound": "host_link",
-                "kernel": "gather_union_kernel (zero-copy mapped-host reads)",
+                "kernel": ("attention_kernel<UnionRows> (fused zero-copy gather + split-K attention)"
+                           if step.fused else "gather_union_kernel (zero-copy mapped-host reads)"),
                 "achieved": round(gather_gbs, 2),
                 "peak": round(pinned, 2),
                 "peak_source": "pinned H2D cudaMemcpyAsync measured in this run (256 MiB, best of 6)",
@@ -452,16 +466,17 @@ def run_e2e(tw, layer, queries, device, K, W) -> dict:
     out_host = torch.empty((G, R, 128), dtype=torch.float16, pin_memory=True)
     entries = list(range(G))
 
+    q_dev = torch.empty((G, R, 128), dtype=torch.float16, device=device)
+    kv_dev = torch.empty((2, G, 128), dtype=torch.float16, device=device)
+    host_kv = torch.stack((layer.key_new, layer.value_new)).pin_memory()
+    out_dev = torch.empty((G, R, 128), dtype=torch.float16, device=device)
+
     def one(i):
-        q = host_q[i].to(device, non_blocking=True)
-        kn = host_k.to(device, non_blocking=True)
-        vn = host_v.to(device, non_blocking=True)
-        qs = [q[g].view(1, R, 1, 128) for g in range(G)]
-        ks = [kn[g] for g in range(G)]
-        vs = [vn[g] for g in range(G)]
-        cache.prepare_layer_selection(entries=entries, queries=qs)
-        out = cache.attend_layer(key_states=ks, value_states=vs, queries=qs, entries=entries)
-        out_host.copy_(out, non_blocking=True)
+        q_dev.copy_(host_q[i], non_blocking=True)
+        kv_dev.copy_(host_kv, non_blocking=True)
+        cache.decode_layer(queries=q_dev, key_states=kv_dev[0], value_states=kv_dev[1],
+                           entries=entries, out=out_dev)
+        out_host.copy_(out_dev, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
 
     for i in range(W):
@@ -475,7 +490,7 @@ def run_e2e(tw, layer, queries, device, K, W) -> dict:
     h2d = (G * R * 128 + 2 * G * 128) * 2
     return {"value": round(K / dt, 3), "unit": "layer-steps/s", "us_per_layer_step": round(dt / K * 1e6, 2),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": G * R * 128 * 2,
-            "api": "TwilightMatchedBudgetOffloadedCache.prepare_layer_selection + attend_layer",
+            "api": "TwilightMatchedBudgetOffloadedCache.decode_layer (one library call per layer-step)",
             "note": "K/V history stays in the pinned host slab and is read over the host link inside the step"}
 
 
@@ -621,6 +636,8 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
+    ap.add_argument("--staged", action="store_true",
+                    help="time the staged path (gather to HBM, then attention) instead of the fused kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -229,6 +229,82 @@ int tw_decode_attention(const void* q, const void* k, const void* v, const int32
                         int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- fused union gather + decode attention ---------------------------------------------------------
+ * The GQA group step without a staged copy: for each group g the split-K
+ * attention CTAs read the rows of union_pos[g][0..union_count[g]) straight
+ * from the (mapped host) slab, then the group's current token (cur_k/cur_v
+ * [G][D]), and write out [G][R][D] (q [G][R][D] in `dtype`).  Same result as
+ * tw_gather_union followed by tw_decode_attention.  Replaces the gather + H2D
+ * + FlashAttention sequence of hi/twilight_offload_cache.py:2973-3101 and
+ * hi/mp.py:258-279.  max_rows_per_group: an upper bound of union_count[g]+1
+ * (sizes the split grid and the workspace, as max_seqlen_k of
+ * tw_decode_attention_workspace_size(groups, R, max_rows_per_group, D)).
+ * Positions outside [0, old_length) are skipped and set *error_flag. */
+int tw_attend_union(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+                    int groups, int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
+                    const int32_t* union_count, const void* cur_k, const void* cur_v,
+                    const void* q, int heads_per_group, int max_rows_per_group, int head_dim,
+                    int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
+                    int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- whole decode layer-step --------------------------------------------------------------------------
+ * One decode layer-step of the Twilight GQA path in one call: Quest score ->
+ * top-k pages -> INT4 QK -> top-p + union -> fused union gather + attention ->
+ * new-token append (6 launches on `stream`, no host synchronisation).
+ * Replaces prepare_layer_selection + update_layer_gqa_group_ragged + the
+ * FlashAttention call of one layer (hi/twilight_offload_cache.py:996-1843,
+ * :2610-3602, hi/mp.py:233-279).  Cache pointers (slab, page min/max, INT4
+ * codes/scale/min) are the bases of entry 0; the layer's entries are
+ * first_entry .. first_entry+groups-1.  q is [G][R][D] in the K/V dtype (the
+ * reference selects with q.float(), an exact widening); k_new/v_new [G][D];
+ * out [G][R][D] in out_dtype.  Requires 0 < b0_pages <= n_pages.  append != 0
+ * also writes the new token at position old_length.  head_pos may be NULL. */
+typedef struct tw_decode_layer_args {
+  void* slab_k;
+  void* slab_v;
+  int64_t max_len;
+  int32_t first_entry;
+  int32_t groups;
+  int32_t heads_per_group;
+  int32_t dtype;
+  void* page_min;
+  void* page_max;
+  int64_t page_capacity;
+  int32_t n_pages;
+  uint8_t* packed;
+  void* scale;
+  void* minimum;
+  int32_t int4_group_size;
+  int32_t sink;
+  int32_t block_size;
+  int32_t b0_pages;
+  double top_p;
+  int64_t old_length;
+  int64_t sink_end;
+  int64_t recent_start;
+  const void* q;
+  const void* k_new;
+  const void* v_new;
+  void* out;
+  int32_t out_dtype;
+  int32_t append;
+  int32_t* pages;
+  int32_t* union_pos;
+  int64_t pos_stride;
+  int32_t* union_count;
+  int32_t* head_count;
+  int32_t* head_pos;
+  int32_t* error_flag;
+  void* select_workspace;
+  size_t select_workspace_bytes;
+  void* attn_workspace;
+  size_t attn_workspace_bytes;
+  int32_t max_rows_per_group;
+} tw_decode_layer_args;
+int tw_twilight_decode_layer(const tw_decode_layer_args* args, void* stream);
+/* sizeof(tw_decode_layer_args), for binding-layout checks. */
+size_t tw_decode_layer_args_size(void);
+
 /* ---- allocation-free decode attention ---------------------------------------------------------------
  * No counterpart in the reference: an addition of this library.  Same
  * computation, arguments and result as tw_decode_attention, but the caller

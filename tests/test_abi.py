@@ -55,3 +55,15 @@ def test_host_side_argument_checks(tw):
                                    None, 0, None, None, 0, None) == L.TW_ERR_UNSUPPORTED
     assert lib.tw_decode_attention_workspace_size(8, 4, 4096, 128) > 0
     assert lib.tw_select_layer_workspace_size(8, 4, 2028, 256, 16) >= 8 * 4 * (2028 + 4096) * 4
+
+
+def test_decode_layer_args_layout(tw):
+    """The ctypes mirror of tw_decode_layer_args has the C struct's size and a
+    plausible field layout (pointers 8-byte aligned)."""
+    lib = tw.load_library()
+    S = tw._lib.DecodeLayerArgs
+    assert ctypes.sizeof(S) == lib.tw_decode_layer_args_size()
+    for name, ctype in S._fields_:
+        if ctype in (ctypes.c_void_p, ctypes.c_int64, ctypes.c_double, ctypes.c_size_t):
+            assert getattr(S, name).offset % 8 == 0, name
+    assert lib.tw_twilight_decode_layer(None, None) == tw._lib.TW_ERR_BAD_ARG

@@ -239,3 +239,38 @@ def test_error_paths(tw, cuda):
     with pytest.raises(RuntimeError, match="capacity"):
         small.update(d.keys[0, :64].reshape(1, 1, 64, 128).to(cuda), d.values[0, :64].reshape(1, 1, 64, 128).to(cuda), 0)
     small.close()
+
+
+@pytest.mark.parametrize("R,dtype", [(4, "float16"), (8, "bfloat16")])
+def test_decode_layer_equals_prepare_plus_attend(tw, cuda, R, dtype):
+    """The one-call layer-step (tw_twilight_decode_layer) gives the same unions
+    and attention output, bit for bit, as prepare_layer_selection + attend_layer,
+    over consecutive steps (its append feeds the next step)."""
+    G, L = 2, 3072
+    tdt = synth.TORCH_DTYPES[dtype]
+    d = layer_data(1, G, R, L, dtype, 31)[0]
+    caches = [make_twilight(tw, cuda, layers=1, G=G, R=R, L=L, dtype=tdt, extra=4, b0_tokens=512)
+              for _ in range(2)]
+    for c in caches:
+        for g in range(G):
+            c.update(d.keys[g].view(1, 1, L, 128).to(cuda), d.values[g].view(1, 1, L, 128).to(cuda), g)
+    for step in range(3):
+        q, kn, vn = _step_inputs(cuda, G, R, dtype, 500 + step)
+        q, kn, vn = q.to(cuda), kn.to(cuda), vn.to(cuda)
+        qs = [q[g].view(1, R, 1, 128) for g in range(G)]
+        ks = [kn[g].view(1, 1, 1, 128) for g in range(G)]
+        vs = [vn[g].view(1, 1, 1, 128) for g in range(G)]
+        caches[0].prepare_layer_selection(entries=[0, 1], queries=qs)
+        two = caches[0].attend_layer(key_states=ks, value_states=vs, queries=qs, entries=[0, 1])
+        one = caches[1].decode_layer(queries=q, key_states=kn, value_states=vn, entries=[0, 1])
+        torch.cuda.synchronize()
+        assert torch.equal(one, two), step
+        b0, b1 = caches[0]._layer_bufs[G], caches[1]._layer_bufs[G]
+        assert torch.equal(b0["union_count"], b1["union_count"])
+        for g in range(G):
+            n = int(b0["union_count"][g])
+            assert torch.equal(b0["union_pos"][g, :n], b1["union_pos"][g, :n])
+    assert caches[1].get_seq_length(0) == L + 3
+    for c in caches:
+        c.synchronize()
+        c.close()

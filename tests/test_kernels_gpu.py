@@ -151,20 +151,27 @@ def test_int4_qk_bitexact(tw, cuda, dtype, group, R, block):
     np.testing.assert_array_equal(logits.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("case", ["random", "ties", "peaked", "p_one", "tiny"])
+CASES_TOP_P = ["random", "ties", "peaked", "p_one", "tiny", "large_radix", "large_ties"]
+
+
+@pytest.mark.parametrize("case", CASES_TOP_P)
 def test_top_p_union_bitexact(tw, cuda, case):
+    """Both top-p paths: the bitonic-sort path (<= 8192 candidates per row) and
+    the radix path (the two large_* cases, 10240 candidates)."""
     G, R, block, sink, top_p = 3, 4, 16, 64, 0.95
     b0 = 64
     L = 64 + 16 * 300 + 255
-    g = torch.Generator().manual_seed(["random", "ties", "peaked", "p_one", "tiny"].index(case))
+    g = torch.Generator().manual_seed(CASES_TOP_P.index(case))
     if case == "tiny":
         R, block, sink, b0, L, top_p = 3, 1, 1, 8, 16, 0.85
+    elif case.startswith("large"):
+        b0, L = 640, 64 + 16 * 700 + 255
     n = b0 * block
     P = (max(sink, L - 255 if case != "tiny" else L - 1) - sink) // block
     pages = torch.stack([torch.stack([torch.randperm(P, generator=g)[:b0].sort().values
                                       for _ in range(R)]) for _ in range(G)]).int()
     logits = torch.randn(G, R, n, generator=g)
-    if case == "ties":
+    if case in ("ties", "large_ties"):
         logits = torch.round(logits * 2) / 2
     elif case == "peaked":
         logits = logits * 10
@@ -348,4 +355,62 @@ def test_append_token_running_metadata(tw, cuda, dtype):
         p, s, m = exact.int4_pack(bits(keys[e]), 32, DTYPE_CODE[dtype], 0)
         np.testing.assert_array_equal(packed[e].cpu().numpy(), p)
         np.testing.assert_array_equal(bits(scale[e].cpu()), s)
+    slab.close()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("R", [1, 4, 8])
+def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
+    """The fused kernel (rows read in place from the mapped slab) equals the staged
+    path (tw_gather_union, then tw_decode_attention) bit for bit, and the float64
+    attention of the oracle within the stated tolerance."""
+    G, L, max_len = 3, 3000, 3100
+    g = torch.Generator().manual_seed(R)
+    keys = torch.randn(G, max_len, 128, generator=g).to(dtype)
+    vals = torch.randn(G, max_len, 128, generator=g).to(dtype)
+    geom = tw.SlabGeometry(num_entries=G, batch_size=1, max_cache_len=max_len, head_dim=128)
+    slab = tw.MappedHostSlab(geom, dtype)
+    slab.rows[0].copy_(keys)
+    slab.rows[1].copy_(vals)
+    counts = [0, 1, 2500]
+    union_pos = torch.zeros((G, L), dtype=torch.int32)
+    for gi, c in enumerate(counts):
+        union_pos[gi, :c] = torch.randperm(L, generator=g)[:c].sort().values.int()
+    union_pos, union_count = union_pos.to(cuda), torch.tensor(counts, dtype=torch.int32, device=cuda)
+    cur_k = torch.randn(G, 128, generator=g).to(dtype).to(cuda)
+    cur_v = torch.randn(G, 128, generator=g).to(dtype).to(cuda)
+    q = (torch.randn(G, R, 128, generator=g) * 2).to(dtype).to(cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    rows_cap = sum(counts) + G
+    flat_k = torch.empty(rows_cap, 128, dtype=dtype, device=cuda)
+    flat_v = torch.empty_like(flat_k)
+    cu = torch.zeros(G + 1, dtype=torch.int32, device=cuda)
+    lib = tw.load_library()
+    tw._lib.check(lib.tw_gather_union(
+        slab.key_device_ptr, slab.value_device_ptr, max_len, 0, G, L, union_pos.data_ptr(), L,
+        union_count.data_ptr(), cur_k.data_ptr(), cur_v.data_ptr(), 128, DTYPE_CODE[dtype],
+        flat_k.data_ptr(), flat_v.data_ptr(), rows_cap, cu.data_ptr(), err.data_ptr(),
+        torch.cuda.current_stream().cuda_stream))
+    max_rows = max(counts) + 1
+    ws = torch.zeros(tw.ops.decode_attention_workspace_bytes(G, R, max_rows), dtype=torch.uint8, device=cuda)
+    for out_dtype in (torch.float32, dtype):
+        staged = tw.ops.decode_attention(q, flat_k, flat_v, cu, max_rows, workspace=ws, out_dtype=out_dtype)
+        fused = tw.ops.attend_union(slab, 0, L, union_pos, union_count, cur_k, cur_v, q, max_rows,
+                                    workspace=ws, error_flag=err, out_dtype=out_dtype)
+        torch.cuda.synchronize()
+        assert torch.equal(staged, fused)
+        tol = ATTN_TOL_FP32 if out_dtype == torch.float32 else ATTN_TOL_16BIT
+        for gi, c in enumerate(counts):
+            pos = union_pos[gi, :c].long().cpu()
+            kk = torch.cat((keys[gi].index_select(0, pos), cur_k[gi:gi + 1].cpu()))
+            vv = torch.cat((vals[gi].index_select(0, pos), cur_v[gi:gi + 1].cpu()))
+            ref = torch_ref.decode_attention(q[gi].cpu(), kk, vv)
+            assert (fused[gi].cpu().double() - ref).abs().max().item() <= tol
+    assert int(err.item()) == 0
+    # a position outside [0, old_length) is skipped and flagged
+    union_pos[2, 5] = L + 7
+    tw.ops.attend_union(slab, 0, L, union_pos, union_count, cur_k, cur_v, q, max_rows, workspace=ws,
+                        error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == tw._lib.TW_ERR_INVALID_INDEX
     slab.close()

@@ -34,6 +34,26 @@ SZ = ctypes.c_size_t
 DBL = ctypes.c_double
 FLT = ctypes.c_float
 
+I32T = ctypes.c_int32
+
+
+class DecodeLayerArgs(ctypes.Structure):
+    """tw_decode_layer_args of include/twilight_b200.h (same field order and types)."""
+
+    _fields_ = [
+        ("slab_k", P), ("slab_v", P), ("max_len", I64), ("first_entry", I32T), ("groups", I32T),
+        ("heads_per_group", I32T), ("dtype", I32T), ("page_min", P), ("page_max", P),
+        ("page_capacity", I64), ("n_pages", I32T), ("packed", P), ("scale", P), ("minimum", P),
+        ("int4_group_size", I32T), ("sink", I32T), ("block_size", I32T), ("b0_pages", I32T),
+        ("top_p", DBL), ("old_length", I64), ("sink_end", I64), ("recent_start", I64), ("q", P),
+        ("k_new", P), ("v_new", P), ("out", P), ("out_dtype", I32T), ("append", I32T),
+        ("pages", P), ("union_pos", P), ("pos_stride", I64), ("union_count", P),
+        ("head_count", P), ("head_pos", P), ("error_flag", P), ("select_workspace", P),
+        ("select_workspace_bytes", SZ), ("attn_workspace", P), ("attn_workspace_bytes", SZ),
+        ("max_rows_per_group", I32T),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/twilight_b200.h
 SIGNATURES = {
     "tw_status_string": (ctypes.c_char_p, [I32]),
@@ -62,6 +82,10 @@ SIGNATURES = {
                               P, I32, P]),
     "tw_decode_attention_workspace_size": (SZ, [I32, I32, I32, I32]),
     "tw_decode_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P, SZ, P]),
+    "tw_attend_union": (I32, [P, P, I64, I32, I32, I64, P, I64, P, P, P, P, I32, I32, I32, I32, FLT,
+                              P, I32, P, P, P, SZ, P]),
+    "tw_twilight_decode_layer": (I32, [ctypes.POINTER(DecodeLayerArgs), P]),
+    "tw_decode_layer_args_size": (SZ, []),
     "tw_decode_attention_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P]),
 }
 

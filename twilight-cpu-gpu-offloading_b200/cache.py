@@ -14,9 +14,9 @@ return as Python ints; attend_layer needs none.
 
 from __future__ import annotations
 
+import ctypes
 import hashlib
 import math
-import time
 from collections import defaultdict
 from typing import Any, Optional
 
@@ -797,18 +797,116 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
 
     def attend_layer(self, *, key_states, value_states, queries, entries,
                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Fused extension of the GQA group step: gather + sparse GQA decode attention
-        + append, with no host synchronisation.  Returns the attention output
-        [G, R, D] in the K/V dtype (what hi/mp.py:258-279 feeds to o_proj)."""
+        """Fused extension of the GQA group step: the split-K attention reads each
+        group's union rows straight from the mapped host slab (no staged copy),
+        then the new token is appended; no host synchronisation.  Returns the
+        attention output [G, R, D] in the K/V dtype (what hi/mp.py:258-279 feeds
+        to o_proj)."""
         old_length, k_new, v_new = self._begin_group_step(key_states, value_states, queries, entries)
         first, G = entries[0], len(entries)
-        bufs, out_k, out_v, cu = self._gather_union(first, G, old_length, k_new, v_new)
+        bufs = self._buffers(first, G)
         q = torch.stack([query[0, :, 0] for query in queries], dim=0).to(self.dtype).contiguous()
         start = self._phase_start()
-        out = ops.decode_attention(q, out_k, out_v, cu, min(bufs["per_group_cap"], old_length + 1),
-                                   workspace=bufs["attn_workspace"], out=out)
+        out = ops.attend_union(self._slab, first, old_length, bufs["union_pos"], bufs["union_count"],
+                               k_new, v_new, q, min(bufs["per_group_cap"], old_length + 1),
+                               workspace=bufs["attn_workspace"], error_flag=self._error_flag, out=out)
         self._phase_end("attention", start)
         self._append_rows(first, G, old_length, k_new, v_new)
+        return out
+
+    def decode_layer(self, *, queries, key_states, value_states, entries,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One whole layer-step in one library call (tw_twilight_decode_layer):
+        selection, fused union gather + attention and the new-token append, no
+        host synchronisation.  Equivalent to prepare_layer_selection followed by
+        attend_layer.  queries may be the reference's list of [1, R, 1, D]
+        tensors or one [G, R, D] tensor; key_states / value_states lists of
+        [1, 1, 1, D] or [G, D] tensors."""
+        G = len(entries)
+        R = self.num_query_heads_per_kv
+        first = _contiguous_entries(entries)
+        if isinstance(queries, torch.Tensor):
+            q = queries
+            if tuple(q.shape) != (G, R, HEAD_DIM):
+                raise ValueError("queries must be [G, R, D]")
+        else:
+            self._validate_layer(entries, queries)
+            q = torch.stack([query[0, :, 0] for query in queries], dim=0)
+        k_new = key_states if isinstance(key_states, torch.Tensor) else torch.cat(
+            [k.reshape(1, HEAD_DIM) for k in key_states], dim=0)
+        v_new = value_states if isinstance(value_states, torch.Tensor) else torch.cat(
+            [v.reshape(1, HEAD_DIM) for v in value_states], dim=0)
+        if tuple(k_new.shape) != (G, HEAD_DIM) or k_new.shape != v_new.shape:
+            raise ValueError("new K/V must be [G, D]")
+        for t in (q, k_new, v_new):
+            if t.dtype != self.dtype or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("queries and new K/V must be contiguous CUDA tensors of the K/V dtype")
+        old_length = self._layer_old_length(entries)
+        if self._prompt_length is None:
+            raise RuntimeError("Twilight prompt metadata is missing")
+        w = self._window(old_length)
+        candidate_pages = min(w["candidate_pages"], self._metadata_pages(entries, old_length))
+        b0_pages = min(candidate_pages, max(1, math.ceil(self.candidate_token_budget / self.block_size)),
+                       self.b0_page_capacity)
+        if candidate_pages == 0 or b0_pages == 0 or self._tracing():
+            # protected-only windows and traced runs take the two-call path
+            self.prepare_layer_selection(entries=entries, queries=[q[g].view(1, R, 1, HEAD_DIM) for g in range(G)])
+            return self.attend_layer(key_states=[k_new[g].view(1, 1, 1, HEAD_DIM) for g in range(G)],
+                                     value_states=[v_new[g].view(1, 1, 1, HEAD_DIM) for g in range(G)],
+                                     queries=[q[g].view(1, R, 1, HEAD_DIM) for g in range(G)],
+                                     entries=entries, out=out)
+        bufs = self._buffers(first, G)
+        if out is None:
+            out = torch.empty((G, R, HEAD_DIM), dtype=self.dtype, device=self.device)
+        args = bufs.get("layer_args")
+        if args is None:
+            args = _lib.DecodeLayerArgs()
+            args.slab_k = self._slab.key_device_ptr
+            args.slab_v = self._slab.value_device_ptr
+            args.max_len = self.geometry.max_cache_len
+            args.groups = G
+            args.heads_per_group = R
+            args.dtype = ops._kv_code(self.dtype)
+            args.page_min = self._page_min.data_ptr()
+            args.page_max = self._page_max.data_ptr()
+            args.page_capacity = self.page_capacity
+            args.packed = self._packed.data_ptr()
+            args.scale = self._scale.data_ptr()
+            args.minimum = self._minimum.data_ptr()
+            args.int4_group_size = self.int4_group_size
+            args.sink = self.sink_tokens
+            args.block_size = self.block_size
+            args.top_p = self.top_p
+            args.append = 1
+            args.pages = bufs["pages"].data_ptr()
+            args.union_pos = bufs["union_pos"].data_ptr()
+            args.pos_stride = self.geometry.max_cache_len
+            args.union_count = bufs["union_count"].data_ptr()
+            args.head_count = bufs["head_count"].data_ptr()
+            args.head_pos = None
+            args.error_flag = self._error_flag.data_ptr()
+            args.select_workspace = bufs["workspace"].data_ptr()
+            args.select_workspace_bytes = bufs["workspace"].numel()
+            args.attn_workspace = bufs["attn_workspace"].data_ptr()
+            args.attn_workspace_bytes = bufs["attn_workspace"].numel()
+            bufs["layer_args"] = args
+        args.first_entry = first
+        args.n_pages = candidate_pages
+        args.b0_pages = b0_pages
+        args.old_length = old_length
+        args.sink_end = w["sink_end"]
+        args.recent_start = w["recent_start"]
+        args.q = q.data_ptr()
+        args.k_new = k_new.data_ptr()
+        args.v_new = v_new.data_ptr()
+        args.out = out.data_ptr()
+        args.out_dtype = ops.DTYPE_CODES[out.dtype]
+        args.max_rows_per_group = min(bufs["per_group_cap"], old_length + 1)
+        start = self._phase_start()
+        _lib.check(_lib.load().tw_twilight_decode_layer(ctypes.byref(args), self._stream()),
+                   "twilight_decode_layer")
+        self._phase_end("decode_layer", start)
+        self._advance_layer(entries)
         return out
 
     # ------------------------------------------------------------- hashes ----

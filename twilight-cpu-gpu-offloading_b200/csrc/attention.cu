@@ -14,9 +14,9 @@
 
 namespace tw {
 
-constexpr int kAttnThreads = 128;   // 4 warps
-constexpr int kAttnChunk = 128;     // rows per split CTA
-constexpr int kAttnUnroll = 4;      // rows per warp iteration
+constexpr int kAttnThreads = 256;   // 8 warps
+constexpr int kAttnChunk = 128;     // rows per split CTA (16 per warp)
+constexpr int kVecPerRow = 16;      // 16-byte vectors per 128-dim fp16/bf16 row
 
 struct AttnWorkspace {
   unsigned int* counters;  // [S]
@@ -31,214 +31,316 @@ inline int attn_max_splits(int max_seqlen_k) {
 }
 
 inline size_t attn_ws_bytes(int S, int R, int max_splits, AttnWorkspace* ws, char* base) {
-  size_t off = 0;
   const size_t c_bytes = align256((size_t)S * sizeof(unsigned int));
   const size_t ml_bytes = align256((size_t)S * max_splits * R * 2 * sizeof(float));
   const size_t o_bytes = align256((size_t)S * max_splits * R * kHeadDim * sizeof(float));
   if (ws) {
-    ws->counters = reinterpret_cast<unsigned int*>(base + off);
-    ws->part_ml = reinterpret_cast<float*>(base + off + c_bytes);
-    ws->part_o = reinterpret_cast<float*>(base + off + c_bytes + ml_bytes);
+    ws->counters = reinterpret_cast<unsigned int*>(base);
+    ws->part_ml = reinterpret_cast<float*>(base + c_bytes);
+    ws->part_o = reinterpret_cast<float*>(base + c_bytes + ml_bytes);
   }
   return c_bytes + ml_bytes + o_bytes;
 }
 
-template <typename T> struct Vec4Of;
-template <> struct Vec4Of<__half> {
-  __device__ static void load(const __half* p, float (&f)[4]) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(p);
-    const __half2 a = *reinterpret_cast<const __half2*>(&raw.x);
-    const __half2 b = *reinterpret_cast<const __half2*>(&raw.y);
-    const float2 fa = __half22float2(a), fb = __half22float2(b);
-    f[0] = fa.x; f[1] = fa.y; f[2] = fb.x; f[3] = fb.y;
+template <typename T> __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]);
+template <> __device__ __forceinline__ void unpack8<__half>(const uint4& u, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
   }
-};
-template <> struct Vec4Of<__nv_bfloat16> {
-  __device__ static void load(const __nv_bfloat16* p, float (&f)[4]) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(p);
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
-    f[0] = fa.x; f[1] = fa.y; f[2] = fb.x; f[3] = fb.y;
-  }
-};
-
-template <typename OutT>
-__device__ __forceinline__ void store_out(OutT* p, float v) { *p = from_f32<OutT>(v); }
-
-// Finalise one (segment, head) from merged (m, l, o[d]) held per thread d.
-template <typename OutT>
-__device__ __forceinline__ void write_final(OutT* out, float* lse, int s, int r, int R, float m,
-                                            float l, float o) {
-  const int d = threadIdx.x;
-  const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
-  store_out(out + ((int64_t)s * R + r) * kHeadDim + d, o * inv);
-  if (lse && d == 0) {
-    lse[(int64_t)s * R + r] = (l > 0.0f) ? (m + log2f(l)) * CUDART_LN2_F : -CUDART_INF_F;
+}
+template <> __device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
   }
 }
 
-template <typename T, int R, typename OutT>
+// Rows already gathered into device memory: segment s = rows [cu[s], cu[s+1]).
+struct FlatRows {
+  const uint4* k;
+  const uint4* v;
+  const int32_t* cu;
+  __device__ __forceinline__ int length(int s) const { return cu[s + 1] - cu[s]; }
+  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp) const {
+    const int64_t r = (int64_t)cu[s] + i;
+    kp = k + r * kVecPerRow;
+    vp = v + r * kVecPerRow;
+    return true;
+  }
+};
+
+// Rows read in place from the (mapped host) slab: segment g = the group's sorted
+// union positions, then its current token.
+struct UnionRows {
+  const uint4* slab_k;
+  const uint4* slab_v;
+  int64_t max_len;
+  int first_entry;
+  int64_t old_length;
+  const int32_t* union_pos;
+  int64_t pos_stride;
+  const int32_t* union_count;
+  const uint4* cur_k;
+  const uint4* cur_v;
+  int32_t* error_flag;
+  __device__ __forceinline__ int length(int s) const { return union_count[s] + 1; }
+  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp) const {
+    if (i >= union_count[s]) {
+      kp = cur_k + (int64_t)s * kVecPerRow;
+      vp = cur_v + (int64_t)s * kVecPerRow;
+      return true;
+    }
+    const int64_t pos = union_pos[(int64_t)s * pos_stride + i];
+    if (pos < 0 || pos >= old_length) {
+      if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
+      return false;
+    }
+    const int64_t r = (int64_t)(first_entry + s) * max_len + pos;
+    kp = slab_k + r * kVecPerRow;
+    vp = slab_v + r * kVecPerRow;
+    return true;
+  }
+};
+
+template <typename OutT>
+__device__ __forceinline__ void write_final(OutT* out, float* lse, int s, int r, int R, int d,
+                                            float m, float l, float o) {
+  const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
+  out[((int64_t)s * R + r) * kHeadDim + d] = from_f32<OutT>(o * inv);
+  if (lse && d == 0)
+    lse[(int64_t)s * R + r] = (l > 0.0f) ? (m + log2f(l)) * CUDART_LN2_F : -CUDART_INF_F;
+}
+
+__device__ __forceinline__ float weight(float m, float M) {
+  return (m == -CUDART_INF_F) ? 0.0f : exp2f(m - M);
+}
+
+// One split CTA: 8 warps x 16 rows.  A half-warp owns a row per step (16 lanes
+// x 8 channels, one 16-byte load each of K and V); every lane keeps its 8
+// channels of q and of the output accumulator for all R heads.  Scores of a
+// block of rows are computed first (4-step shuffle reduction inside the
+// half-warp), then one online-softmax update per block.  The 8 warps are
+// combined in shared memory; with several splits the last split CTA of the
+// segment merges all partials in parallel (threads over (head, channel)).
+template <typename T, int R, typename OutT, typename Rows>
 __global__ void __launch_bounds__(kAttnThreads)
-decode_attention_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                        const int32_t* __restrict__ cu, float scale_log2, int max_splits,
-                        AttnWorkspace ws, OutT* __restrict__ out, float* __restrict__ lse) {
-  __shared__ float s_m[4][R];
-  __shared__ float s_l[4][R];
-  __shared__ float s_o[4][R][kHeadDim];
+attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_splits,
+                 AttnWorkspace ws, OutT* __restrict__ out, float* __restrict__ lse) {
+  constexpr int kWarps = kAttnThreads / 32;
+  constexpr int kRowsPerWarp = kAttnChunk / kWarps;
+  constexpr int kRowsPerHalf = (R <= 4) ? 8 : 4;
+  constexpr int kIters = kRowsPerWarp / (2 * kRowsPerHalf);
+  __shared__ float s_m[kWarps][R];
+  __shared__ float s_l[kWarps][R];
+  __shared__ float s_o[kWarps][R][kHeadDim];
+  __shared__ float s_M[R], s_L[R];
   __shared__ bool s_last;
 
   const int s = blockIdx.y;
   const int split = blockIdx.x;
-  const int seg_begin = cu[s];
   // Rows beyond max_splits * kAttnChunk (a caller's max_seqlen_k below the real
   // segment length) are not read: the split count is clamped to the grid.
-  const int seg_len = min(cu[s + 1] - seg_begin, max_splits * kAttnChunk);
+  const int seg_len = min(rows.length(s), max_splits * kAttnChunk);
   const int nsplit = (seg_len + kAttnChunk - 1) / kAttnChunk;
   if (split >= max(nsplit, 1)) return;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int row_begin = seg_begin + split * kAttnChunk;
-  const int row_end = min(seg_begin + seg_len, row_begin + kAttnChunk);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int half = lane >> 4;
+  const int l16 = lane & 15;
 
-  float qf[R][4];
+  float qf[R][8];
 #pragma unroll
-  for (int r = 0; r < R; ++r) Vec4Of<T>::load(q + ((int64_t)s * R + r) * kHeadDim + 4 * lane, qf[r]);
+  for (int r = 0; r < R; ++r)
+    unpack8<T>(reinterpret_cast<const uint4*>(q + ((int64_t)s * R + r) * kHeadDim)[l16], qf[r]);
 
-  float m[R], l[R], acc[R][4];
+  float m[R], l[R], acc[R][8];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     m[r] = -CUDART_INF_F;
     l[r] = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+    for (int c = 0; c < 8; ++c) acc[r][c] = 0.0f;
   }
 
-  for (int base = row_begin + warp; base < row_end; base += 4 * kAttnUnroll) {
-    float kf[kAttnUnroll][4], vf[kAttnUnroll][4];
+  const int warp_row0 = split * kAttnChunk + warp * kRowsPerWarp;
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const int row = base + 4 * u;
-      if (row < row_end) {
-        Vec4Of<T>::load(k + (int64_t)row * kHeadDim + 4 * lane, kf[u]);
-        Vec4Of<T>::load(v + (int64_t)row * kHeadDim + 4 * lane, vf[u]);
+  for (int it = 0; it < kIters; ++it) {
+    uint4 kr[kRowsPerHalf], vr[kRowsPerHalf];
+    bool ok[kRowsPerHalf];
+#pragma unroll
+    for (int j = 0; j < kRowsPerHalf; ++j) {
+      const int i = warp_row0 + it * 2 * kRowsPerHalf + 2 * j + half;
+      ok[j] = false;
+      kr[j] = make_uint4(0, 0, 0, 0);
+      vr[j] = kr[j];
+      const uint4 *kp, *vp;
+      if (i < seg_len && rows.locate(s, i, kp, vp)) {
+        kr[j] = __ldcs(kp + l16);
+        vr[j] = __ldcs(vp + l16);
+        ok[j] = true;
       }
     }
+    float sc[kRowsPerHalf][R];
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const int row = base + 4 * u;
-      if (row >= row_end) break;  // warp-uniform
+    for (int j = 0; j < kRowsPerHalf; ++j) {
+      float kf[8];
+      unpack8<T>(kr[j], kf);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float dot = qf[r][0] * kf[u][0] + qf[r][1] * kf[u][1] + qf[r][2] * kf[u][2] +
-                    qf[r][3] * kf[u][3];
+        float p = 0.0f;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-        const float sc = dot * scale_log2;
-        const float m_new = fmaxf(m[r], sc);
-        const float corr = exp2f(m[r] - m_new);
-        const float p = exp2f(sc - m_new);
-        l[r] = l[r] * corr + p;
+        for (int c = 0; c < 8; ++c) p = fmaf(qf[r][c], kf[c], p);
+        p += __shfl_xor_sync(0xffffffffu, p, 8);
+        p += __shfl_xor_sync(0xffffffffu, p, 4);
+        p += __shfl_xor_sync(0xffffffffu, p, 2);
+        p += __shfl_xor_sync(0xffffffffu, p, 1);
+        sc[j][r] = ok[j] ? p * scale_log2 : -CUDART_INF_F;
+      }
+    }
+    float mb[R];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[r][c] = acc[r][c] * corr + p * vf[u][c];
-        m[r] = m_new;
+    for (int r = 0; r < R; ++r) {
+      float x = m[r];
+#pragma unroll
+      for (int j = 0; j < kRowsPerHalf; ++j) x = fmaxf(x, sc[j][r]);
+      mb[r] = x;
+      const float corr = (x == -CUDART_INF_F) ? 1.0f : exp2f(m[r] - x);
+      l[r] *= corr;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[r][c] *= corr;
+      m[r] = x;
+    }
+#pragma unroll
+    for (int j = 0; j < kRowsPerHalf; ++j) {
+      float vf[8];
+      unpack8<T>(vr[j], vf);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float p = (mb[r] == -CUDART_INF_F) ? 0.0f : exp2f(sc[j][r] - mb[r]);
+        l[r] += p;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[r][c] = fmaf(p, vf[c], acc[r][c]);
       }
     }
   }
 
-  // Merge the 4 warps of this CTA.
+  // Combine the two half-warps (they hold disjoint rows, same channels).
 #pragma unroll
   for (int r = 0; r < R; ++r) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m[r], 16);
+    const float lo = __shfl_xor_sync(0xffffffffu, l[r], 16);
+    const float M = fmaxf(m[r], mo);
+    const float wa = weight(m[r], M), wb = weight(mo, M);
+    l[r] = l[r] * wa + lo * wb;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float ao = __shfl_xor_sync(0xffffffffu, acc[r][c], 16);
+      acc[r][c] = acc[r][c] * wa + ao * wb;
+    }
+    m[r] = M;
     if (lane == 0) {
       s_m[warp][r] = m[r];
       s_l[warp][r] = l[r];
     }
+    if (half == 0) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) s_o[warp][r][4 * lane + c] = acc[r][c];
+      for (int c = 0; c < 8; ++c) s_o[warp][r][8 * l16 + c] = acc[r][c];
+    }
   }
   __syncthreads();
-  const int d = threadIdx.x;  // 128 threads == kHeadDim
-  float cm[R], cl[R], co[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float mm = -CUDART_INF_F;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, s_m[w][r]);
-    float ll = 0.0f, oo = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float wm = s_m[w][r];
-      const float f = (wm == -CUDART_INF_F) ? 0.0f : exp2f(wm - mm);
-      ll += s_l[w][r] * f;
-      oo += s_o[w][r][d] * f;
-    }
-    cm[r] = mm;
-    cl[r] = ll;
-    co[r] = oo;
-  }
 
-  if (nsplit <= 1) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) write_final<OutT>(out, lse, s, r, R, cm[r], cl[r], co[r]);
-    return;
-  }
-
-  // Publish this split's partial, then the last split of the segment merges.
+  // Combine the warps; write the output (one split) or this split's partial.
   float* pml = ws.part_ml + ((int64_t)s * max_splits + split) * R * 2;
   float* po = ws.part_o + ((int64_t)s * max_splits + split) * R * kHeadDim;
+  for (int idx = tid; idx < R * kHeadDim; idx += kAttnThreads) {
+    const int r = idx / kHeadDim;
+    const int d = idx % kHeadDim;
+    float M = -CUDART_INF_F;
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    po[r * kHeadDim + d] = co[r];
-    if (d == 0) {
-      pml[2 * r] = cm[r];
-      pml[2 * r + 1] = cl[r];
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, s_m[w][r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = weight(s_m[w][r], M);
+      L += s_l[w][r] * f;
+      O += s_o[w][r][d] * f;
+    }
+    if (nsplit <= 1) {
+      write_final<OutT>(out, lse, s, r, R, d, M, L, O);
+    } else {
+      po[r * kHeadDim + d] = O;
+      if (d == 0) {
+        pml[2 * r] = M;
+        pml[2 * r + 1] = L;
+      }
     }
   }
+  if (nsplit <= 1) return;
+
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     const unsigned int prev = atomicAdd(&ws.counters[s], 1u);
     s_last = (prev == (unsigned int)nsplit - 1u);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-#pragma unroll 1
-  for (int r = 0; r < R; ++r) {
-    float mm = -CUDART_INF_F;
-    for (int j = 0; j < nsplit; ++j)
-      mm = fmaxf(mm, __ldcg(ws.part_ml + (((int64_t)s * max_splits + j) * R + r) * 2));
-    float ll = 0.0f, oo = 0.0f;
-    for (int j = 0; j < nsplit; ++j) {
-      const float* ml = ws.part_ml + (((int64_t)s * max_splits + j) * R + r) * 2;
-      const float wm = __ldcg(ml);
-      const float f = (wm == -CUDART_INF_F) ? 0.0f : exp2f(wm - mm);
-      ll += __ldcg(ml + 1) * f;
-      oo += __ldcg(ws.part_o + (((int64_t)s * max_splits + j) * R + r) * kHeadDim + d) * f;
+
+  // Last split: per-head max and normaliser (warp per head), then the
+  // weighted sum of the partial outputs (threads over (head, channel)).
+  const float* ml = ws.part_ml + (int64_t)s * max_splits * R * 2;
+  const float* po_all = ws.part_o + (int64_t)s * max_splits * R * kHeadDim;
+  for (int r = warp; r < R; r += kWarps) {
+    float M = -CUDART_INF_F;
+    for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(ml + ((int64_t)j * R + r) * 2));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.0f;
+    for (int j = lane; j < nsplit; j += 32) {
+      const float* e = ml + ((int64_t)j * R + r) * 2;
+      L += __ldcg(e + 1) * weight(__ldcg(e), M);
     }
-    write_final<OutT>(out, lse, s, r, R, mm, ll, oo);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (lane == 0) {
+      s_M[r] = M;
+      s_L[r] = L;
+    }
   }
-  if (threadIdx.x == 0) ws.counters[s] = 0u;
+  __syncthreads();
+  for (int idx = tid; idx < R * kHeadDim; idx += kAttnThreads) {
+    const int r = idx / kHeadDim;
+    const int d = idx % kHeadDim;
+    const float M = s_M[r];
+    float O = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < nsplit; ++j) {
+      const float f = weight(__ldcg(ml + ((int64_t)j * R + r) * 2), M);
+      O += f * __ldcg(po_all + ((int64_t)j * R + r) * kHeadDim + d);
+    }
+    write_final<OutT>(out, lse, s, r, R, d, M, s_L[r], O);
+  }
+  if (tid == 0) ws.counters[s] = 0u;
 }
 
-template <typename T, int R, typename OutT>
-int launch_attention_r(const void* q, const void* k, const void* v, const int32_t* cu, int S,
-                       int max_splits, float scale_log2, const AttnWorkspace& ws, void* out,
-                       float* lse, cudaStream_t stream) {
+template <typename T, typename OutT, typename Rows>
+int launch_rows(const Rows& rows, const void* q, int S, int R, int max_splits, float scale_log2,
+                const AttnWorkspace& ws, void* out, float* lse, cudaStream_t stream) {
   dim3 grid(max_splits, S);
-  decode_attention_kernel<T, R, OutT><<<grid, kAttnThreads, 0, stream>>>(
-      (const T*)q, (const T*)k, (const T*)v, cu, scale_log2, max_splits, ws, (OutT*)out, lse);
-  return check_launch();
-}
-
-template <typename T, typename OutT>
-int launch_attention(const void* q, const void* k, const void* v, const int32_t* cu, int S, int R,
-                     int max_splits, float scale_log2, const AttnWorkspace& ws, void* out,
-                     float* lse, cudaStream_t stream) {
-#define TW_ATTN_CASE(RR)                                                                     \
-  case RR:                                                                                   \
-    return launch_attention_r<T, RR, OutT>(q, k, v, cu, S, max_splits, scale_log2, ws, out, \
-                                           lse, stream);
+#define TW_ATTN_CASE(RR)                                                                    \
+  case RR:                                                                                  \
+    attention_kernel<T, RR, OutT, Rows><<<grid, kAttnThreads, 0, stream>>>(                 \
+        rows, (const T*)q, scale_log2, max_splits, ws, (OutT*)out, lse);                    \
+    return check_launch();
   switch (R) {
     TW_ATTN_CASE(1)
     TW_ATTN_CASE(2)
@@ -252,6 +354,14 @@ int launch_attention(const void* q, const void* k, const void* v, const int32_t*
       return TW_ERR_UNSUPPORTED;
   }
 #undef TW_ATTN_CASE
+}
+
+template <typename T, typename OutT>
+int launch_attention(const void* q, const void* k, const void* v, const int32_t* cu, int S, int R,
+                     int max_splits, float scale_log2, const AttnWorkspace& ws, void* out,
+                     float* lse, cudaStream_t stream) {
+  FlatRows rows{(const uint4*)k, (const uint4*)v, cu};
+  return launch_rows<T, OutT>(rows, q, S, R, max_splits, scale_log2, ws, out, lse, stream);
 }
 
 }  // namespace tw
@@ -302,6 +412,50 @@ extern "C" int tw_decode_attention(const void* q, const void* k, const void* v,
                                                           scale_log2, ws, out, lse, st);
   }
   return TW_ERR_UNSUPPORTED;
+}
+
+extern "C" int tw_attend_union(const void* slab_k, const void* slab_v, int64_t max_len,
+                               int first_entry, int groups, int64_t old_length,
+                               const int32_t* union_pos, int64_t pos_stride,
+                               const int32_t* union_count, const void* cur_k, const void* cur_v,
+                               const void* q, int heads_per_group, int max_rows_per_group,
+                               int head_dim, int dtype, float softmax_scale, void* out,
+                               int out_dtype, float* lse, int32_t* error_flag, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
+  if (!slab_k || !slab_v || !union_pos || !union_count || !cur_k || !cur_v || !q || !out ||
+      groups <= 0 || groups > 65535 || heads_per_group <= 0 || first_entry < 0 ||
+      old_length < 0 || old_length > max_len || pos_stride < old_length ||
+      max_rows_per_group < 1 || !(softmax_scale > 0.0f))
+    return TW_ERR_BAD_ARG;
+  if (heads_per_group > kMaxHeadsPerGroup) return TW_ERR_UNSUPPORTED;
+  if (dtype != TW_F16 && dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
+  if (out_dtype != dtype && out_dtype != TW_F32) return TW_ERR_BAD_ARG;
+  if ((((uintptr_t)slab_k | (uintptr_t)slab_v | (uintptr_t)cur_k | (uintptr_t)cur_v |
+        (uintptr_t)q) & 15) != 0)
+    return TW_ERR_BAD_ARG;
+  const int max_splits = attn_max_splits(max_rows_per_group);
+  AttnWorkspace ws{};
+  const size_t need = attn_ws_bytes(groups, heads_per_group, max_splits, &ws,
+                                    reinterpret_cast<char*>(workspace));
+  if (max_splits > 1 && (!workspace || workspace_bytes < need)) return TW_ERR_CAPACITY;
+  UnionRows rows{(const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, old_length,
+                 union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
+                 error_flag};
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == TW_F16) {
+    if (out_dtype == TW_F32)
+      return launch_rows<__half, float>(rows, q, groups, heads_per_group, max_splits, scale_log2,
+                                        ws, out, lse, st);
+    return launch_rows<__half, __half>(rows, q, groups, heads_per_group, max_splits, scale_log2,
+                                       ws, out, lse, st);
+  }
+  if (out_dtype == TW_F32)
+    return launch_rows<__nv_bfloat16, float>(rows, q, groups, heads_per_group, max_splits,
+                                             scale_log2, ws, out, lse, st);
+  return launch_rows<__nv_bfloat16, __nv_bfloat16>(rows, q, groups, heads_per_group, max_splits,
+                                                   scale_log2, ws, out, lse, st);
 }
 
 // ---- allocation-free variant ----------------------------------------------------

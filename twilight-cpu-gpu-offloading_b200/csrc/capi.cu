@@ -24,6 +24,24 @@ extern "C" int tw_top_p_union(const float*, const int32_t*, int, int, int, int, 
                               int64_t, int64_t, int64_t, int32_t*, int64_t, int32_t*, int32_t*,
                               int32_t*, int32_t*, void*);
 
+namespace tw {
+int quest_score_dispatch(const void* q, int q_dtype, const void* pmin, const void* pmax, int groups,
+                         int R, int n_pages, int64_t stride, int dtype, float* scores,
+                         cudaStream_t stream);
+}  // namespace tw
+int launch_int4_qk(const void* q, int q_dtype, const uint8_t* packed, const void* scale,
+                   const void* minimum, int64_t entry_stride_tokens, const int32_t* pages,
+                   int groups, int R, int b0_pages, int block_size, int sink, int group_size,
+                   int dtype, float* logits, cudaStream_t stream);
+
+extern "C" int tw_attend_union(const void*, const void*, int64_t, int, int, int64_t, const int32_t*,
+                               int64_t, const int32_t*, const void*, const void*, const void*, int,
+                               int, int, int, float, void*, int, float*, int32_t*, void*, size_t,
+                               void*);
+extern "C" int tw_append_token(void*, void*, int64_t, int, int, int64_t, const void*, const void*,
+                               int, int, int, int, void*, void*, int64_t, uint8_t*, void*, void*,
+                               int, void*);
+
 extern "C" const char* tw_status_string(int status) {
   switch (status) {
     case TW_OK: return "ok";
@@ -125,4 +143,55 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
   return tw_top_p_union(logits, pages_out, groups, heads_per_group, b0_pages, block_size, sink,
                         top_p, old_length, sink_end, recent_start, union_pos, pos_stride,
                         union_count, head_count, head_pos, error_flag, stream);
+}
+
+extern "C" size_t tw_decode_layer_args_size(void) { return sizeof(tw_decode_layer_args); }
+
+extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* stream) {
+  if (!a) return TW_ERR_BAD_ARG;
+  if (a->dtype != TW_F16 && a->dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
+  if (a->b0_pages <= 0 || a->b0_pages > a->n_pages || a->groups <= 0 || a->first_entry < 0 ||
+      !a->q || !a->k_new || !a->v_new || !a->out || !a->pages)
+    return TW_ERR_BAD_ARG;
+  const int G = a->groups, R = a->heads_per_group;
+  const size_t need = tw_select_layer_workspace_size(G, R, a->n_pages, a->b0_pages, a->block_size);
+  if (need == 0) return TW_ERR_BAD_ARG;
+  if (!a->select_workspace || a->select_workspace_bytes < need) return TW_ERR_CAPACITY;
+  if (a->int4_group_size != 32 && a->int4_group_size != 64 && a->int4_group_size != 128)
+    return TW_ERR_UNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t elem = 2;  // fp16 / bf16
+  const int ngroups = kHeadDim / a->int4_group_size;
+  const int64_t e0 = a->first_entry;
+  const char* pmin = (const char*)a->page_min + e0 * a->page_capacity * kHeadDim * elem;
+  const char* pmax = (const char*)a->page_max + e0 * a->page_capacity * kHeadDim * elem;
+  const uint8_t* packed = a->packed + e0 * a->max_len * (kHeadDim / 2);
+  const char* scale = (const char*)a->scale + e0 * a->max_len * ngroups * elem;
+  const char* minimum = (const char*)a->minimum + e0 * a->max_len * ngroups * elem;
+  const size_t rows = (size_t)G * R;
+  float* scores = reinterpret_cast<float*>(a->select_workspace);
+  float* logits = reinterpret_cast<float*>(reinterpret_cast<char*>(a->select_workspace) +
+                                           align256(rows * (size_t)a->n_pages * sizeof(float)));
+  int rc = quest_score_dispatch(a->q, a->dtype, pmin, pmax, G, R, a->n_pages,
+                                a->page_capacity * kHeadDim, a->dtype, scores, st);
+  if (rc != TW_OK) return rc;
+  rc = tw_topk_pages(scores, (int)rows, a->n_pages, a->b0_pages, a->pages, stream);
+  if (rc != TW_OK) return rc;
+  rc = launch_int4_qk(a->q, a->dtype, packed, scale, minimum, a->max_len, a->pages, G, R,
+                      a->b0_pages, a->block_size, a->sink, a->int4_group_size, a->dtype, logits, st);
+  if (rc != TW_OK) return rc;
+  rc = tw_top_p_union(logits, a->pages, G, R, a->b0_pages, a->block_size, a->sink, a->top_p,
+                      a->old_length, a->sink_end, a->recent_start, a->union_pos, a->pos_stride,
+                      a->union_count, a->head_count, a->head_pos, a->error_flag, stream);
+  if (rc != TW_OK) return rc;
+  rc = tw_attend_union(a->slab_k, a->slab_v, a->max_len, a->first_entry, G, a->old_length,
+                       a->union_pos, a->pos_stride, a->union_count, a->k_new, a->v_new, a->q, R,
+                       a->max_rows_per_group, kHeadDim, a->dtype,
+                       1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
+                       a->error_flag, a->attn_workspace, a->attn_workspace_bytes, stream);
+  if (rc != TW_OK || !a->append) return rc;
+  return tw_append_token(a->slab_k, a->slab_v, a->max_len, a->first_entry, G, a->old_length,
+                         a->k_new, a->v_new, kHeadDim, a->dtype, a->sink, a->block_size,
+                         a->page_min, a->page_max, a->page_capacity * kHeadDim, a->packed,
+                         a->scale, a->minimum, a->int4_group_size, stream);
 }

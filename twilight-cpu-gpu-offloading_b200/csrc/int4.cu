@@ -77,9 +77,9 @@ __global__ void int4_pack_kernel(const T* __restrict__ keys, int64_t key_entry_s
 // INT4 QK estimate.  4 lanes per candidate token, lane j covers channels
 // 32j .. 32j+31 (16 code bytes, one uint4 load).  Per channel k = code*s + m
 // (separately rounded), acc += k*q in channel order, then (a0+a1)+(a2+a3).
-template <typename T>
+template <typename T, typename QT>
 __global__ void __launch_bounds__(256)
-int4_qk_kernel(const float* __restrict__ q, const uint8_t* __restrict__ packed,
+int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
                const T* __restrict__ scale, const T* __restrict__ minimum,
                int64_t entry_stride, const int32_t* __restrict__ pages, int R, int b0,
                int block, int sink, int group_size, float inv_sqrt_d,
@@ -93,12 +93,9 @@ int4_qk_kernel(const float* __restrict__ q, const uint8_t* __restrict__ packed,
   const int tok = lane >> 2;
   const int n_cand = b0 * block;
   float qr[32];
-  const float* qrow = q + (int64_t)row * kHeadDim + 32 * sub;
+  const QT* qrow = q + (int64_t)row * kHeadDim + 32 * sub;
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 v = *reinterpret_cast<const float4*>(qrow + i);
-    qr[i] = v.x; qr[i + 1] = v.y; qr[i + 2] = v.z; qr[i + 3] = v.w;
-  }
+  for (int i = 0; i < 32; ++i) qr[i] = to_f32(qrow[i]);
   const int ngroups = kHeadDim / group_size;
   const int grp = (32 * sub) / group_size;
   const int32_t* prow = pages + (int64_t)row * b0;
@@ -247,19 +244,26 @@ float inv_sqrt_head_dim(int head_dim) {
   return 1.0f / d;
 }
 
-int launch_int4_qk(const float* q, const uint8_t* packed, const void* scale, const void* minimum,
-                   int64_t entry_stride_tokens, const int32_t* pages, int groups, int R,
-                   int b0_pages, int block_size, int sink, int group_size, int dtype,
-                   float* logits, cudaStream_t stream) {
+// q in fp32 (q_dtype TW_F32) or in the K dtype (converted exactly on load).
+int launch_int4_qk(const void* q, int q_dtype, const uint8_t* packed, const void* scale,
+                   const void* minimum, int64_t entry_stride_tokens, const int32_t* pages,
+                   int groups, int R, int b0_pages, int block_size, int sink, int group_size,
+                   int dtype, float* logits, cudaStream_t stream) {
   const int n_cand = b0_pages * block_size;
   constexpr int kThreads = 256;
   constexpr int kTokensPerCta = 256;
   dim3 grid((n_cand + kTokensPerCta - 1) / kTokensPerCta, groups * R);
   const float inv = inv_sqrt_head_dim(kHeadDim);
+  if (q_dtype != TW_F32 && q_dtype != dtype) return TW_ERR_BAD_ARG;
   TW_DISPATCH_KV_DTYPE(dtype, T, {
-    int4_qk_kernel<T><<<grid, kThreads, 0, stream>>>(
-        q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages, R, b0_pages,
-        block_size, sink, group_size, inv, logits, kTokensPerCta);
+    if (q_dtype == TW_F32)
+      int4_qk_kernel<T, float><<<grid, kThreads, 0, stream>>>(
+          (const float*)q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages,
+          R, b0_pages, block_size, sink, group_size, inv, logits, kTokensPerCta);
+    else
+      int4_qk_kernel<T, T><<<grid, kThreads, 0, stream>>>(
+          (const T*)q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages, R,
+          b0_pages, block_size, sink, group_size, inv, logits, kTokensPerCta);
     return check_launch();
   });
 }
@@ -275,7 +279,7 @@ extern "C" int tw_int4_qk(const float* q, const uint8_t* packed, const void* sca
       (int64_t)groups * heads_per_group > 65535)
     return TW_ERR_BAD_ARG;
   if (b0_pages == 0) return TW_OK;
-  return launch_int4_qk(q, packed, scale, minimum, entry_stride_tokens, pages, groups,
+  return launch_int4_qk(q, TW_F32, packed, scale, minimum, entry_stride_tokens, pages, groups,
                         heads_per_group, b0_pages, block_size, sink, group_size, dtype, logits,
                         (cudaStream_t)stream);
 }

@@ -35,8 +35,8 @@ __global__ void quest_page_meta_kernel(const T* __restrict__ keys, int64_t key_e
 // Warp per page, all R query heads of the group share each min/max load.
 // Lane l holds channels l, l+32, l+64, l+96; per head the products are added in
 // that order (mul and add separately rounded), then reduced by shfl-down 1..16.
-template <typename T, int R>
-__global__ void quest_score_kernel(const float* __restrict__ q, const T* __restrict__ pmin,
+template <typename T, int R, typename QT>
+__global__ void quest_score_kernel(const QT* __restrict__ q, const T* __restrict__ pmin,
                                    const T* __restrict__ pmax, int n_pages,
                                    int64_t meta_group_stride, float* __restrict__ scores) {
   const int g = blockIdx.y;
@@ -47,7 +47,7 @@ __global__ void quest_score_kernel(const float* __restrict__ q, const T* __restr
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) qr[r][c] = q[((int64_t)g * R + r) * kHeadDim + lane + 32 * c];
+    for (int c = 0; c < 4; ++c) qr[r][c] = to_f32(q[((int64_t)g * R + r) * kHeadDim + lane + 32 * c]);
 
   const T* gmin = pmin + g * meta_group_stride;
   const T* gmax = pmax + g * meta_group_stride;
@@ -126,6 +126,7 @@ topk_pages_kernel(const float* __restrict__ scores, int n, int k, int32_t* __res
       }
       const uint32_t above = suffix - sum;  // count in bins of higher lanes
       const uint32_t need = s_remaining;
+      __syncwarp();
       // the crossing lane: above < need <= suffix
       if (above < need && need <= suffix) {
         uint32_t acc = above;
@@ -183,32 +184,44 @@ int launch_quest_meta(const void* keys, int64_t key_entry_stride, int n_entries,
   return check_launch();
 }
 
-template <typename T, int R>
-int launch_quest_score_r(const float* q, const void* pmin, const void* pmax, int groups,
+template <typename T, int R, typename QT>
+int launch_quest_score_r(const void* q, const void* pmin, const void* pmax, int groups,
                          int n_pages, int64_t stride, float* scores, cudaStream_t stream) {
   constexpr int kThreads = 256;
   const int warps = kThreads / 32;
   int blocks_x = (n_pages + warps - 1) / warps;
   dim3 grid(blocks_x, groups);
-  quest_score_kernel<T, R><<<grid, kThreads, 0, stream>>>(q, (const T*)pmin, (const T*)pmax,
-                                                           n_pages, stride, scores);
+  quest_score_kernel<T, R, QT><<<grid, kThreads, 0, stream>>>(
+      (const QT*)q, (const T*)pmin, (const T*)pmax, n_pages, stride, scores);
   return check_launch();
 }
 
-template <typename T>
-int launch_quest_score(const float* q, const void* pmin, const void* pmax, int groups, int R,
+template <typename T, typename QT>
+int launch_quest_score(const void* q, const void* pmin, const void* pmax, int groups, int R,
                        int n_pages, int64_t stride, float* scores, cudaStream_t stream) {
+#define TW_QS_CASE(RR) \
+  case RR: return launch_quest_score_r<T, RR, QT>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
   switch (R) {
-    case 1: return launch_quest_score_r<T, 1>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 2: return launch_quest_score_r<T, 2>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 3: return launch_quest_score_r<T, 3>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 4: return launch_quest_score_r<T, 4>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 5: return launch_quest_score_r<T, 5>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 6: return launch_quest_score_r<T, 6>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 7: return launch_quest_score_r<T, 7>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
-    case 8: return launch_quest_score_r<T, 8>(q, pmin, pmax, groups, n_pages, stride, scores, stream);
+    TW_QS_CASE(1) TW_QS_CASE(2) TW_QS_CASE(3) TW_QS_CASE(4)
+    TW_QS_CASE(5) TW_QS_CASE(6) TW_QS_CASE(7) TW_QS_CASE(8)
     default: return TW_ERR_UNSUPPORTED;
   }
+#undef TW_QS_CASE
+}
+
+// q in fp32 (q_dtype TW_F32) or in the K dtype (converted exactly on load).
+int quest_score_dispatch(const void* q, int q_dtype, const void* pmin, const void* pmax, int groups,
+                         int R, int n_pages, int64_t stride, int dtype, float* scores,
+                         cudaStream_t stream) {
+  if (q_dtype == TW_F32) {
+    TW_DISPATCH_KV_DTYPE(dtype, T,
+                         return launch_quest_score<T, float>(q, pmin, pmax, groups, R, n_pages,
+                                                             stride, scores, stream));
+  }
+  if (q_dtype != dtype) return TW_ERR_BAD_ARG;
+  TW_DISPATCH_KV_DTYPE(dtype, T,
+                       return launch_quest_score<T, T>(q, pmin, pmax, groups, R, n_pages, stride,
+                                                       scores, stream));
 }
 
 constexpr int kTopkMaxN = 16384;
@@ -216,16 +229,12 @@ constexpr int kTopkMaxN = 16384;
 int launch_topk_pages(const float* scores, int rows, int n, int k, int32_t* out,
                       cudaStream_t stream) {
   const size_t smem = (size_t)n * sizeof(uint32_t);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t err = cudaFuncSetAttribute(topk_pages_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kTopkMaxN * (int)sizeof(uint32_t));
-    if (err != cudaSuccess) {
-      set_last_cuda_error(err);
-      return TW_ERR_CUDA;
-    }
-    configured = true;
+  cudaError_t err = cudaFuncSetAttribute(topk_pages_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kTopkMaxN * (int)sizeof(uint32_t));
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
   }
   topk_pages_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, n, k, out);
   return check_launch();
@@ -262,11 +271,8 @@ extern "C" int tw_quest_score(const float* q, const void* page_min, const void* 
     return TW_ERR_BAD_ARG;
   if (heads_per_group > kMaxHeadsPerGroup) return TW_ERR_UNSUPPORTED;
   if (n_pages == 0) return TW_OK;
-  TW_DISPATCH_KV_DTYPE(dtype, T,
-                       return launch_quest_score<T>(q, page_min, page_max, groups,
-                                                    heads_per_group, n_pages,
-                                                    meta_group_stride, scores,
-                                                    (cudaStream_t)stream));
+  return quest_score_dispatch(q, TW_F32, page_min, page_max, groups, heads_per_group, n_pages,
+                              meta_group_stride, dtype, scores, (cudaStream_t)stream);
 }
 
 extern "C" int tw_topk_pages(const float* scores, int rows, int n, int k, int32_t* out_pages,

@@ -7,14 +7,21 @@
 // (hi/twilight_offload_cache.py:1527-1549) and its sorted decode via
 // np.flatnonzero (:1602-1614).
 //
-// Top-p without a sort: softmax masses are fixed-point integers (e * 2^48), so
-// their sums are exact and order-free.  A 4-pass radix search over the
-// logits' order-preserving keys finds the key K* where the mass of the keys
-// above K* is < target <= mass of the keys >= K*; the count is the number of
-// keys above K* plus the fewest K*-ties (lowest candidate index first) that
-// reach the target.  Each CTA then ORs its selected positions into the
-// cluster leader's shared-memory bitmap over distributed shared memory; the
-// leader writes the sorted union by a popcount scan.
+// Softmax masses are fixed-point integers (e * 2^48, e = exp(l - max) by the
+// deterministic det_exp), so their sums are exact and order-free.  The count
+// is the fewest candidates, in descending logit order with ties taken in
+// candidate order, whose mass reaches ceil(p * total):
+//  * fast path: candidates are binned linearly in (max - logit) over 2048
+//    bins, an order-preserving partition (a higher logit never lands in a
+//    later bin); one scan of the exact per-bin masses finds the bin where the
+//    cumulative mass crosses the target, and the few candidates of that bin
+//    are ranked exactly (logit key, then candidate index) to finish the count;
+//  * fallback, when the crossing bin holds more than 256 candidates (e.g. many
+//    equal logits): a 4-pass radix search over the logits' order-preserving
+//    keys for the threshold key, then the fewest ties that reach the target.
+// Each CTA then ORs its selected positions, one 32-bit word per page, into
+// the cluster leader's shared-memory bitmap over distributed shared memory;
+// the leader writes the sorted union by a popcount scan.
 #include <cooperative_groups.h>
 
 #include "tw_common.cuh"
@@ -23,7 +30,7 @@ namespace cg = cooperative_groups;
 
 namespace tw {
 
-constexpr int kTopPThreads = 512;
+constexpr int kTopPThreads = 1024;
 
 struct TopPArgs {
   const float* logits;
@@ -44,23 +51,49 @@ struct TopPArgs {
   int32_t* error_flag;
 };
 
+// Bits of the 32 positions lo .. lo+31 that lie below x.
+__device__ __forceinline__ uint32_t bits_below(int64_t x, int64_t lo) {
+  if (x <= lo) return 0u;
+  if (x >= lo + 32) return 0xffffffffu;
+  return (1u << (uint32_t)(x - lo)) - 1u;
+}
+
 __device__ __forceinline__ int64_t cand_position(const int32_t* prow, int n, int block, int sink) {
   return (int64_t)sink + (int64_t)prow[n / block] * block + (n % block);
 }
 
-// Dynamic shared memory layout: keys[n] u32 | mass[n] u64 | bitmap[words] u32 (leader only).
+__host__ __device__ __forceinline__ size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// Dynamic shared memory: keys u32[n] | mass u64[n] | bitmap u32[words] | sel u8[n].
+__host__ __device__ __forceinline__ size_t top_p_head_bytes(int n) {
+  return align16((size_t)n * 4) + (size_t)n * 8;
+}
+
+__device__ __forceinline__ unsigned long long target_of(unsigned long long z, double top_p) {
+  const double t = ceil(__dmul_rn((double)z, top_p));
+  unsigned long long target = (t >= (double)z) ? z : (unsigned long long)t;
+  return target == 0ull ? 1ull : target;
+}
+
+constexpr int kTopPBins = 2048;
+constexpr int kTopPSmallBin = 256;
+
 __global__ void __launch_bounds__(kTopPThreads)
 top_p_union_kernel(TopPArgs a) {
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ unsigned long long bin_mass[kTopPBins];
+  __shared__ uint32_t bin_cnt[kTopPBins];
+  __shared__ unsigned long long list[kTopPSmallBin];
+  __shared__ unsigned long long ranked[kTopPSmallBin];
   __shared__ unsigned long long hist_mass[256];
   __shared__ uint32_t hist_cnt[256];
   __shared__ uint32_t scan_scratch[32];
-  __shared__ unsigned long long s_red[32];
-  __shared__ uint32_t s_prefix;
+  __shared__ unsigned long long scan64[32];
+  __shared__ unsigned long long stage[kTopPThreads / 32][32];
+  __shared__ uint32_t s_prefix, s_cnt_gt, s_kmax, s_kmin, s_list_n;
   __shared__ unsigned long long s_mass_gt, s_target;
-  __shared__ uint32_t s_cnt_gt;
-  __shared__ float s_max;
+  __shared__ int s_bstar, s_count;
 
   const int R = a.R;
   const int rank = (int)cluster.block_rank();  // query head within the group
@@ -76,191 +109,317 @@ top_p_union_kernel(TopPArgs a) {
   const int words = (int)((L + 31) >> 5);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);
   unsigned long long* mass =
-      reinterpret_cast<unsigned long long*>(smem_raw + (((size_t)n * 4 + 15) & ~(size_t)15));
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(mass) +
-                                                 (size_t)n * 8);
+      reinterpret_cast<unsigned long long*>(smem_raw + align16((size_t)n * 4));
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + top_p_head_bytes(n));
+  unsigned char* sel = reinterpret_cast<unsigned char*>(bitmap + words);
 
   // Leader: clear the bitmap and set the protected sink / recent ranges.
   if (rank == 0) {
+    const int64_t sink_hi = min(a.sink_end, L);
     for (int w = tid; w < words; w += blockDim.x) {
       const int64_t lo = (int64_t)w * 32;
-      uint32_t bits = 0u;
-      for (int b = 0; b < 32; ++b) {
-        const int64_t p = lo + b;
-        if (p < L && (p < a.sink_end || p >= a.recent_start)) bits |= 1u << b;
-      }
-      bitmap[w] = bits;
+      bitmap[w] = bits_below(sink_hi, lo) | (bits_below(L, lo) & ~bits_below(a.recent_start, lo));
     }
   }
+  for (int b = tid; b < kTopPBins; b += blockDim.x) {
+    bin_mass[b] = 0ull;
+    bin_cnt[b] = 0u;
+  }
+  if (tid == 0) {
+    s_kmax = 0u;
+    s_kmin = 0xffffffffu;
+    s_list_n = 0u;
+    s_bstar = -1;
+  }
+  __syncthreads();
 
   const float* lrow = a.logits + (int64_t)row * n;
   const int32_t* prow = a.pages + (int64_t)row * a.b0;
 
-  // 1. keys and the row maximum.
-  uint32_t kmax = 0u;
+  // 1. keys, row max and min.
+  uint32_t kmax = 0u, kmin = 0xffffffffu;
   for (int i = tid; i < n; i += blockDim.x) {
     const uint32_t k = float_key(lrow[i]);
     keys[i] = k;
     kmax = max(kmax, k);
+    kmin = min(kmin, k);
   }
-  for (int off = 16; off > 0; off >>= 1) kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
-  if (lane == 0) scan_scratch[warp] = kmax;
-  __syncthreads();
-  if (tid == 0) {
-    uint32_t m = 0u;
-    for (int w = 0; w < nwarps; ++w) m = max(m, scan_scratch[w]);
-    s_max = key_float(m);
+  for (int off = 16; off > 0; off >>= 1) {
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
+  }
+  if (lane == 0) {
+    atomicMax(&s_kmax, kmax);
+    atomicMin(&s_kmin, kmin);
   }
   __syncthreads();
-  const float lmax = s_max;
+  const float lmax = key_float(s_kmax);
+  const float span = __fsub_rn(lmax, key_float(s_kmin));
+  const float inv_w = span > 0.0f ? __fdiv_rn((float)kTopPBins, span) : 0.0f;
 
-  // 2. fixed-point masses and their exact total.
+  // 2. masses, their exact total and the binned mass histogram.
   unsigned long long part = 0ull;
   for (int i = tid; i < n; i += blockDim.x) {
     const float d = __fsub_rn(key_float(keys[i]), lmax);
     const unsigned long long m = mass_of(det_exp((double)d));
     mass[i] = m;
     part += m;
+    const int b = min(kTopPBins - 1, (int)__fmul_rn(-d, inv_w));
+    atomicAdd(&bin_mass[b], m);
+    atomicAdd(&bin_cnt[b], 1u);
   }
-  for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-  if (lane == 0) s_red[warp] = part;
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long z = 0ull;
-    for (int w = 0; w < nwarps; ++w) z += s_red[w];
-    double t = ceil(__dmul_rn((double)z, a.top_p));
-    unsigned long long target = (t >= (double)z) ? z : (unsigned long long)t;
-    if (target == 0ull) target = 1ull;
-    s_target = target;
-    s_mass_gt = 0ull;
-    s_cnt_gt = 0u;
-    s_prefix = 0u;
-  }
-  __syncthreads();
+  unsigned long long z;
+  block_exclusive_scan_u64(part, scan64, &z);
+  const unsigned long long target = target_of(z, a.top_p);
 
-  // 3. radix search for the threshold key by mass.
-  uint32_t mask = 0u;
-#pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int b = tid; b < 256; b += blockDim.x) {
-      hist_mass[b] = 0ull;
-      hist_cnt[b] = 0u;
+  // 3. crossing bin: bins in order (highest logits first), two per thread.
+  constexpr int kBinsPerThread = kTopPBins / kTopPThreads;
+  unsigned long long bm_local = 0ull;
+  uint32_t bc_local = 0u;
+#pragma unroll
+  for (int j = 0; j < kBinsPerThread; ++j) {
+    bm_local += bin_mass[kBinsPerThread * tid + j];
+    bc_local += bin_cnt[kBinsPerThread * tid + j];
+  }
+  unsigned long long mrun = block_exclusive_scan_u64(bm_local, scan64, &z);
+  uint32_t ctotal;
+  uint32_t crun = block_exclusive_scan(bc_local, scan_scratch, &ctotal);
+#pragma unroll
+  for (int j = 0; j < kBinsPerThread; ++j) {
+    const int b = kBinsPerThread * tid + j;
+    if (mrun < target && target <= mrun + bin_mass[b]) {
+      s_bstar = b;
+      s_mass_gt = mrun;
+      s_cnt_gt = crun;
+    }
+    mrun += bin_mass[b];
+    crun += bin_cnt[b];
+  }
+  __syncthreads();
+  const int bstar = s_bstar;
+
+  int count;
+  if (bstar >= 0 && bin_cnt[bstar] <= (uint32_t)kTopPSmallBin) {
+    // 4a. rank the crossing bin's candidates exactly and walk their masses.
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float d = __fsub_rn(key_float(keys[i]), lmax);
+      const int b = min(kTopPBins - 1, (int)__fmul_rn(-d, inv_w));
+      sel[i] = b < bstar ? 1 : 0;
+      if (b == bstar) list[atomicAdd(&s_list_n, 1u)] = rank_key(keys[i], i);
     }
     __syncthreads();
-    const uint32_t prefix = s_prefix;
-    for (int i = tid; i < n; i += blockDim.x) {
-      const uint32_t key = keys[i];
-      if ((key & mask) == prefix) {
-        const uint32_t b = (key >> shift) & 255u;
-        atomicAdd(&hist_mass[b], mass[i]);
-        atomicAdd(&hist_cnt[b], 1u);
-      }
+    const int m_in = (int)s_list_n;
+    for (int t = tid; t < m_in; t += blockDim.x) {
+      const unsigned long long me = list[t];
+      int r = 0;
+      for (int j = 0; j < m_in; ++j) r += list[j] > me;
+      ranked[r] = me;
     }
     __syncthreads();
     if (warp == 0) {
-      const unsigned long long target = s_target;
-      const unsigned long long base_mass = s_mass_gt;
-      const uint32_t base_cnt = s_cnt_gt;
-      unsigned long long lm[8];
-      uint32_t lc[8];
-      unsigned long long sm = 0ull;
-      uint32_t sc = 0u;
+      unsigned long long base = s_mass_gt;
+      int taken = m_in;
+      for (int c0 = 0; c0 < m_in; c0 += 32) {
+        const int j = c0 + lane;
+        unsigned long long v = j < m_in ? mass[rank_index(ranked[j])] : 0ull;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        lm[j] = hist_mass[8 * lane + j];
-        lc[j] = hist_cnt[8 * lane + j];
-        sm += lm[j];
-        sc += lc[j];
-      }
-      unsigned long long suf_m = sm;
-      uint32_t suf_c = sc;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const unsigned long long ym = __shfl_down_sync(0xffffffffu, suf_m, off);
-        const uint32_t yc = __shfl_down_sync(0xffffffffu, suf_c, off);
-        if (lane + off < 32) {
-          suf_m += ym;
-          suf_c += yc;
+        for (int off = 1; off < 32; off <<= 1) {
+          const unsigned long long y = __shfl_up_sync(0xffffffffu, v, off);
+          if (lane >= off) v += y;
         }
+        const unsigned hit = __ballot_sync(0xffffffffu, j < m_in && base + v >= target);
+        if (hit) {
+          taken = c0 + __ffs(hit);
+          break;
+        }
+        base += __shfl_sync(0xffffffffu, v, 31);
       }
-      const unsigned long long above_m = base_mass + suf_m - sm;
-      const uint32_t above_c = base_cnt + suf_c - sc;
+      if (lane == 0) s_count = (int)s_cnt_gt + taken;
       __syncwarp();
-      // crossing lane: above_m < target <= above_m + sm (exactly one lane; sm > 0 there)
-      if (above_m < target && target <= above_m + sm) {
-        unsigned long long acc_m = above_m;
-        uint32_t acc_c = above_c;
-        for (int j = 7; j >= 0; --j) {
-          if (acc_m + lm[j] >= target) {
-            s_prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
-            s_mass_gt = acc_m;
-            s_cnt_gt = acc_c;
-            break;
+      for (int j = lane; j < taken; j += 32) sel[rank_index(ranked[j])] = 1;
+    }
+    __syncthreads();
+    count = s_count;
+  } else {
+    // 4b. fallback: radix search over the order-preserving keys.
+    if (tid == 0) {
+      s_target = target;
+      s_mass_gt = 0ull;
+      s_cnt_gt = 0u;
+      s_prefix = 0u;
+    }
+    __syncthreads();
+
+    uint32_t mask = 0u;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int b = tid; b < 256; b += blockDim.x) {
+        hist_mass[b] = 0ull;
+        hist_cnt[b] = 0u;
+      }
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      // Warp-aggregated histogram: lanes with the same bin are grouped with
+      // match.any and each group's leader adds the group's mass (staged per
+      // warp in shared memory) and count with one atomic each.
+      for (int base = warp * 32; base < n; base += nwarps * 32) {
+        const int i = base + lane;
+        uint32_t bin = 256u;
+        unsigned long long mv = 0ull;
+        if (i < n) {
+          const uint32_t key = keys[i];
+          if ((key & mask) == prefix) {
+            bin = (key >> shift) & 255u;
+            mv = mass[i];
           }
-          acc_m += lm[j];
-          acc_c += lc[j];
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        stage[warp][lane] = mv;
+        __syncwarp();
+        if (bin != 256u && lane == __ffs(peers) - 1) {
+          unsigned long long sum = 0ull;
+          for (unsigned p = peers; p; p &= p - 1) sum += stage[warp][__ffs(p) - 1];
+          atomicAdd(&hist_mass[bin], sum);
+          atomicAdd(&hist_cnt[bin], (uint32_t)__popc(peers));
+        }
+        __syncwarp();
+      }
+      __syncthreads();
+      if (warp == 0) {
+        const unsigned long long tgt = s_target;
+        const unsigned long long base_mass = s_mass_gt;
+        const uint32_t base_cnt = s_cnt_gt;
+        unsigned long long lm[8];
+        uint32_t lc[8];
+        unsigned long long sm = 0ull;
+        uint32_t sc = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          lm[j] = hist_mass[8 * lane + j];
+          lc[j] = hist_cnt[8 * lane + j];
+          sm += lm[j];
+          sc += lc[j];
+        }
+        unsigned long long suf_m = sm;
+        uint32_t suf_c = sc;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const unsigned long long ym = __shfl_down_sync(0xffffffffu, suf_m, off);
+          const uint32_t yc = __shfl_down_sync(0xffffffffu, suf_c, off);
+          if (lane + off < 32) {
+            suf_m += ym;
+            suf_c += yc;
+          }
+        }
+        const unsigned long long above_m = base_mass + suf_m - sm;
+        const uint32_t above_c = base_cnt + suf_c - sc;
+        __syncwarp();
+        // crossing lane: above_m < target <= above_m + sm (exactly one lane)
+        if (above_m < tgt && tgt <= above_m + sm) {
+          unsigned long long acc_m = above_m;
+          uint32_t acc_c = above_c;
+          for (int j = 7; j >= 0; --j) {
+            if (acc_m + lm[j] >= tgt) {
+              s_prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
+              s_mass_gt = acc_m;
+              s_cnt_gt = acc_c;
+              break;
+            }
+            acc_m += lm[j];
+            acc_c += lc[j];
+          }
         }
       }
+      mask |= 255u << shift;
+      __syncthreads();
     }
-    mask |= 255u << shift;
-    __syncthreads();
+    const uint32_t kstar = s_prefix;
+    const unsigned long long mass_gt = s_mass_gt;
+    const uint32_t cnt_gt = s_cnt_gt;
+    // every K*-tie has the same logit, hence the same mass
+    const unsigned long long m_tie =
+        mass_of(det_exp((double)__fsub_rn(key_float(kstar), lmax)));
+    const unsigned long long need_ull =
+        (m_tie > 0ull) ? (target - mass_gt + m_tie - 1ull) / m_tie : 1ull;
+    // tie ranks in candidate order
+    const int seg = (n + blockDim.x - 1) / blockDim.x;
+    const int beg = min(n, tid * seg);
+    const int end = min(n, beg + seg);
+    uint32_t eq = 0u;
+    for (int i = beg; i < end; ++i) eq += keys[i] == kstar;
+    uint32_t total_eq;
+    const uint32_t eq_before = block_exclusive_scan(eq, scan_scratch, &total_eq);
+    const uint32_t need = (uint32_t)min(need_ull, (unsigned long long)total_eq);
+    const uint32_t take_eq = (eq_before >= need) ? 0u : min(eq, need - eq_before);
+    uint32_t seen = 0u;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t key = keys[i];
+      bool take = key > kstar;
+      if (key == kstar) {
+        take = seen < take_eq;
+        ++seen;
+      }
+      sel[i] = take ? 1 : 0;
+    }
+    count = (int)(cnt_gt + need);
   }
-  const uint32_t kstar = s_prefix;
-  const unsigned long long mass_gt = s_mass_gt;
-  const uint32_t cnt_gt = s_cnt_gt;
-  const unsigned long long target = s_target;
-  // every K*-tie has the same logit, hence the same mass
-  const unsigned long long m_tie =
-      mass_of(det_exp((double)__fsub_rn(key_float(kstar), lmax)));
-  unsigned long long need_ull = (m_tie > 0ull) ? (target - mass_gt + m_tie - 1ull) / m_tie : 1ull;
+  __syncthreads();
 
-  // 4. tie ranks in candidate order and the per-row outputs.
-  const int seg = (n + blockDim.x - 1) / blockDim.x;
-  const int beg = min(n, tid * seg);
-  const int end = min(n, beg + seg);
-  uint32_t eq = 0u, gt = 0u;
-  for (int i = beg; i < end; ++i) {
-    eq += keys[i] == kstar;
-    gt += keys[i] > kstar;
+  // Per-row outputs: the count and (optionally) the selected positions in
+  // candidate order, i.e. ascending positions (pages are ascending).
+  if (tid == 0) a.head_count[row] = count;
+  if (a.head_pos) {
+    const int seg = (n + blockDim.x - 1) / blockDim.x;
+    const int beg = min(n, tid * seg);
+    const int end = min(n, beg + seg);
+    uint32_t c = 0u;
+    for (int i = beg; i < end; ++i) c += sel[i];
+    uint32_t total;
+    uint32_t slot = block_exclusive_scan(c, scan_scratch, &total);
+    int32_t* hp = a.head_pos + (int64_t)row * n;
+    for (int i = beg; i < end; ++i)
+      if (sel[i]) hp[slot++] = (int32_t)cand_position(prow, i, a.block, a.sink);
   }
-  uint32_t total_eq;
-  const uint32_t eq_before = block_exclusive_scan(eq, scan_scratch, &total_eq);
-  const uint32_t need = (uint32_t)min(need_ull, (unsigned long long)total_eq);
-  const uint32_t take_eq = (eq_before >= need) ? 0u : min(eq, need - eq_before);
-  uint32_t total_sel;
-  const uint32_t slot0 = block_exclusive_scan(gt + take_eq, scan_scratch, &total_sel);
-  if (tid == 0) a.head_count[row] = (int32_t)(cnt_gt + need);
 
   // All rows are final and the leader's bitmap is initialised.
   cluster.sync();
 
+  // One remote OR per selected page (its block_size candidates are
+  // consecutive positions); pages wider than 32 positions OR per candidate.
   uint32_t* leader_bitmap = cluster.map_shared_rank(bitmap, 0);
-  int32_t* hp = a.head_pos ? a.head_pos + (int64_t)row * n : nullptr;
-  uint32_t slot = slot0, seen = 0u;
   bool bad = false;
-  for (int i = beg; i < end; ++i) {
-    const uint32_t key = keys[i];
-    bool take = key > kstar;
-    if (key == kstar) {
-      take = seen < take_eq;
-      ++seen;
+  for (int pg = tid; pg < a.b0; pg += blockDim.x) {
+    const int64_t pos0 = (int64_t)a.sink + (int64_t)prow[pg] * a.block;
+    if (a.block <= 32) {
+      uint32_t m32 = 0u;
+      for (int j = 0; j < a.block; ++j) m32 |= (uint32_t)sel[pg * a.block + j] << j;
+      if (!m32) continue;
+      if (pos0 < 0 || pos0 + a.block > L) {
+        bad = true;
+        continue;
+      }
+      const uint32_t sh = (uint32_t)(pos0 & 31);
+      atomicOr(&leader_bitmap[pos0 >> 5], m32 << sh);
+      if (sh + (uint32_t)a.block > 32u && (m32 >> (32u - sh)))
+        atomicOr(&leader_bitmap[(pos0 >> 5) + 1], m32 >> (32u - sh));
+    } else {
+      for (int j = 0; j < a.block; ++j) {
+        if (!sel[pg * a.block + j]) continue;
+        const int64_t pos = pos0 + j;
+        if (pos < 0 || pos >= L) {
+          bad = true;
+          continue;
+        }
+        atomicOr(&leader_bitmap[pos >> 5], 1u << (pos & 31));
+      }
     }
-    if (!take) continue;
-    const int64_t pos = cand_position(prow, i, a.block, a.sink);
-    if (hp) hp[slot] = (int32_t)pos;
-    ++slot;
-    if (pos < 0 || pos >= L) {
-      bad = true;
-      continue;
-    }
-    atomicOr(&leader_bitmap[pos >> 5], 1u << (pos & 31));
   }
   if (bad && a.error_flag) atomicExch(a.error_flag, TW_ERR_INVALID_INDEX);
   cluster.sync();
 
   if (rank != 0) return;
-  // 5. leader: sorted union by popcount scan over contiguous word segments.
+  // Leader: sorted union by popcount scan over contiguous word segments.
   const int wseg = (words + blockDim.x - 1) / blockDim.x;
   const int wbeg = min(words, tid * wseg);
   const int wend = min(words, wbeg + wseg);
@@ -281,9 +440,8 @@ top_p_union_kernel(TopPArgs a) {
 }
 
 size_t top_p_smem_bytes(int n, int64_t old_length) {
-  const size_t keys = (((size_t)n * 4) + 15) & ~(size_t)15;
   const size_t words = (size_t)((old_length + 31) / 32);
-  return keys + (size_t)n * 8 + words * 4;
+  return top_p_head_bytes(n) + words * 4 + (size_t)n;
 }
 
 int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
@@ -293,12 +451,15 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
   cudaGetDevice(&device);
   int max_optin = 0;
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-  // static shared: histograms + scratch (~3.5 KB)
-  if (smem + 4096 > (size_t)max_optin) return TW_ERR_CAPACITY;
-  cudaError_t err = cudaFuncSetAttribute(top_p_union_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err == cudaSuccess)
-    err = cudaFuncSetAttribute(top_p_union_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncAttributes fa{};
+  cudaError_t err = cudaFuncGetAttributes(&fa, top_p_union_kernel);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  if (smem + fa.sharedSizeBytes > (size_t)max_optin) return TW_ERR_CAPACITY;
+  err = cudaFuncSetAttribute(top_p_union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
   if (err != cudaSuccess) {
     set_last_cuda_error(err);
     return TW_ERR_CUDA;

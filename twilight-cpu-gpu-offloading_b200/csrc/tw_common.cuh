@@ -122,6 +122,72 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return warp_base + x - v;
 }
 
+// 64-bit variant of block_exclusive_scan (scratch: 32 u64).
+__device__ __forceinline__ unsigned long long block_exclusive_scan_u64(
+    unsigned long long v, unsigned long long* scratch, unsigned long long* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  unsigned long long x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    unsigned long long y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    unsigned long long w = (lane < nwarps) ? scratch[lane] : 0ull;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      unsigned long long y = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += y;
+    }
+    scratch[lane] = w;
+  }
+  __syncthreads();
+  const unsigned long long warp_base = (warp > 0) ? scratch[warp - 1] : 0ull;
+  *total = scratch[nwarps - 1];
+  __syncthreads();
+  return warp_base + x - v;
+}
+
+// In-place bitonic sort, descending, of n (a power of two) 64-bit keys in
+// shared memory by the whole block.  The caller synchronises before the call;
+// the sorted keys are visible to all threads on return.
+__device__ __forceinline__ void bitonic_sort_desc(unsigned long long* s, int n) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int t = threadIdx.x; t < (n >> 1); t += blockDim.x) {
+        const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));
+        const int p = i | j;
+        const unsigned long long a = s[i], b = s[p];
+        const bool desc = (i & k) == 0;
+        if (desc ? (a < b) : (a > b)) {
+          s[i] = b;
+          s[p] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Sort key of candidate i with order-preserving float key k: larger k first,
+// then lower i first (the rank order the selection uses for ties).
+__device__ __forceinline__ unsigned long long rank_key(uint32_t k, int i) {
+  return ((unsigned long long)k << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+}
+__device__ __forceinline__ int rank_index(unsigned long long rk) {
+  return (int)(0xffffffffu - (uint32_t)(rk & 0xffffffffull));
+}
+
+__host__ __device__ __forceinline__ int next_pow2(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
 }  // namespace tw
 
 #define TW_DISPATCH_KV_DTYPE(dtype, T, ...)                 \
