@@ -392,7 +392,7 @@ def run_ours(args) -> int:
                 "mean_union_rows": avg["union_rows"],
             },
             "clocks": clocks,
-            "gpu_launches": step.launches_per_step * K,
+            "gpu_launches": step.launches_per_step * K * world,
             "kernel_ms": {n: round(float(np.mean(v)), 5) for n, v in kern_ms.items()},
             "roofline": {
                 "bound": "host_link",
