@@ -235,7 +235,8 @@ class DeviceStep:
             if "gather" in ev:
                 ev["gather"][0].record()
             tw._lib.check(lib.tw_gather_union(
-                self.slab.key_device_ptr, self.slab.value_device_ptr, self.max_len, 0, G, self.L,
+                self.slab.key_device_ptr, self.slab.value_device_ptr, None, 0, self.max_len, 0, G,
+                self.L,
                 self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
                 self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, self.flat_k.data_ptr(),
                 self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), st),
@@ -249,7 +250,7 @@ class DeviceStep:
                 ev["attention"][1].record()
         # new token written at position L (the step is repeated at a fixed length)
         tw._lib.check(lib.tw_append_token(
-            self.slab.key_device_ptr, self.slab.value_device_ptr, self.max_len, 0, G, self.L,
+            self.slab.key_device_ptr, self.slab.value_device_ptr, None, 0, self.max_len, 0, G, self.L,
             self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, CFG["sink"], CFG["block"],
             self.pmin.data_ptr(), self.pmax.data_ptr(), self.page_cap * 128, self.packed.data_ptr(),
             self.scale.data_ptr(), self.minimum.data_ptr(), CFG["int4_group"], st), "append_token")
@@ -563,7 +564,16 @@ def make_gather(layer):
     return fn, "torch.index_select (hi/twilight_offload_cache.py:3017-3020)"
 
 
+def host_threads() -> int:
+    """All host cores this process may use (torchrun sets OMP_NUM_THREADS=1 by default)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(layer, queries, budget_s: float = 15.0, max_steps: int = 40) -> dict:
+    torch.set_num_threads(host_threads())
     prep = cpu_prepare(layer)
     gather_fn, gname = make_gather(layer)
     cpu_layer_step(layer, queries[0], prep, gather_fn)  # warm-up
@@ -588,6 +598,7 @@ def run_reference(args) -> int:
         return 0
     from oracle import synth  # noqa: F401  (the reference arm executes the oracle port)
 
+    torch.set_num_threads(host_threads())
     layer, queries = build_workload(None, torch.device("cpu"), seed=0, n_queries=args.steps + args.warmup)
     prep = cpu_prepare(layer)
     gather_fn, gname = make_gather(layer)

@@ -15,6 +15,15 @@
  *   int4 scale / min    [E][max_len][D/gs]   K dtype, gs = quantisation group
  *   queries             [G][R][D]            fp32 (the reference's q.float())
  *
+ * ENTRY DIRECTORY.  Functions that read or write slab rows take
+ * (slab_k, slab_v, entry_dirs, n_entries, max_len).  With entry_dirs NULL,
+ * row p of entry e is slab_{k,v} + (e*max_len + p)*D elements.  Otherwise
+ * entry_dirs is a device array [2][n_entries] of byte addresses: entry_dirs[e]
+ * is row 0 of entry e's K and entry_dirs[n_entries+e] of its V, each entry
+ * holding max_len contiguous rows.  That places GPU-resident heads in device
+ * memory and offloaded heads in the mapped host slab (HeadInfer's head-wise
+ * residency, hi/cache.py:5-145) without a second code path.
+ *
  * Reference interfaces are cited as path:line inside the reference project
  * (source/headinfer/headinfer/ abbreviated hi/).
  */
@@ -175,7 +184,8 @@ int tw_gather_kv(const void* k, const void* v, void* out_k, void* out_v,
  * and the miss branch of assemble_zero_copy (hi/resident_zero_copy.cu:7-42).
  * slab_k/slab_v: device-visible addresses of the K and V planes.
  * Rows beyond rows_cap or positions outside [0, old_length) set *error_flag. */
-int tw_gather_union(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+int tw_gather_union(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
+                    int64_t n_entries, int64_t max_len, int first_entry,
                     int groups, int64_t old_length,
                     const int32_t* union_pos, int64_t pos_stride, const int32_t* union_count,
                     const void* cur_k, const void* cur_v, int head_dim, int dtype,
@@ -190,7 +200,8 @@ int tw_gather_union(const void* slab_k, const void* slab_v, int64_t max_len, int
  * Replaces _selected_positions + update_layer_flat_ragged packing
  * (hi/quest_offload_cache.py:403-511, :724-987) and the per-entry pack of update
  * (:578-630). */
-int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+int tw_gather_quest_heads(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
+                          int64_t n_entries, int64_t max_len, int first_entry,
                           int groups, int heads_per_group, int64_t old_length,
                           int64_t sink_end, int64_t recent_start, int sink, int block_size,
                           const int32_t* pages, int k_pages,
@@ -205,7 +216,8 @@ int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int64_t max_le
  * (hi/quest_offload_cache.py:230-274, hi/twilight_offload_cache.py:551-794) and
  * extends the prefill-only metadata (hi/quest_offload_cache.py:276-289,
  * hi/twilight_offload_cache.py:925-936) to appended tokens. */
-int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int first_entry, int groups,
+int tw_append_token(void* slab_k, void* slab_v, const uint64_t* entry_dirs, int64_t n_entries,
+                    int64_t max_len, int first_entry, int groups,
                     int64_t position, const void* cur_k, const void* cur_v,
                     int head_dim, int dtype, int sink, int block_size,
                     void* page_min, void* page_max, int64_t meta_entry_stride,
@@ -240,7 +252,8 @@ int tw_decode_attention(const void* q, const void* k, const void* v, const int32
  * (sizes the split grid and the workspace, as max_seqlen_k of
  * tw_decode_attention_workspace_size(groups, R, max_rows_per_group, D)).
  * Positions outside [0, old_length) are skipped and set *error_flag. */
-int tw_attend_union(const void* slab_k, const void* slab_v, int64_t max_len, int first_entry,
+int tw_attend_union(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
+                    int64_t n_entries, int64_t max_len, int first_entry,
                     int groups, int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
                     const int32_t* union_count, const void* cur_k, const void* cur_v,
                     const void* q, int heads_per_group, int max_rows_per_group, int head_dim,
@@ -262,6 +275,8 @@ int tw_attend_union(const void* slab_k, const void* slab_v, int64_t max_len, int
 typedef struct tw_decode_layer_args {
   void* slab_k;
   void* slab_v;
+  const uint64_t* entry_dirs; /* [2][n_entries] row-0 addresses, or NULL (see ENTRY DIRECTORY) */
+  int64_t n_entries;
   int64_t max_len;
   int32_t first_entry;
   int32_t groups;

@@ -274,3 +274,50 @@ def test_decode_layer_equals_prepare_plus_attend(tw, cuda, R, dtype):
     for c in caches:
         c.synchronize()
         c.close()
+
+
+def test_resident_heads_match_offloaded(tw, cuda):
+    """GPU-resident entries (device K/V) and offloaded entries (mapped host slab)
+    go through one directory: a cache with half its heads resident gives the same
+    unions, gathered rows and attention, bit for bit, as a fully offloaded one,
+    and the appended token lands where its entry lives."""
+    layers, G, R, L = 2, 4, 4, 2048
+    data = layer_data(layers, G, R, L, "bfloat16", 71)
+    plain = make_twilight(tw, cuda, layers=layers, G=G, R=R, L=L, dtype=torch.bfloat16, extra=4)
+    mixed = make_twilight(tw, cuda, layers=layers, G=G, R=R, L=L, dtype=torch.bfloat16, extra=4,
+                          resident_entries=[0, 3, 5, 6])
+    assert mixed.state_snapshot()["resident_entries"] == [0, 3, 5, 6]
+    for c in (plain, mixed):
+        for li, d in enumerate(data):
+            for g in range(G):
+                c.update(d.keys[g].view(1, 1, L, 128).to(cuda), d.values[g].view(1, 1, L, 128).to(cuda),
+                         li * G + g)
+    assert mixed.entry_kv("key", 3).is_cuda and not mixed.entry_kv("key", 2).is_cuda
+    for step in range(2):
+        for li in range(layers):
+            entries = [li * G + g for g in range(G)]
+            q, kn, vn = _step_inputs(cuda, G, R, "bfloat16", 900 + 10 * step + li)
+            q, kn, vn = q.to(cuda), kn.to(cuda), vn.to(cuda)
+            if step == 0:
+                qs = [q[g].view(1, R, 1, 128) for g in range(G)]
+                ks = [kn[g].view(1, 1, 1, 128) for g in range(G)]
+                vs = [vn[g].view(1, 1, 1, 128) for g in range(G)]
+                outs = []
+                for c in (plain, mixed):
+                    c.prepare_layer_selection(entries=entries, queries=qs)
+                    outs.append(c.update_layer_gqa_group_ragged(key_states=ks, value_states=vs,
+                                                                queries=qs, entries=entries))
+                for i in range(3):
+                    assert torch.equal(outs[0][i], outs[1][i])
+                assert outs[0][3:] == outs[1][3:]
+            else:
+                a = plain.decode_layer(queries=q, key_states=kn, value_states=vn, entries=entries)
+                b = mixed.decode_layer(queries=q, key_states=kn, value_states=vn, entries=entries)
+                torch.cuda.synchronize()
+                assert torch.equal(a, b)
+            for g in range(G):
+                e = li * G + g
+                assert torch.equal(mixed.entry_kv("key", e)[L + step].cpu(), kn[g].cpu())
+    for c in (plain, mixed):
+        c.synchronize()
+        c.close()

@@ -341,7 +341,7 @@ def test_append_token_running_metadata(tw, cuda, dtype):
         kn = kd[:, pos].contiguous()
         vn = vd[:, pos].contiguous()
         tw._lib.check(lib.tw_append_token(
-            slab.key_device_ptr, slab.value_device_ptr, max_len, 0, G, pos, kn.data_ptr(),
+            slab.key_device_ptr, slab.value_device_ptr, None, 0, max_len, 0, G, pos, kn.data_ptr(),
             vn.data_ptr(), 128, DTYPE_CODE[dtype], sink, block, pmin.data_ptr(), pmax.data_ptr(),
             cap * 128, packed.data_ptr(), scale.data_ptr(), minimum.data_ptr(), 32,
             torch.cuda.current_stream().cuda_stream))
@@ -387,7 +387,7 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
     cu = torch.zeros(G + 1, dtype=torch.int32, device=cuda)
     lib = tw.load_library()
     tw._lib.check(lib.tw_gather_union(
-        slab.key_device_ptr, slab.value_device_ptr, max_len, 0, G, L, union_pos.data_ptr(), L,
+        slab.key_device_ptr, slab.value_device_ptr, None, 0, max_len, 0, G, L, union_pos.data_ptr(), L,
         union_count.data_ptr(), cur_k.data_ptr(), cur_v.data_ptr(), 128, DTYPE_CODE[dtype],
         flat_k.data_ptr(), flat_v.data_ptr(), rows_cap, cu.data_ptr(), err.data_ptr(),
         torch.cuda.current_stream().cuda_stream))

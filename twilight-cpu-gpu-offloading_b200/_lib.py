@@ -41,7 +41,7 @@ class DecodeLayerArgs(ctypes.Structure):
     """tw_decode_layer_args of include/twilight_b200.h (same field order and types)."""
 
     _fields_ = [
-        ("slab_k", P), ("slab_v", P), ("max_len", I64), ("first_entry", I32T), ("groups", I32T),
+        ("slab_k", P), ("slab_v", P), ("entry_dirs", P), ("n_entries", I64), ("max_len", I64), ("first_entry", I32T), ("groups", I32T),
         ("heads_per_group", I32T), ("dtype", I32T), ("page_min", P), ("page_max", P),
         ("page_capacity", I64), ("n_pages", I32T), ("packed", P), ("scale", P), ("minimum", P),
         ("int4_group_size", I32T), ("sink", I32T), ("block_size", I32T), ("b0_pages", I32T),
@@ -74,15 +74,15 @@ SIGNATURES = {
     "tw_select_layer": (I32, [P, P, P, I64, I32, P, P, P, I64, I32, I32, I32, I32, I32, I32, I32,
                               I32, DBL, I64, I64, I64, P, P, I64, P, P, P, P, P, SZ, P]),
     "tw_gather_kv": (I32, [P, P, P, P, P, I64, I64, I64, P, P]),
-    "tw_gather_union": (I32, [P, P, I64, I32, I32, I64, P, I64, P, P, P, I32, I32, P, P, I64, P,
+    "tw_gather_union": (I32, [P, P, P, I64, I64, I32, I32, I64, P, I64, P, P, P, I32, I32, P, P, I64, P,
                               P, P]),
-    "tw_gather_quest_heads": (I32, [P, P, I64, I32, I32, I32, I64, I64, I64, I32, I32, P, I32, P,
+    "tw_gather_quest_heads": (I32, [P, P, P, I64, I64, I32, I32, I32, I64, I64, I64, I32, I32, P, I32, P,
                                     P, I32, I32, P, P, P, P]),
-    "tw_append_token": (I32, [P, P, I64, I32, I32, I64, P, P, I32, I32, I32, I32, P, P, I64, P, P,
+    "tw_append_token": (I32, [P, P, P, I64, I64, I32, I32, I64, P, P, I32, I32, I32, I32, P, P, I64, P, P,
                               P, I32, P]),
     "tw_decode_attention_workspace_size": (SZ, [I32, I32, I32, I32]),
     "tw_decode_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P, SZ, P]),
-    "tw_attend_union": (I32, [P, P, I64, I32, I32, I64, P, I64, P, P, P, P, I32, I32, I32, I32, FLT,
+    "tw_attend_union": (I32, [P, P, P, I64, I64, I32, I32, I64, P, I64, P, P, P, P, I32, I32, I32, I32, FLT,
                               P, I32, P, P, P, SZ, P]),
     "tw_twilight_decode_layer": (I32, [ctypes.POINTER(DecodeLayerArgs), P]),
     "tw_decode_layer_args_size": (SZ, []),

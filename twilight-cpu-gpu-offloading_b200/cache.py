@@ -38,10 +38,14 @@ def _contiguous_entries(entries: list[int]) -> int:
 class QuestTopKOffloadedCache:
     """Pinned-host full cache with per-query-head Quest top-k pages.
 
-    hi/quest_offload_cache.py:23-1055.  Extra keyword (not in the reference):
+    hi/quest_offload_cache.py:23-1055.  Extra keywords (not in the reference):
     ``incremental_page_metadata`` (default False = the reference's candidate
     window capped at the prompt's pages, hi/twilight_offload_cache.py:1062-1069;
-    True = pages completed by appended tokens become candidates).
+    True = pages completed by appended tokens become candidates) and
+    ``resident_entries`` (entries whose K/V stay in GPU memory, HeadInfer's
+    GPU-resident heads; all other entries live in the pinned, mapped host slab).
+    Kernels find each entry's rows through a device directory [2, E] of row-0
+    addresses, so resident and offloaded heads share one code path.
     """
 
     def __init__(self, *, num_cache_entries: int, max_cache_len: int, head_dim: int,
@@ -52,7 +56,8 @@ class QuestTopKOffloadedCache:
                  layer_batched_selection: bool = False, layer_flat_ragged_execution: bool = False,
                  sparse_gather_stabilized: bool = False,
                  per_head_varlen_attention_reference: bool = False,
-                 incremental_page_metadata: bool = False, **ignored: Any) -> None:
+                 incremental_page_metadata: bool = False,
+                 resident_entries: Optional[Any] = None, **ignored: Any) -> None:
         device = torch.device(device)
         if device.type != "cuda" or not torch.cuda.is_available():
             raise ValueError("an operational CUDA device is required")
@@ -106,6 +111,23 @@ class QuestTopKOffloadedCache:
         self._prompt_length: Optional[int] = None
 
         self._slab = MappedHostSlab(self.geometry, dtype)
+        res = sorted(set(int(e) for e in (resident_entries or ())))
+        if any(not 0 <= e < num_cache_entries for e in res):
+            raise ValueError("resident_entries outside [0, num_cache_entries)")
+        self.resident_entries = tuple(res)
+        self._resident_index = {e: i for i, e in enumerate(res)}
+        self._resident_kv = (torch.empty((2, len(res), max_cache_len, head_dim), dtype=dtype,
+                                         device=device) if res else None)
+        itemsize = torch.tensor([], dtype=dtype).element_size()
+        entry_bytes = max_cache_len * head_dim * itemsize
+        dirs = []
+        for plane, base in ((0, self._slab.key_device_ptr), (1, self._slab.value_device_ptr)):
+            for e in range(num_cache_entries):
+                if e in self._resident_index:
+                    dirs.append(self._resident_kv[plane, self._resident_index[e]].data_ptr())
+                else:
+                    dirs.append(base + e * entry_bytes)
+        self._dirs = torch.tensor(dirs, dtype=torch.int64).view(2, num_cache_entries).to(device)
         self.page_capacity = max(1, math.ceil(max(0, max_cache_len - sink_tokens) / block_size))
         E, D = num_cache_entries, head_dim
         self._page_min = torch.empty((E, self.page_capacity, D), dtype=dtype, device=device)
@@ -237,8 +259,16 @@ class QuestTopKOffloadedCache:
 
     def _schedule_d2h(self, entry: int, start: int, key_states, value_states) -> None:
         n = int(key_states.shape[-2])
-        self._host_tensor("key", entry)[0, 0, start:start + n].copy_(key_states[0, 0], non_blocking=True)
-        self._host_tensor("value", entry)[0, 0, start:start + n].copy_(value_states[0, 0], non_blocking=True)
+        self.entry_kv("key", entry)[start:start + n].copy_(key_states[0, 0], non_blocking=True)
+        self.entry_kv("value", entry)[start:start + n].copy_(value_states[0, 0], non_blocking=True)
+
+    def entry_kv(self, kind: str, entry: int) -> torch.Tensor:
+        """[max_len, D] rows of one entry where they live: a device view for a
+        resident entry, the pinned host slab view otherwise."""
+        idx = self._resident_index.get(entry)
+        if idx is not None:
+            return self._resident_kv[0 if kind == "key" else 1, idx]
+        return self._host_tensor(kind, entry)[0, 0]
 
     def _append_rows(self, first_entry: int, groups: int, position: int, k_new: torch.Tensor,
                      v_new: torch.Tensor) -> None:
@@ -246,7 +276,8 @@ class QuestTopKOffloadedCache:
         packed = getattr(self, "_packed", None)
         lib = _lib.load()
         _lib.check(lib.tw_append_token(
-            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self._dirs.data_ptr(),
+            self.geometry.num_entries, self.geometry.max_cache_len,
             first_entry, groups, position, k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM,
             ops._kv_code(self.dtype), self.sink_tokens, self.block_size,
             self._page_min.data_ptr(), self._page_max.data_ptr(), self.page_capacity * HEAD_DIM,
@@ -392,7 +423,8 @@ class QuestTopKOffloadedCache:
         out_k, out_v = self._quest_pack_buffers(total)
         start = self._phase_start()
         _lib.check(_lib.load().tw_gather_quest_heads(
-            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self._dirs.data_ptr(),
+            self.geometry.num_entries, self.geometry.max_cache_len,
             first, groups, R, old_length, w["sink_end"], w["recent_start"], self.sink_tokens,
             self.block_size, None if pages is None else pages.data_ptr(), k_pages,
             k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM, ops._kv_code(self.dtype),
@@ -502,6 +534,9 @@ class QuestTopKOffloadedCache:
             "recent_tokens": self.recent_tokens,
             "num_query_heads_per_kv": self.num_query_heads_per_kv,
             "incremental_page_metadata": self.incremental_page_metadata,
+            "resident_entries": list(self.resident_entries),
+            "resident_kv_gpu_bytes": 0 if self._resident_kv is None else
+            self._resident_kv.numel() * self._resident_kv.element_size(),
             "backend": "sm_100a",
         }
 
@@ -745,7 +780,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         cu = bufs["cu"][slot]
         start = self._phase_start()
         _lib.check(_lib.load().tw_gather_union(
-            self._slab.key_device_ptr, self._slab.value_device_ptr, self.geometry.max_cache_len,
+            self._slab.key_device_ptr, self._slab.value_device_ptr, self._dirs.data_ptr(),
+            self.geometry.num_entries, self.geometry.max_cache_len,
             first, G, old_length, bufs["union_pos"].data_ptr(), self.geometry.max_cache_len,
             bufs["union_count"].data_ptr(), k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM,
             ops._kv_code(self.dtype), out_k.data_ptr(), out_v.data_ptr(), bufs["rows_cap"],
@@ -809,7 +845,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         start = self._phase_start()
         out = ops.attend_union(self._slab, first, old_length, bufs["union_pos"], bufs["union_count"],
                                k_new, v_new, q, min(bufs["per_group_cap"], old_length + 1),
-                               workspace=bufs["attn_workspace"], error_flag=self._error_flag, out=out)
+                               workspace=bufs["attn_workspace"], error_flag=self._error_flag, out=out,
+                               entry_dirs=self._dirs)
         self._phase_end("attention", start)
         self._append_rows(first, G, old_length, k_new, v_new)
         return out
@@ -863,6 +900,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             args = _lib.DecodeLayerArgs()
             args.slab_k = self._slab.key_device_ptr
             args.slab_v = self._slab.value_device_ptr
+            args.entry_dirs = self._dirs.data_ptr()
+            args.n_entries = self.geometry.num_entries
             args.max_len = self.geometry.max_cache_len
             args.groups = G
             args.heads_per_group = R

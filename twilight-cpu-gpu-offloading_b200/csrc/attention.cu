@@ -76,11 +76,14 @@ struct FlatRows {
   }
 };
 
-// Rows read in place from the (mapped host) slab: segment g = the group's sorted
-// union positions, then its current token.
+// Rows read in place from the (mapped host) slab, or per entry through an
+// entry directory (row-0 addresses; resident entries point into device memory):
+// segment g = the group's sorted union positions, then its current token.
 struct UnionRows {
   const uint4* slab_k;
   const uint4* slab_v;
+  const unsigned long long* dirs;  // [2][n_entries] or null
+  int64_t n_entries;
   int64_t max_len;
   int first_entry;
   int64_t old_length;
@@ -102,9 +105,14 @@ struct UnionRows {
       if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
       return false;
     }
-    const int64_t r = (int64_t)(first_entry + s) * max_len + pos;
-    kp = slab_k + r * kVecPerRow;
-    vp = slab_v + r * kVecPerRow;
+    const int64_t e = (int64_t)first_entry + s;
+    if (dirs) {
+      kp = reinterpret_cast<const uint4*>(dirs[e]) + pos * kVecPerRow;
+      vp = reinterpret_cast<const uint4*>(dirs[n_entries + e]) + pos * kVecPerRow;
+    } else {
+      kp = slab_k + (e * max_len + pos) * kVecPerRow;
+      vp = slab_v + (e * max_len + pos) * kVecPerRow;
+    }
     return true;
   }
 };
@@ -414,7 +422,8 @@ extern "C" int tw_decode_attention(const void* q, const void* k, const void* v,
   return TW_ERR_UNSUPPORTED;
 }
 
-extern "C" int tw_attend_union(const void* slab_k, const void* slab_v, int64_t max_len,
+extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
+                               const uint64_t* entry_dirs, int64_t n_entries, int64_t max_len,
                                int first_entry, int groups, int64_t old_length,
                                const int32_t* union_pos, int64_t pos_stride,
                                const int32_t* union_count, const void* cur_k, const void* cur_v,
@@ -423,8 +432,9 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v, int64_t m
                                int out_dtype, float* lse, int32_t* error_flag, void* workspace,
                                size_t workspace_bytes, void* stream) {
   if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
-  if (!slab_k || !slab_v || !union_pos || !union_count || !cur_k || !cur_v || !q || !out ||
-      groups <= 0 || groups > 65535 || heads_per_group <= 0 || first_entry < 0 ||
+  if ((!entry_dirs && (!slab_k || !slab_v)) || !union_pos || !union_count || !cur_k || !cur_v ||
+      !q || !out || groups <= 0 || groups > 65535 || heads_per_group <= 0 || first_entry < 0 ||
+      (entry_dirs && first_entry + groups > n_entries) ||
       old_length < 0 || old_length > max_len || pos_stride < old_length ||
       max_rows_per_group < 1 || !(softmax_scale > 0.0f))
     return TW_ERR_BAD_ARG;
@@ -439,9 +449,10 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v, int64_t m
   const size_t need = attn_ws_bytes(groups, heads_per_group, max_splits, &ws,
                                     reinterpret_cast<char*>(workspace));
   if (max_splits > 1 && (!workspace || workspace_bytes < need)) return TW_ERR_CAPACITY;
-  UnionRows rows{(const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, old_length,
-                 union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
-                 error_flag};
+  UnionRows rows{(const uint4*)slab_k, (const uint4*)slab_v,
+                 (const unsigned long long*)entry_dirs, n_entries, max_len, first_entry,
+                 old_length, union_pos, pos_stride, union_count, (const uint4*)cur_k,
+                 (const uint4*)cur_v, error_flag};
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == TW_F16) {

@@ -34,13 +34,13 @@ int launch_int4_qk(const void* q, int q_dtype, const uint8_t* packed, const void
                    int groups, int R, int b0_pages, int block_size, int sink, int group_size,
                    int dtype, float* logits, cudaStream_t stream);
 
-extern "C" int tw_attend_union(const void*, const void*, int64_t, int, int, int64_t, const int32_t*,
-                               int64_t, const int32_t*, const void*, const void*, const void*, int,
-                               int, int, int, float, void*, int, float*, int32_t*, void*, size_t,
-                               void*);
-extern "C" int tw_append_token(void*, void*, int64_t, int, int, int64_t, const void*, const void*,
-                               int, int, int, int, void*, void*, int64_t, uint8_t*, void*, void*,
-                               int, void*);
+extern "C" int tw_attend_union(const void*, const void*, const uint64_t*, int64_t, int64_t, int,
+                               int, int64_t, const int32_t*, int64_t, const int32_t*, const void*,
+                               const void*, const void*, int, int, int, int, float, void*, int,
+                               float*, int32_t*, void*, size_t, void*);
+extern "C" int tw_append_token(void*, void*, const uint64_t*, int64_t, int64_t, int, int, int64_t,
+                               const void*, const void*, int, int, int, int, void*, void*, int64_t,
+                               uint8_t*, void*, void*, int, void*);
 
 extern "C" const char* tw_status_string(int status) {
   switch (status) {
@@ -184,13 +184,15 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
                       a->old_length, a->sink_end, a->recent_start, a->union_pos, a->pos_stride,
                       a->union_count, a->head_count, a->head_pos, a->error_flag, stream);
   if (rc != TW_OK) return rc;
-  rc = tw_attend_union(a->slab_k, a->slab_v, a->max_len, a->first_entry, G, a->old_length,
+  rc = tw_attend_union(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
+                       a->first_entry, G, a->old_length,
                        a->union_pos, a->pos_stride, a->union_count, a->k_new, a->v_new, a->q, R,
                        a->max_rows_per_group, kHeadDim, a->dtype,
                        1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
                        a->error_flag, a->attn_workspace, a->attn_workspace_bytes, stream);
   if (rc != TW_OK || !a->append) return rc;
-  return tw_append_token(a->slab_k, a->slab_v, a->max_len, a->first_entry, G, a->old_length,
+  return tw_append_token(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
+                         a->first_entry, G, a->old_length,
                          a->k_new, a->v_new, kHeadDim, a->dtype, a->sink, a->block_size,
                          a->page_min, a->page_max, a->page_capacity * kHeadDim, a->packed,
                          a->scale, a->minimum, a->int4_group_size, stream);

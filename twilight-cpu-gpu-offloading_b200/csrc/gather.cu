@@ -60,9 +60,24 @@ constexpr int kMaxGroups = 64;
 
 // Rows of the union layout: group g occupies [off[g], off[g] + count[g] + 1);
 // its last row is the current token.
+// Row-0 address of entry e: from the entry directory when given, else the slab.
+__device__ __forceinline__ void entry_rows(const uint4* slab_k, const uint4* slab_v,
+                                           const unsigned long long* dirs, int64_t n_entries,
+                                           int64_t max_len, int64_t e, int vec,
+                                           const uint4*& kb, const uint4*& vb) {
+  if (dirs) {
+    kb = reinterpret_cast<const uint4*>(dirs[e]);
+    vb = reinterpret_cast<const uint4*>(dirs[n_entries + e]);
+  } else {
+    kb = slab_k + e * max_len * vec;
+    vb = slab_v + e * max_len * vec;
+  }
+}
+
 template <int kVec>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
+                    const unsigned long long* __restrict__ dirs, int64_t n_entries,
                     int64_t max_len, int first_entry, int groups, int64_t old_length,
                     const int32_t* __restrict__ union_pos, int64_t pos_stride,
                     const int32_t* __restrict__ union_count, const uint4* __restrict__ cur_k,
@@ -107,9 +122,10 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
           kv[u] = make_uint4(0, 0, 0, 0);
           vv[u] = kv[u];
         } else {
-          const int64_t src = ((int64_t)(first_entry + g) * max_len + pos) * kVec + col;
-          kv[u] = __ldcs(slab_k + src);
-          vv[u] = __ldcs(slab_v + src);
+          const uint4 *kb, *vb;
+          entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec, kb, vb);
+          kv[u] = __ldcs(kb + pos * kVec + col);
+          vv[u] = __ldcs(vb + pos * kVec + col);
         }
       } else {
         kv[u] = cur_k[(int64_t)g * kVec + col];
@@ -131,6 +147,7 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
 template <int kVec>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_quest_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
+                    const unsigned long long* __restrict__ dirs, int64_t n_entries,
                     int64_t max_len, int first_entry, int R, int64_t old_length, int64_t sink_end,
                     int64_t recent_start, int sink, int block, const int32_t* __restrict__ pages,
                     int k_pages, const uint4* __restrict__ cur_k, const uint4* __restrict__ cur_v,
@@ -171,9 +188,10 @@ gather_quest_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
         kv[u] = make_uint4(0, 0, 0, 0);
         vv[u] = kv[u];
       } else {
-        const int64_t src = ((int64_t)(first_entry + g) * max_len + pos) * kVec + col;
-        kv[u] = __ldcs(slab_k + src);
-        vv[u] = __ldcs(slab_v + src);
+        const uint4 *kb, *vb;
+        entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec, kb, vb);
+        kv[u] = __ldcs(kb + pos * kVec + col);
+        vv[u] = __ldcs(vb + pos * kVec + col);
       }
     }
 #pragma unroll
@@ -220,7 +238,8 @@ extern "C" int tw_gather_kv(const void* k, const void* v, void* out_k, void* out
   return check_launch();
 }
 
-extern "C" int tw_gather_union(const void* slab_k, const void* slab_v, int64_t max_len,
+extern "C" int tw_gather_union(const void* slab_k, const void* slab_v,
+                               const uint64_t* entry_dirs, int64_t n_entries, int64_t max_len,
                                int first_entry, int groups, int64_t old_length,
                                const int32_t* union_pos, int64_t pos_stride,
                                const int32_t* union_count, const void* cur_k, const void* cur_v,
@@ -228,9 +247,10 @@ extern "C" int tw_gather_union(const void* slab_k, const void* slab_v, int64_t m
                                int64_t rows_cap, int32_t* cu_seqlens, int32_t* error_flag,
                                void* stream) {
   if (head_dim != kHeadDim || (dtype != TW_F16 && dtype != TW_BF16)) return TW_ERR_UNSUPPORTED;
-  if (!slab_k || !slab_v || !union_pos || !union_count || !cur_k || !cur_v || !out_k || !out_v ||
-      !cu_seqlens || groups <= 0 || groups > kMaxGroups || first_entry < 0 || old_length < 0 ||
-      old_length > max_len || rows_cap <= 0)
+  if ((!entry_dirs && (!slab_k || !slab_v)) || !union_pos || !union_count || !cur_k || !cur_v ||
+      !out_k || !out_v || !cu_seqlens || groups <= 0 || groups > kMaxGroups || first_entry < 0 ||
+      old_length < 0 || old_length > max_len || rows_cap <= 0 ||
+      (entry_dirs && first_entry + groups > n_entries))
     return TW_ERR_BAD_ARG;
   if (!aligned16(slab_k) || !aligned16(slab_v) || !aligned16(cur_k) || !aligned16(cur_v) ||
       !aligned16(out_k) || !aligned16(out_v))
@@ -238,22 +258,26 @@ extern "C" int tw_gather_union(const void* slab_k, const void* slab_v, int64_t m
   constexpr int kVec = kHeadDim * 2 / 16;  // 16 vectors per 256-byte row
   const int grid = gather_grid(rows_cap, kGatherThreads / kVec);
   gather_union_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
-      (const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, groups, old_length,
+      (const uint4*)slab_k, (const uint4*)slab_v, (const unsigned long long*)entry_dirs,
+      n_entries, max_len, first_entry, groups, old_length,
       union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
       (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens, error_flag);
   return check_launch();
 }
 
-extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int64_t max_len,
-                                     int first_entry, int groups, int heads_per_group,
+extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v,
+                                     const uint64_t* entry_dirs, int64_t n_entries,
+                                     int64_t max_len, int first_entry, int groups,
+                                     int heads_per_group,
                                      int64_t old_length, int64_t sink_end, int64_t recent_start,
                                      int sink, int block_size, const int32_t* pages, int k_pages,
                                      const void* cur_k, const void* cur_v, int head_dim,
                                      int dtype, void* out_k, void* out_v, int32_t* error_flag,
                                      void* stream) {
   if (head_dim != kHeadDim || (dtype != TW_F16 && dtype != TW_BF16)) return TW_ERR_UNSUPPORTED;
-  if (!slab_k || !slab_v || !cur_k || !cur_v || !out_k || !out_v || groups <= 0 ||
-      heads_per_group <= 0 || first_entry < 0 || old_length < 0 || old_length > max_len ||
+  if ((!entry_dirs && (!slab_k || !slab_v)) || !cur_k || !cur_v || !out_k || !out_v ||
+      groups <= 0 || heads_per_group <= 0 || first_entry < 0 || old_length < 0 ||
+      old_length > max_len || (entry_dirs && first_entry + groups > n_entries) ||
       sink_end < 0 || sink_end > old_length || recent_start < sink_end ||
       recent_start > old_length || k_pages < 0 || (k_pages > 0 && !pages) || block_size <= 0)
     return TW_ERR_BAD_ARG;
@@ -266,7 +290,8 @@ extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v, int
   constexpr int kVec = kHeadDim * 2 / 16;
   const int grid = gather_grid(total, kGatherThreads / kVec);
   gather_quest_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
-      (const uint4*)slab_k, (const uint4*)slab_v, max_len, first_entry, heads_per_group,
+      (const uint4*)slab_k, (const uint4*)slab_v, (const unsigned long long*)entry_dirs, n_entries,
+      max_len, first_entry, heads_per_group,
       old_length, sink_end, recent_start, sink, block_size, pages, k_pages, (const uint4*)cur_k,
       (const uint4*)cur_v, (uint4*)out_k, (uint4*)out_v, seg_len, total, error_flag);
   return check_launch();

@@ -138,7 +138,9 @@ int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
 // and INT4-packs it.
 template <typename T>
 __global__ void append_token_kernel(uint4* __restrict__ slab_k, uint4* __restrict__ slab_v,
-                                    int64_t max_len, int first_entry, int64_t position,
+                                    const unsigned long long* __restrict__ dirs,
+                                    int64_t n_entries, int64_t max_len, int first_entry,
+                                    int64_t position,
                                     const T* __restrict__ cur_k, const T* __restrict__ cur_v,
                                     int sink, int block, T* __restrict__ pmin, T* __restrict__ pmax,
                                     int64_t meta_entry_stride, uint8_t* __restrict__ packed,
@@ -149,14 +151,17 @@ __global__ void append_token_kernel(uint4* __restrict__ slab_k, uint4* __restric
   const int d = threadIdx.x;
   const T* krow = cur_k + (int64_t)g * kHeadDim;
   const T* vrow = cur_v + (int64_t)g * kHeadDim;
-  const int64_t slab_row = (int64_t)entry * max_len + position;
   constexpr int kVecPerRow = kHeadDim * sizeof(T) / 16;
-  if (slab_k != nullptr) {
+  if (slab_k != nullptr || dirs != nullptr) {
+    uint4* kb = dirs ? reinterpret_cast<uint4*>(dirs[entry])
+                     : slab_k + (int64_t)entry * max_len * kVecPerRow;
+    uint4* vb = dirs ? reinterpret_cast<uint4*>(dirs[n_entries + entry])
+                     : slab_v + (int64_t)entry * max_len * kVecPerRow;
     if (d < kVecPerRow) {
-      slab_k[slab_row * kVecPerRow + d] = reinterpret_cast<const uint4*>(krow)[d];
+      kb[position * kVecPerRow + d] = reinterpret_cast<const uint4*>(krow)[d];
     } else if (d < 2 * kVecPerRow) {
       const int j = d - kVecPerRow;
-      slab_v[slab_row * kVecPerRow + j] = reinterpret_cast<const uint4*>(vrow)[j];
+      vb[position * kVecPerRow + j] = reinterpret_cast<const uint4*>(vrow)[j];
     }
   }
   if (pmin != nullptr && position >= sink) {
@@ -284,7 +289,8 @@ extern "C" int tw_int4_qk(const float* q, const uint8_t* packed, const void* sca
                         (cudaStream_t)stream);
 }
 
-extern "C" int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int first_entry,
+extern "C" int tw_append_token(void* slab_k, void* slab_v, const uint64_t* entry_dirs,
+                               int64_t n_entries, int64_t max_len, int first_entry,
                                int groups, int64_t position, const void* cur_k, const void* cur_v,
                                int head_dim, int dtype, int sink, int block_size, void* page_min,
                                void* page_max, int64_t meta_entry_stride, uint8_t* packed,
@@ -294,6 +300,7 @@ extern "C" int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int 
       position >= max_len || block_size <= 0 || sink < 0)
     return TW_ERR_BAD_ARG;
   if ((slab_k == nullptr) != (slab_v == nullptr)) return TW_ERR_BAD_ARG;
+  if (entry_dirs && first_entry + groups > n_entries) return TW_ERR_BAD_ARG;
   if ((page_min == nullptr) != (page_max == nullptr)) return TW_ERR_BAD_ARG;
   if (packed != nullptr && (!scale || !minimum || !valid_group_size(group_size)))
     return TW_ERR_BAD_ARG;
@@ -301,7 +308,8 @@ extern "C" int tw_append_token(void* slab_k, void* slab_v, int64_t max_len, int 
     return TW_ERR_BAD_ARG;
   TW_DISPATCH_KV_DTYPE(dtype, T, {
     append_token_kernel<T><<<groups, kHeadDim, 0, (cudaStream_t)stream>>>(
-        (uint4*)slab_k, (uint4*)slab_v, max_len, first_entry, position, (const T*)cur_k,
+        (uint4*)slab_k, (uint4*)slab_v, (const unsigned long long*)entry_dirs, n_entries, max_len,
+        first_entry, position, (const T*)cur_k,
         (const T*)cur_v, sink, block_size, (T*)page_min, (T*)page_max, meta_entry_stride,
         packed, (T*)scale, (T*)minimum, packed ? group_size : 128, kScaleReciprocal);
     return check_launch();

@@ -212,8 +212,10 @@ def attend_union(slab, first_entry: int, old_length: int, union_pos: torch.Tenso
                  q: torch.Tensor, max_rows_per_group: int, *, workspace: torch.Tensor,
                  error_flag: torch.Tensor, out: torch.Tensor | None = None,
                  out_dtype: torch.dtype | None = None, lse: torch.Tensor | None = None,
-                 softmax_scale: float | None = None) -> torch.Tensor:
-    """Fused union gather + decode attention straight from the mapped slab.
+                 softmax_scale: float | None = None,
+                 entry_dirs: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused union gather + decode attention straight from the mapped slab (or,
+    with entry_dirs [2, E] int64 row-0 addresses, from each entry's placement).
     q [G,R,D] (K/V dtype), cur_k/cur_v [G,D], union_pos [G, stride] int32,
     union_count [G] int32 -> out [G,R,D]."""
     _cuda(union_pos, union_count, cur_k, cur_v, q, workspace, error_flag, out, lse)
@@ -223,7 +225,8 @@ def attend_union(slab, first_entry: int, old_length: int, union_pos: torch.Tenso
         out = torch.empty((G, R, D), device=q.device, dtype=out_dtype)
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
     _lib.check(lib().tw_attend_union(
-        slab.key_device_ptr, slab.value_device_ptr, slab.geometry.max_cache_len, first_entry, G,
+        slab.key_device_ptr, slab.value_device_ptr, _ptr(entry_dirs),
+        entry_dirs.shape[-1] if entry_dirs is not None else 0, slab.geometry.max_cache_len, first_entry, G,
         old_length, _ptr(union_pos), union_pos.shape[-1], _ptr(union_count), _ptr(cur_k),
         _ptr(cur_v), _ptr(q), R, int(max_rows_per_group), D, _kv_code(q.dtype),
         ctypes.c_float(scale), _ptr(out), DTYPE_CODES[out.dtype], _ptr(lse), _ptr(error_flag),
