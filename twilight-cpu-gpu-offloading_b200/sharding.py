@@ -57,3 +57,36 @@ def max_over_ranks(value: float, device: torch.device | None = None, group=None)
                      device=device if device is not None else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class HeadShardedLayerStep:
+    """Decode layer-steps of one request whose KV heads are sharded over the
+    ranks of a process group (one KV-head group per GPU).
+
+    Each rank owns `cache`, a TwilightMatchedBudgetOffloadedCache holding only
+    its KV heads (entries = layer * heads_local + i).  `step` runs the local
+    sparse layer-step (selection, zero-copy gather + attention, append) and
+    all-gathers the [heads_local, R, D] outputs into the [G, R, D] tensor that
+    o_proj consumes.  q / k_new / v_new are the full [G, R, D] / [G, D] inputs;
+    each rank reads its own slice (in a tensor-parallel model each rank would
+    compute only that slice)."""
+
+    def __init__(self, cache, kv_heads: int, group=None) -> None:
+        self.cache = cache
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.heads = shard_kv_heads(kv_heads, self.world, self.rank)
+        self.heads_local = len(self.heads)
+        if cache.geometry.num_entries % self.heads_local:
+            raise ValueError("cache entries must be layers x local KV heads")
+
+    def step(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+             out_local: torch.Tensor | None = None) -> torch.Tensor:
+        h0, h1 = self.heads.start, self.heads.stop
+        entries = [layer * self.heads_local + i for i in range(self.heads_local)]
+        local = self.cache.decode_layer(queries=q[h0:h1].contiguous(),
+                                        key_states=k_new[h0:h1].contiguous(),
+                                        value_states=v_new[h0:h1].contiguous(), entries=entries,
+                                        out=out_local)
+        return gather_head_outputs(local, self.group)
