@@ -45,6 +45,8 @@ def gather_head_outputs(local: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather [G_local, R, D] attention outputs into [G, R, D] (rank order =
     KV-head order).  Runs on the tensors' device: NCCL on CUDA, gloo on CPU."""
     world = dist.get_world_size(group)
+    if world == 1:
+        return local
     out = torch.empty((world * local.shape[0], *local.shape[1:]), dtype=local.dtype,
                       device=local.device)
     dist.all_gather_into_tensor(out, local.contiguous(), group=group)
