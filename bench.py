@@ -134,7 +134,11 @@ def pinned_h2d_peak_gbs(device: torch.device, nbytes: int = 256 << 20) -> float:
 
 # --------------------------------------------------------------- workload ---
 
-def build_workload(tw, device: torch.device, seed: int, n_queries: int):
+def build_workload(tw, device: torch.device, seed: int, n_queries: int, rho: float = 0.0):
+    """Seeded cfg2 layer and n_queries decode queries.  rho = 0: independent
+    N(0,1) queries; rho > 0: an AR(1) sequence q_t = rho*q_{t-1} +
+    sqrt(1-rho^2)*eps_t (stationary N(0,1) marginals), the step-to-step query
+    continuity that previous-token row reuse depends on."""
     from oracle import synth  # seeded synthetic inputs (test infrastructure)
 
     G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
@@ -142,16 +146,23 @@ def build_workload(tw, device: torch.device, seed: int, n_queries: int):
                              workload="outliers", sink=CFG["sink"], recent=CFG["recent"],
                              block=CFG["block"], n_outlier_channels=CFG["n_outlier_channels"])
     gq = torch.Generator().manual_seed(seed + 17)
-    queries = torch.randn(n_queries, G, R, 128, generator=gq).to(torch.float16)
-    return layer, queries
+    eps = torch.randn(n_queries, G, R, 128, generator=gq)
+    if rho > 0.0:
+        for t in range(1, n_queries):
+            eps[t] = rho * eps[t - 1] + math.sqrt(1.0 - rho * rho) * eps[t]
+    return layer, eps.to(torch.float16)
 
 
 class DeviceStep:
     """The hot path launched through the C ABI on fixed device buffers."""
 
-    def __init__(self, tw, layer, device: torch.device, fused: bool = True) -> None:
+    def __init__(self, tw, layer, device: torch.device, fused: bool = True,
+                 reuse: bool = False, n_steps: int = 0) -> None:
         self.tw = tw
         self.fused = fused
+        self.reuse = reuse
+        if reuse and not fused:
+            raise ValueError("row reuse is timed on the fused path")
         self.lib = tw.load_library()
         G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
         self.G, self.R, self.L = G, R, L
@@ -201,6 +212,14 @@ class DeviceStep:
         self.k_new = layer.key_new.to(device)
         self.v_new = layer.value_new.to(device)
         self.launches_per_step = 6 if fused else 7
+        self.t = 0
+        if reuse:
+            # ping-pong: step t keeps its rows in slot t % 2 under tag t + 1 and
+            # reads the other slot's rows (tag t) through the row map
+            self.rows2 = torch.empty((2, 2, G, self.per_group_cap, 128), dtype=torch.float16,
+                                     device=device)
+            self.row_map = torch.zeros((G, self.max_len), dtype=torch.int64, device=device)
+            self.row_log = torch.zeros((max(n_steps, 1), G, 2), dtype=torch.int32, device=device)
 
     def load_query(self, q16: torch.Tensor) -> None:
         self.q16.copy_(q16)
@@ -211,6 +230,18 @@ class DeviceStep:
         tw, lib, G, R = self.tw, self.lib, self.G, self.R
         st = torch.cuda.current_stream(self.device).cuda_stream
         ev = events or {}
+        union_pos, union_count, reuse = self.union_pos, self.union_count, None
+        if self.reuse:
+            # The step repeats at length L: positions < L never change, so the
+            # kept rows hold the slab's data; the token row kept at position L
+            # is never looked up (every union position is < L).
+            cur, prv = self.t % 2, 1 - self.t % 2
+            log = self.row_log[min(self.t, self.row_log.shape[0] - 1)]
+            kw = {} if self.t == 0 else dict(prev_tag=self.t, prev_k=self.rows2[prv, 0],
+                                             prev_v=self.rows2[prv, 1])
+            reuse = tw.ops.row_reuse(self.row_map, self.t + 1, next_k=self.rows2[cur, 0],
+                                     next_v=self.rows2[cur, 1], row_counts=log, **kw)
+            self.t += 1
         if "select" in ev:
             ev["select"][0].record()
         tw._lib.check(lib.tw_select_layer(
@@ -218,17 +249,18 @@ class DeviceStep:
             self.cand_pages, self.packed.data_ptr(), self.scale.data_ptr(), self.minimum.data_ptr(),
             self.max_len, G, R, self.b0, CFG["block"], CFG["sink"], 128, CFG["int4_group"], 0,
             CFG["top_p"], self.L, self.sink_end, self.recent_start, self.pages.data_ptr(),
-            self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
+            union_pos.data_ptr(), self.max_len, union_count.data_ptr(),
             self.head_count.data_ptr(), None, self.err.data_ptr(), self.ws.data_ptr(),
             self.ws.numel(), st), "select_layer")
         if "select" in ev:
             ev["select"][1].record()
+        self.last_union_count = union_count
         if self.fused:
             if "attention" in ev:
                 ev["attention"][0].record()
-            tw.ops.attend_union(self.slab, 0, self.L, self.union_pos, self.union_count, self.k_new,
+            tw.ops.attend_union(self.slab, 0, self.L, union_pos, union_count, self.k_new,
                                 self.v_new, self.q16, self.per_group_cap, workspace=self.attn_ws,
-                                error_flag=self.err, out=self.out)
+                                error_flag=self.err, out=self.out, reuse=reuse)
             if "attention" in ev:
                 ev["attention"][1].record()
         else:
@@ -239,8 +271,8 @@ class DeviceStep:
                 self.L,
                 self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
                 self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, self.flat_k.data_ptr(),
-                self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), st),
-                "gather_union")
+                self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), None,
+                st), "gather_union")
             if "gather" in ev:
                 ev["gather"][1].record()
                 ev["attention"][0].record()
@@ -255,21 +287,25 @@ class DeviceStep:
             self.pmin.data_ptr(), self.pmax.data_ptr(), self.page_cap * 128, self.packed.data_ptr(),
             self.scale.data_ptr(), self.minimum.data_ptr(), CFG["int4_group"], st), "append_token")
 
-    def step_bytes(self) -> dict:
-        """Algorithmic bytes of the last step (union / candidate sizes read back)."""
-        counts = self.union_count.cpu().numpy().astype(np.int64)
-        pages = self.pages.cpu().numpy()
+    def step_bytes(self, counts: np.ndarray, pages: np.ndarray,
+                   hit_miss: np.ndarray | None = None) -> dict:
+        """Algorithmic bytes of one step from its union counts [G], selected
+        pages [G, R, b0] and, with row reuse, its (hit, miss) rows [G, 2]."""
+        counts = counts.astype(np.int64)
         uniq_pages = sum(len(np.unique(pages[g])) for g in range(self.G))
         ng = 128 // CFG["int4_group"]
         cand_tokens = uniq_pages * CFG["block"]
         rows = int(counts.sum())
-        host = 512 * rows                                   # K + V rows over the host link
+        hits = int(hit_miss[:, 0].sum()) if hit_miss is not None else 0
+        host = 512 * (rows - hits)                          # K + V rows over the host link
         hbm = (2 * self.G * self.cand_pages * 128 * 2      # Quest min/max, read once per group
                + cand_tokens * (64 + ng * 2 * 2)           # INT4 codes + scale/min of unique candidates
                + 3 * 4 * self.G * self.R * self.b0 * CFG["block"]  # fp32 logits write/read + scores
-               + (0 if self.fused else 2 * 512 * (rows + self.G)))  # staged K/V written then read
+               + (0 if self.fused else 2 * 512 * (rows + self.G))  # staged K/V written then read
+               + (512 * hits + 512 * (rows + self.G) if self.reuse else 0))  # kept rows read / written
         return {"union_rows": rows, "host_bytes": host, "hbm_bytes": hbm,
-                "gather_bytes": host, "unique_candidate_tokens": cand_tokens}
+                "gather_bytes": host, "unique_candidate_tokens": cand_tokens, "hit_rows": hits,
+                "reuse_hbm_bytes": 512 * hits + 512 * (rows + self.G) if self.reuse else 0}
 
     def close(self) -> None:
         self.slab.close()
@@ -289,8 +325,9 @@ def run_ours(args) -> int:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
     K, W = args.steps, args.warmup
-    layer, queries = build_workload(tw, device, seed=rank, n_queries=K + W)
-    step = DeviceStep(tw, layer, device, fused=not args.staged)
+    rho = args.reuse_rho if args.reuse else 0.0
+    layer, queries = build_workload(tw, device, seed=rank, n_queries=K + W, rho=rho)
+    step = DeviceStep(tw, layer, device, fused=not args.staged, reuse=args.reuse, n_steps=K + W)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     torch.cuda.synchronize()
 
@@ -320,7 +357,7 @@ def run_ours(args) -> int:
         per_step.append((s, e))
         for n in names:
             kern[n].append(ev[n])
-        byte_log.append((step.union_count.clone(), step.pages.clone()))
+        byte_log.append((step.last_union_count.clone(), step.pages.clone()))
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -333,10 +370,10 @@ def run_ours(args) -> int:
 
     # algorithmic bytes per step (averaged over the timed steps)
     byts = []
-    for cnt, pg in byte_log:
-        step.union_count.copy_(cnt)
-        step.pages.copy_(pg)
-        byts.append(step.step_bytes())
+    row_log = step.row_log.cpu().numpy() if step.reuse else None
+    for i, (cnt, pg) in enumerate(byte_log):
+        hm = row_log[W + i] if row_log is not None else None
+        byts.append(step.step_bytes(cnt.cpu().numpy(), pg.cpu().numpy(), hm))
     avg = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
 
     t = torch.tensor([total_ms], dtype=torch.float64, device=device)
@@ -350,7 +387,7 @@ def run_ours(args) -> int:
     if rank == 0:
         pinned = pinned_h2d_peak_gbs(device)
         mapped = mapped_read_peak_gbs(tw, step, device)
-        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W)
+        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W, reuse=args.reuse)
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
     if world > 1:
@@ -389,8 +426,11 @@ def run_ours(args) -> int:
                             "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
                 "l2": "flushed before every timed step (512 MiB device write, outside the events)",
                 "parallelism": f"request-sharded replicas x{world}",
-                "path": "fused gather+attention" if step.fused else "staged gather then attention",
+                "path": ("fused gather+attention" if step.fused else "staged gather then attention")
+                        + (" + previous-token row reuse" if step.reuse else ""),
                 "mean_union_rows": avg["union_rows"],
+                "queries": (f"AR(1) rho={rho} (step-to-step continuity)" if step.reuse
+                            else "independent N(0,1) per step"),
             },
             "clocks": clocks,
             "gpu_launches": step.launches_per_step * K * world,
@@ -419,6 +459,12 @@ def run_ours(args) -> int:
             },
             "e2e": e2e,
         }
+        if step.reuse:
+            line["row_reuse"] = {
+                "hit_ratio": round(avg["hit_rows"] / max(avg["union_rows"], 1.0), 4),
+                "mean_hit_rows": avg["hit_rows"],
+                "hbm_bytes_kept_rows": avg["reuse_hbm_bytes"],
+            }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -446,7 +492,7 @@ def mapped_read_peak_gbs(tw, step: DeviceStep, device) -> float:
     return best
 
 
-def run_e2e(tw, layer, queries, device, K, W) -> dict:
+def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False) -> dict:
     """Same step through the public cache API with host buffers: per step H2D of
     the query and the new token's K/V from pinned memory, prepare_layer_selection
     + attend_layer, D2H of the attention output."""
@@ -456,7 +502,7 @@ def run_e2e(tw, layer, queries, device, K, W) -> dict:
         dtype=torch.float16, device=device, sink_tokens=CFG["sink"], recent_tokens=CFG["recent"],
         block_size=CFG["block"], candidate_token_budget=CFG["b0_tokens"], top_p=CFG["top_p"],
         budget_mode="dynamic", layer_batched_selection=True, gqa_groupwise_execution=True,
-        qk_backend="cuda", int4_group_size=CFG["int4_group"])
+        qk_backend="cuda", int4_group_size=CFG["int4_group"], previous_token_resident_cache=reuse)
     for e in range(G):
         cache.update(layer.keys[e].view(1, 1, L, 128).to(device),
                      layer.values[e].view(1, 1, L, 128).to(device), e)
@@ -487,9 +533,14 @@ def run_e2e(tw, layer, queries, device, K, W) -> dict:
         one(W + i)
     dt = time.perf_counter() - t0
     cache.synchronize()
+    extra = {}
+    if reuse:
+        rows = cache.resident_reuse_trace()[W:]
+        extra["row_reuse_hit_ratio"] = round(
+            sum(r["hit_rows"] for r in rows) / max(1, sum(r["history_rows"] for r in rows)), 4)
     cache.close()
     h2d = (G * R * 128 + 2 * G * 128) * 2
-    return {"value": round(K / dt, 3), "unit": "layer-steps/s", "us_per_layer_step": round(dt / K * 1e6, 2),
+    return {**extra,"value": round(K / dt, 3), "unit": "layer-steps/s", "us_per_layer_step": round(dt / K * 1e6, 2),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": G * R * 128 * 2,
             "api": "TwilightMatchedBudgetOffloadedCache.decode_layer (one library call per layer-step)",
             "note": "K/V history stays in the pinned host slab and is read over the host link inside the step"}
@@ -734,6 +785,10 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
                     help="cfg2 (default, the metric's configuration) or cfg5 (head-sharded 70B layer)")
+    ap.add_argument("--reuse", action="store_true",
+                    help="previous-token row reuse (fused path) with AR(1) query continuity")
+    ap.add_argument("--reuse-rho", type=float, default=0.98,
+                    help="AR(1) coefficient of the query sequence under --reuse")
     ap.add_argument("--staged", action="store_true",
                     help="time the staged path (gather to HBM, then attention) instead of the fused kernel")
     args = ap.parse_args()

@@ -175,6 +175,48 @@ int tw_gather_kv(const void* k, const void* v, void* out_k, void* out_v,
                  const int64_t* rows, int64_t n, int64_t source_rows, int64_t row_bytes,
                  int32_t* error_flag, void* stream);
 
+/* ---- previous-token row reuse -----------------------------------------------------------------------
+ * Rows a group gathered at the previous decode step stay in device memory; a
+ * row of this step's union whose position the previous step also read (one
+ * of its union positions, or its current token) is read from there instead of
+ * over the host link.  The reference's previous_token_resident_cache
+ * (hi/twilight_offload_cache.py:2457-2608, :2798-3470; hit/miss mapping
+ * hi/resident_gpu_mapping.py:103-144, hi/resident_mapping.cpp:6-53;
+ * hi/resident_zero_copy.cu:7-42).
+ *
+ * row_map is a direct-addressed table per group: row_map[g][pos] =
+ * (tag << 32) | row, written for every row a step keeps (its union rows and
+ * its current token at pos = old_length), where row indexes that step's kept
+ * rows.  A step reads row_map[g][pos]; the entry is a hit when its tag equals
+ * prev_tag (nonzero) and row < prev_rows, and then the row is read from
+ * prev_k / prev_v.  The step then stores its own entries with next_tag.  Each
+ * position is read and written by one thread group of one launch, so reads
+ * and writes of a step never race.  Zero the table once before the first
+ * step; use tags that are nonzero and unique per step of the table's layer
+ * (a stale entry never carries the previous tag).
+ *
+ * tw_attend_union / tw_twilight_decode_layer keep rows strided: row of
+ * (group g, index i) = g * rows_stride + i in next_k / next_v [G][rows_stride][D]
+ * (union rows in order, then the current token).  tw_gather_union keeps its
+ * own packed output (row = its output row): there next_k / next_v must be
+ * NULL and rows_stride is unused.  prev_k / prev_v hold prev_rows rows of the
+ * previous step's layout, and must not overlap the rows being written.
+ * row_counts [G][2] (nullable) accumulates (hit rows, miss rows) of the union
+ * (the current token is not counted). */
+typedef struct tw_row_reuse {
+  uint64_t* row_map;        /* [G][map_stride], map_stride > old_length */
+  int64_t map_stride;
+  uint32_t prev_tag;        /* 0: no previous rows (every row is a miss) */
+  uint32_t next_tag;        /* nonzero, != prev_tag */
+  const void* prev_k;
+  const void* prev_v;
+  int64_t prev_rows;
+  void* next_k;
+  void* next_v;
+  int64_t rows_stride;
+  int32_t* row_counts;
+} tw_row_reuse;
+
 /* ---- GQA union gather into the attention layout ----------------------------------------------
  * Zero-copy gather of each group's union rows from the host slab, followed by
  * the group's current-token row: out rows [cu[g], cu[g+1]) = slab rows of
@@ -183,14 +225,15 @@ int tw_gather_kv(const void* k, const void* v, void* out_k, void* out_v,
  * update_layer_gqa_group_ragged (hi/twilight_offload_cache.py:2973-3101, :3307-3310)
  * and the miss branch of assemble_zero_copy (hi/resident_zero_copy.cu:7-42).
  * slab_k/slab_v: device-visible addresses of the K and V planes.
- * Rows beyond rows_cap or positions outside [0, old_length) set *error_flag. */
+ * Rows beyond rows_cap or positions outside [0, old_length) set *error_flag.
+ * reuse (nullable): previous-token row reuse, see tw_row_reuse. */
 int tw_gather_union(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
                     int64_t n_entries, int64_t max_len, int first_entry,
                     int groups, int64_t old_length,
                     const int32_t* union_pos, int64_t pos_stride, const int32_t* union_count,
                     const void* cur_k, const void* cur_v, int head_dim, int dtype,
                     void* out_k, void* out_v, int64_t rows_cap, int32_t* cu_seqlens,
-                    int32_t* error_flag, void* stream);
+                    int32_t* error_flag, const tw_row_reuse* reuse, void* stream);
 
 /* ---- Quest per-query-head gather ------------------------------------------------------------------
  * Per (g, r): rows [0, sink_end) U {sink + pages[g][r][i]*block_size + j} U
@@ -232,8 +275,8 @@ int tw_append_token(void* slab_k, void* slab_v, const uint64_t* entry_dirs, int6
  * q: [S][R][D] in `dtype`; k/v: [rows][D] in `dtype`; out: [S][R][D] in out_dtype
  * (dtype or TW_F32); lse (nullable): [S][R] fp32 natural-log sum-exp.
  * max_seqlen_k: an upper bound of cu[s+1]-cu[s] (sizes the split grid).
- * workspace: >= tw_decode_attention_workspace_size(...) bytes; its counter area
- * must be zero before the first call (the kernel leaves it zero). */
+ * workspace: >= tw_decode_attention_workspace_size(...) bytes, 16-byte aligned;
+ * its counter area must be zero before the first call (the kernel leaves it zero). */
 size_t tw_decode_attention_workspace_size(int segments, int heads_per_segment, int max_seqlen_k,
                                           int head_dim);
 int tw_decode_attention(const void* q, const void* k, const void* v, const int32_t* cu_seqlens,
@@ -258,7 +301,8 @@ int tw_attend_union(const void* slab_k, const void* slab_v, const uint64_t* entr
                     const int32_t* union_count, const void* cur_k, const void* cur_v,
                     const void* q, int heads_per_group, int max_rows_per_group, int head_dim,
                     int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
-                    int32_t* error_flag, void* workspace, size_t workspace_bytes, void* stream);
+                    int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                    const tw_row_reuse* reuse, void* stream);
 
 /* ---- whole decode layer-step --------------------------------------------------------------------------
  * One decode layer-step of the Twilight GQA path in one call: Quest score ->
@@ -315,10 +359,13 @@ typedef struct tw_decode_layer_args {
   void* attn_workspace;
   size_t attn_workspace_bytes;
   int32_t max_rows_per_group;
+  const tw_row_reuse* reuse; /* NULL: no row reuse */
 } tw_decode_layer_args;
 int tw_twilight_decode_layer(const tw_decode_layer_args* args, void* stream);
 /* sizeof(tw_decode_layer_args), for binding-layout checks. */
 size_t tw_decode_layer_args_size(void);
+/* sizeof(tw_row_reuse), for binding-layout checks. */
+size_t tw_row_reuse_size(void);
 
 /* ---- allocation-free decode attention ---------------------------------------------------------------
  * No counterpart in the reference: an addition of this library.  Same

@@ -389,7 +389,7 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
     tw._lib.check(lib.tw_gather_union(
         slab.key_device_ptr, slab.value_device_ptr, None, 0, max_len, 0, G, L, union_pos.data_ptr(), L,
         union_count.data_ptr(), cur_k.data_ptr(), cur_v.data_ptr(), 128, DTYPE_CODE[dtype],
-        flat_k.data_ptr(), flat_v.data_ptr(), rows_cap, cu.data_ptr(), err.data_ptr(),
+        flat_k.data_ptr(), flat_v.data_ptr(), rows_cap, cu.data_ptr(), err.data_ptr(), None,
         torch.cuda.current_stream().cuda_stream))
     max_rows = max(counts) + 1
     ws = torch.zeros(tw.ops.decode_attention_workspace_bytes(G, R, max_rows), dtype=torch.uint8, device=cuda)

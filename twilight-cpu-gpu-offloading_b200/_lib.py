@@ -50,7 +50,17 @@ class DecodeLayerArgs(ctypes.Structure):
         ("pages", P), ("union_pos", P), ("pos_stride", I64), ("union_count", P),
         ("head_count", P), ("head_pos", P), ("error_flag", P), ("select_workspace", P),
         ("select_workspace_bytes", SZ), ("attn_workspace", P), ("attn_workspace_bytes", SZ),
-        ("max_rows_per_group", I32T),
+        ("max_rows_per_group", I32T), ("reuse", P),
+    ]
+
+
+class RowReuse(ctypes.Structure):
+    """tw_row_reuse of include/twilight_b200.h (previous-token row reuse)."""
+
+    _fields_ = [
+        ("row_map", P), ("map_stride", I64), ("prev_tag", ctypes.c_uint32),
+        ("next_tag", ctypes.c_uint32), ("prev_k", P), ("prev_v", P), ("prev_rows", I64),
+        ("next_k", P), ("next_v", P), ("rows_stride", I64), ("row_counts", P),
     ]
 
 
@@ -75,7 +85,7 @@ SIGNATURES = {
                               I32, DBL, I64, I64, I64, P, P, I64, P, P, P, P, P, SZ, P]),
     "tw_gather_kv": (I32, [P, P, P, P, P, I64, I64, I64, P, P]),
     "tw_gather_union": (I32, [P, P, P, I64, I64, I32, I32, I64, P, I64, P, P, P, I32, I32, P, P, I64, P,
-                              P, P]),
+                              P, ctypes.POINTER(RowReuse), P]),
     "tw_gather_quest_heads": (I32, [P, P, P, I64, I64, I32, I32, I32, I64, I64, I64, I32, I32, P, I32, P,
                                     P, I32, I32, P, P, P, P]),
     "tw_append_token": (I32, [P, P, P, I64, I64, I32, I32, I64, P, P, I32, I32, I32, I32, P, P, I64, P, P,
@@ -83,9 +93,10 @@ SIGNATURES = {
     "tw_decode_attention_workspace_size": (SZ, [I32, I32, I32, I32]),
     "tw_decode_attention": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P, SZ, P]),
     "tw_attend_union": (I32, [P, P, P, I64, I64, I32, I32, I64, P, I64, P, P, P, P, I32, I32, I32, I32, FLT,
-                              P, I32, P, P, P, SZ, P]),
+                              P, I32, P, P, P, SZ, ctypes.POINTER(RowReuse), P]),
     "tw_twilight_decode_layer": (I32, [ctypes.POINTER(DecodeLayerArgs), P]),
     "tw_decode_layer_args_size": (SZ, []),
+    "tw_row_reuse_size": (SZ, []),
     "tw_decode_attention_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P]),
 }
 

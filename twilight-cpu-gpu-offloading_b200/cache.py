@@ -544,6 +544,116 @@ class QuestTopKOffloadedCache:
         self._slab.close()
 
 
+_RESIDENT_OPTIONS = {
+    # option: (default, allowed values); hi/twilight_offload_cache.py:163-175, :215-262
+    "resident_mapping_backend": ("torch", {"torch", "native", "native_compact", "gpu_bitmap"}),
+    "resident_hit_copy_backend": ("torch", {"torch", "triton"}),
+    "resident_snapshot_backend": ("torch", {"torch", "triton", "contiguous"}),
+    "resident_position_snapshot_backend": ("clone", {"clone", "reference"}),
+}
+
+
+def _check_resident_options(enabled: bool, options: dict[str, Any]) -> None:
+    """The reference's validation of its resident-cache implementation options
+    (hi/twilight_offload_cache.py:215-262).  They select among the reference's
+    own mapping / copy / snapshot implementations; here one CUDA path serves
+    them all, so valid values are accepted and otherwise unused."""
+    for name, (default, allowed) in _RESIDENT_OPTIONS.items():
+        value = options.get(name, default)
+        if value not in allowed:
+            raise ValueError(f"unknown {name.replace('_', ' ')}")
+        if value != default and not enabled:
+            raise ValueError(f"{name} requires the previous-token resident cache")
+    if options.get("resident_zero_copy", False) and not enabled:
+        raise ValueError("resident zero-copy requires resident cache")
+    if options.get("resident_precompute_gpu_mapping", False) and not options.get(
+            "resident_zero_copy", False):
+        raise ValueError("precomputed GPU mapping requires mapped resident fast path")
+    mapping = options.get("resident_mapping_backend", "torch")
+    hit_copy = options.get("resident_hit_copy_backend", "torch")
+    snapshot = options.get("resident_snapshot_backend", "torch")
+    if mapping in {"native_compact", "gpu_bitmap"} and hit_copy != "triton":
+        raise ValueError("compact hit indices require Triton hit copy")
+    if snapshot == "contiguous" and (mapping not in {"native_compact", "gpu_bitmap"}
+                                     or hit_copy != "triton"):
+        raise ValueError("contiguous snapshot requires native_compact mapping and Triton hit copy")
+
+
+class _RowReusePool:
+    """Previous-token row reuse state of one GQA group count: per layer, the
+    K/V rows of the previous decode step (union rows, then the current token)
+    stay in device memory, and the next step reads every row it shares with
+    them from there instead of over the host link
+    (hi/twilight_offload_cache.py:2457-2608 and :3323-3470 keep the same
+    per-layer state; hi/resident_gpu_mapping.py:103-144 maps hits/misses).
+    Which previous row holds a position is recorded in the cache's row map
+    under the step's tag.
+
+    A slot holds one layer-step's rows kv [2, G * rows_per_group, D] and, for
+    the staged gather, its cu_seqlens [G + 1].  A step writes a free slot and
+    releases its layer's old one, so layers stepping in turn hold layers + 1
+    slots."""
+
+    def __init__(self, groups: int, rows_per_group: int, dtype: torch.dtype,
+                 device: torch.device) -> None:
+        self.groups = groups
+        self.rows_per_group = rows_per_group
+        self.dtype = dtype
+        self.device = device
+        self.slots: list[dict[str, torch.Tensor]] = []
+        self.free: list[int] = []
+        self.layers: dict[int, tuple[int, int]] = {}  # first entry -> (slot, tag)
+        self.tag = 0
+        self.log_chunks: list[torch.Tensor] = []
+        self.log_used = 0
+
+    def begin(self, first: int) -> tuple[Optional[tuple[torch.Tensor, int]], int, int]:
+        """(previous (kv, tag) of the layer or None, reserved slot, its tag)."""
+        if self.free:
+            idx = self.free.pop()
+        else:
+            G = self.groups
+            self.slots.append({
+                "kv": torch.empty((2, G * self.rows_per_group, HEAD_DIM), dtype=self.dtype,
+                                  device=self.device),
+                "cu": torch.zeros(G + 1, dtype=torch.int32, device=self.device),
+            })
+            idx = len(self.slots) - 1
+        self.tag = self.tag + 1 if self.tag < 0xFFFFFFFF else 1
+        state = self.layers.get(first)
+        prev = None if state is None else (self.slots[state[0]]["kv"], state[1])
+        if prev is not None and prev[1] == self.tag:  # after 2^32 steps: skip one reuse
+            prev = None
+        return prev, idx, self.tag
+
+    def commit(self, first: int, idx: int, tag: int) -> None:
+        state = self.layers.get(first)
+        if state is not None:
+            self.free.append(state[0])
+        self.layers[first] = (idx, tag)
+
+    def abort(self, idx: int) -> None:
+        self.free.append(idx)
+
+    def log_row(self) -> tuple[torch.Tensor, int]:
+        """A zeroed [G, 2] (hit rows, miss rows) counter for one step."""
+        chunk, row = divmod(self.log_used, 1024)
+        if chunk == len(self.log_chunks):
+            self.log_chunks.append(torch.zeros((1024, self.groups, 2), dtype=torch.int32,
+                                               device=self.device))
+        self.log_used += 1
+        return self.log_chunks[chunk][row], self.log_used - 1
+
+    def log_counts(self) -> torch.Tensor:
+        if not self.log_chunks:
+            return torch.zeros((0, self.groups, 2), dtype=torch.int32)
+        return torch.cat(self.log_chunks).cpu()[: self.log_used]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for slot in self.slots for t in slot.values()) + \
+            sum(t.numel() * t.element_size() for t in self.log_chunks)
+
+
 class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
     """Quest B0 + INT4 QK + top-p with the dynamic budget, GQA-group execution.
 
@@ -556,7 +666,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
     def __init__(self, *, candidate_token_budget: int = 8192, top_p: float = 0.95,
                  matched_budget_fraction: float = 0.05, budget_mode: str = "dynamic",
                  gqa_groupwise_execution: bool = False, qk_backend: str = "pytorch",
-                 int4_group_size: int = 128, **kwargs: Any) -> None:
+                 int4_group_size: int = 128, previous_token_resident_cache: bool = False,
+                 **kwargs: Any) -> None:
         if candidate_token_budget <= 0:
             raise ValueError("candidate_token_budget must be positive")
         if not 0.0 < top_p <= 1.0:
@@ -579,6 +690,9 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             raise ValueError("GQA group-wise and per-Query-head flat execution are exclusive")
         if int4_group_size not in (32, 64, 128):
             raise ValueError("int4_group_size must be 32, 64 or 128")
+        _check_resident_options(bool(previous_token_resident_cache), kwargs)
+        if previous_token_resident_cache and not gqa_groupwise_execution:
+            raise ValueError("previous-token resident cache requires GQA group-wise execution")
         max_cache_len = int(kwargs["max_cache_len"])
         sink = int(kwargs.get("sink_tokens", 64))
         block = int(kwargs.get("block_size", 16))
@@ -606,6 +720,12 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         self._group_union_trace: list[dict[str, Any]] = []
         self._cached_group_positions: dict[int, torch.Tensor] = {}
         self._cached_per_q_positions: dict[int, tuple[torch.Tensor, ...]] = {}
+        self.previous_token_resident_cache = bool(previous_token_resident_cache)
+        self._reuse_pools: dict[int, _RowReusePool] = {}
+        self._reuse_trace_enabled = self.previous_token_resident_cache
+        self._reuse_trace: list[dict[str, Any]] = []
+        self._reuse_pending: list[tuple[dict[str, Any], int, int]] = []  # (row, G, log row)
+        self._row_map: Optional[torch.Tensor] = None  # [E, L] int64 (tag << 32) | kept row
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs: Optional[dict[str, Any]] = None):
@@ -659,6 +779,79 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         }
         self._layer_bufs[groups] = bufs
         return bufs
+
+    # ------------------------------------------------------------ row reuse --
+    def _reuse_pool(self, groups: int) -> _RowReusePool:
+        pool = self._reuse_pools.get(groups)
+        if pool is None:
+            per_group = self._buffers(0, groups)["per_group_cap"]
+            pool = _RowReusePool(groups, per_group, self.dtype, self.device)
+            self._reuse_pools[groups] = pool
+            if self._row_map is None:
+                self._row_map = torch.zeros((self.geometry.num_entries, self.geometry.max_cache_len),
+                                            dtype=torch.int64, device=self.device)
+        return pool
+
+    def _reuse_begin(self, first: int, G: int, old_length: int, staged: bool):
+        """Reserve this layer-step's kept rows: (RowReuse or None, slot or None)."""
+        if not self.previous_token_resident_cache:
+            return None, None
+        pool = self._reuse_pool(G)
+        prev, idx, tag = pool.begin(first)
+        counts = None
+        if self._reuse_trace_enabled:
+            counts, log_idx = pool.log_row()
+            self._reuse_pending.append(({
+                "decode_step": old_length - (self._prompt_length or 0) + 1,
+                "layer": first // G, "reuse_active": prev is not None}, G, log_idx))
+        kv = pool.slots[idx]["kv"]
+        rows = self._row_map[first: first + G]
+        kw = {} if prev is None else dict(prev_tag=prev[1], prev_k=prev[0][0], prev_v=prev[0][1])
+        if staged:
+            r = ops.row_reuse(rows, tag, row_counts=counts, **kw)
+        else:
+            per = pool.rows_per_group
+            r = ops.row_reuse(rows, tag, next_k=kv[0].view(G, per, HEAD_DIM),
+                              next_v=kv[1].view(G, per, HEAD_DIM), row_counts=counts, **kw)
+        return r, (idx, tag)
+
+    def _reuse_end(self, first: int, G: int, slot, ok: bool) -> None:
+        if slot is None:
+            return
+        pool = self._reuse_pools[G]
+        if ok:
+            pool.commit(first, *slot)
+        else:
+            pool.abort(slot[0])
+
+    def enable_resident_reuse_trace(self, enabled: bool = True) -> None:
+        """Record per-layer-step hit / miss row counts (on by default with the
+        previous-token resident cache; each recorded step adds two counter
+        atomics per warp, no host synchronisation)."""
+        self._reuse_trace_enabled = bool(enabled) and self.previous_token_resident_cache
+
+    def resident_reuse_trace(self) -> list[dict[str, Any]]:
+        """Per-layer-step hit / miss rows of the previous-token resident cache
+        (hi/twilight_offload_cache.py:803-823 and its trace rows at :2545-2557,
+        :3447-3470).  hit_rows counts the union rows read from the previous
+        step's device rows; the previous step's own token counts as a hit (the
+        reference reads it from the host).  Reading synchronises."""
+        if self._reuse_pending:
+            logs = {G: pool.log_counts() for G, pool in self._reuse_pools.items()}
+            item = torch.tensor([], dtype=self.dtype).element_size()
+            for row, G, idx in self._reuse_pending:
+                hits = int(logs[G][idx, :, 0].sum())
+                misses = int(logs[G][idx, :, 1].sum())
+                history = hits + misses
+                miss_bytes = 2 * misses * HEAD_DIM * item
+                row.update({
+                    "history_rows": history, "hit_rows": hits, "miss_rows": misses,
+                    "hit_ratio": hits / history if history else 0.0,
+                    "selected_kv_h2d_bytes": miss_bytes, "mapped_cpu_kv_read_bytes": miss_bytes,
+                    "resident_logical_bytes": 2 * history * HEAD_DIM * item})
+                self._reuse_trace.append(row)
+            self._reuse_pending.clear()
+        return list(self._reuse_trace)
 
     # -------------------------------------------------------------- selection --
     def prepare_layer_selection(self, *, entries: list[int], queries: list[torch.Tensor]) -> None:
@@ -773,19 +966,27 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
 
     def _gather_union(self, first: int, G: int, old_length: int, k_new, v_new):
         bufs = self._buffers(first, G)
-        slot = bufs["slot"]
-        bufs["slot"] = 1 - slot
-        out_k = bufs["flat"][slot, 0]
-        out_v = bufs["flat"][slot, 1]
-        cu = bufs["cu"][slot]
+        reuse, slot = self._reuse_begin(first, G, old_length, staged=True)
+        if slot is None:
+            cur = bufs["slot"]
+            bufs["slot"] = 1 - cur
+            out_k = bufs["flat"][cur, 0]
+            out_v = bufs["flat"][cur, 1]
+            cu = bufs["cu"][cur]
+        else:
+            kept = self._reuse_pools[G].slots[slot[0]]
+            out_k, out_v, cu = kept["kv"][0], kept["kv"][1], kept["cu"]
         start = self._phase_start()
-        _lib.check(_lib.load().tw_gather_union(
+        status = _lib.load().tw_gather_union(
             self._slab.key_device_ptr, self._slab.value_device_ptr, self._dirs.data_ptr(),
             self.geometry.num_entries, self.geometry.max_cache_len,
             first, G, old_length, bufs["union_pos"].data_ptr(), self.geometry.max_cache_len,
             bufs["union_count"].data_ptr(), k_new.data_ptr(), v_new.data_ptr(), HEAD_DIM,
             ops._kv_code(self.dtype), out_k.data_ptr(), out_v.data_ptr(), bufs["rows_cap"],
-            cu.data_ptr(), self._error_flag.data_ptr(), self._stream()), "gather_union")
+            cu.data_ptr(), self._error_flag.data_ptr(),
+            ctypes.byref(reuse) if reuse is not None else None, self._stream())
+        self._reuse_end(first, G, slot, status == _lib.TW_OK)
+        _lib.check(status, "gather_union")
         self._phase_end("h2d", start)
         return bufs, out_k, out_v, cu
 
@@ -810,16 +1011,15 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         total = sum(lengths)
         for g, entry in enumerate(entries):
             self._last_query_head_lengths[entry] = tuple([lengths[g]] * self.num_query_heads_per_kv)
-        self._record_group_step(entries, old_length, counts)
+        self._record_group_step(entries, old_length, counts, bufs["union_pos"])
         return (out_k[:total].view(total, 1, HEAD_DIM), out_v[:total].view(total, 1, HEAD_DIM), cu,
                 max(lengths), lengths)
 
-    def _record_group_step(self, entries, old_length, counts) -> None:
+    def _record_group_step(self, entries, old_length, counts, union_pos) -> None:
         decode_step = old_length - (self._prompt_length or 0) + 1
         if self._capture_selection_trace:
-            bufs = self._layer_bufs[len(entries)]
             for g, entry in enumerate(entries):
-                union = bufs["union_pos"][g, : counts[g]].to(torch.int64).cpu()
+                union = union_pos[g, : counts[g]].to(torch.int64).cpu()
                 self._cached_group_positions[entry] = union
                 self._group_union_trace.append({
                     "decode_step": decode_step, "entry": entry, "kv_head": g,
@@ -842,11 +1042,18 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         first, G = entries[0], len(entries)
         bufs = self._buffers(first, G)
         q = torch.stack([query[0, :, 0] for query in queries], dim=0).to(self.dtype).contiguous()
+        reuse, slot = self._reuse_begin(first, G, old_length, staged=False)
         start = self._phase_start()
-        out = ops.attend_union(self._slab, first, old_length, bufs["union_pos"], bufs["union_count"],
-                               k_new, v_new, q, min(bufs["per_group_cap"], old_length + 1),
-                               workspace=bufs["attn_workspace"], error_flag=self._error_flag, out=out,
-                               entry_dirs=self._dirs)
+        try:
+            out = ops.attend_union(self._slab, first, old_length, bufs["union_pos"],
+                                   bufs["union_count"], k_new, v_new, q,
+                                   min(bufs["per_group_cap"], old_length + 1),
+                                   workspace=bufs["attn_workspace"], error_flag=self._error_flag,
+                                   out=out, entry_dirs=self._dirs, reuse=reuse)
+        except Exception:
+            self._reuse_end(first, G, slot, False)
+            raise
+        self._reuse_end(first, G, slot, True)
         self._phase_end("attention", start)
         self._append_rows(first, G, old_length, k_new, v_new)
         return out
@@ -929,6 +1136,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             args.attn_workspace = bufs["attn_workspace"].data_ptr()
             args.attn_workspace_bytes = bufs["attn_workspace"].numel()
             bufs["layer_args"] = args
+        reuse, slot = self._reuse_begin(first, G, old_length, staged=False)
+        args.reuse = ctypes.addressof(reuse) if reuse is not None else None
         args.first_entry = first
         args.n_pages = candidate_pages
         args.b0_pages = b0_pages
@@ -942,8 +1151,10 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         args.out_dtype = ops.DTYPE_CODES[out.dtype]
         args.max_rows_per_group = min(bufs["per_group_cap"], old_length + 1)
         start = self._phase_start()
-        _lib.check(_lib.load().tw_twilight_decode_layer(ctypes.byref(args), self._stream()),
-                   "twilight_decode_layer")
+        status = _lib.load().tw_twilight_decode_layer(ctypes.byref(args), self._stream())
+        args.reuse = None
+        self._reuse_end(first, G, slot, status == _lib.TW_OK)
+        _lib.check(status, "twilight_decode_layer")
         self._phase_end("decode_layer", start)
         self._advance_layer(entries)
         return out
@@ -985,5 +1196,14 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             "twilight_gqa_groupwise_execution": self.gqa_groupwise_execution,
             "twilight_gqa_group_semantics": "exact union of the original per-Query-head selected token sets",
             "selection_boundary": "device-resident union; host reads only the union lengths",
+            "previous_token_resident_cache": self.previous_token_resident_cache,
+            "resident_cache_allocated_bytes": sum(p.nbytes() for p in self._reuse_pools.values())
+            + (self._row_map.numel() * 8 if self._row_map is not None else 0),
         })
         return snap
+
+    def _device_bytes(self) -> int:
+        extra = sum(p.nbytes() for p in self._reuse_pools.values())
+        if self._row_map is not None:
+            extra += self._row_map.numel() * self._row_map.element_size()
+        return super()._device_bytes() + extra

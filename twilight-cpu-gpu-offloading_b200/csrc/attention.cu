@@ -17,6 +17,7 @@ namespace tw {
 constexpr int kAttnThreads = 256;   // 8 warps
 constexpr int kAttnChunk = 128;     // rows per split CTA (16 per warp)
 constexpr int kVecPerRow = 16;      // 16-byte vectors per 128-dim fp16/bf16 row
+constexpr int kMergeChunk = 128;    // splits whose weights the merge stages at once
 
 struct AttnWorkspace {
   unsigned int* counters;  // [S]
@@ -67,8 +68,11 @@ struct FlatRows {
   const uint4* k;
   const uint4* v;
   const int32_t* cu;
+  __device__ __forceinline__ void keep(int, int, int64_t, int, const uint4&, const uint4&) const {}
   __device__ __forceinline__ int length(int s) const { return cu[s + 1] - cu[s]; }
-  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp) const {
+  __device__ __forceinline__ void count(int, int, int) const {}
+  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp,
+                                         int64_t&, int&, int&) const {
     const int64_t r = (int64_t)cu[s] + i;
     kp = k + r * kVecPerRow;
     vp = v + r * kVecPerRow;
@@ -93,18 +97,77 @@ struct UnionRows {
   const uint4* cur_k;
   const uint4* cur_v;
   int32_t* error_flag;
+  // previous-token row reuse (row_map null: every row from the slab, none kept)
+  unsigned long long* row_map;
+  int64_t map_stride;
+  unsigned prev_tag;
+  unsigned next_tag;
+  const uint4* prev_k;
+  const uint4* prev_v;
+  int64_t prev_rows;
+  uint4* next_k;
+  uint4* next_v;
+  int64_t rows_stride;
+  int32_t* row_counts;
+  // Adds this warp's hit / miss row counts to group s (lane 0 of the warp).
+  __device__ __forceinline__ void count(int s, int hits, int misses) const {
+    if (!row_counts) return;
+    hits = __reduce_add_sync(0xffffffffu, hits);
+    misses = __reduce_add_sync(0xffffffffu, misses);
+    if ((threadIdx.x & 31) == 0 && (hits | misses)) {
+      atomicAdd(&row_counts[2 * s], hits);
+      atomicAdd(&row_counts[2 * s + 1], misses);
+    }
+  }
   __device__ __forceinline__ int length(int s) const { return union_count[s] + 1; }
-  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp) const {
+  // Row i (position pos) of group s is kept for the next step: its vectors go
+  // to next_k / next_v and lane 0 of the half-warp records it in the row map
+  // (after the whole half-warp has read the entry in locate).
+  __device__ __forceinline__ void keep(int s, int i, int64_t pos, int l16, const uint4& kv,
+                                       const uint4& vv) const {
+    if (!row_map || i >= rows_stride) return;
+    const int64_t row = (int64_t)s * rows_stride + i;
+    next_k[row * kVecPerRow + l16] = kv;
+    next_v[row * kVecPerRow + l16] = vv;
+    if (l16 == 0)
+      row_map[(int64_t)s * map_stride + pos] =
+          ((unsigned long long)next_tag << 32) | (unsigned long long)row;
+  }
+  // The previous step's row holding position pos of group s, or -1.  Lane 0
+  // of the half-warp reads the entry and broadcasts it to the other 15.
+  __device__ __forceinline__ int64_t previous_row(int s, int64_t pos) const {
+    const unsigned half_mask = 0xffffu << (threadIdx.x & 16);
+    unsigned long long e = 0;
+    if ((threadIdx.x & 15) == 0) e = row_map[(int64_t)s * map_stride + pos];
+    e = __shfl_sync(half_mask, e, 0, 16);
+    const int64_t row = (int64_t)(e & 0xffffffffull);
+    return (prev_tag != 0 && (unsigned)(e >> 32) == prev_tag && row < prev_rows) ? row : -1;
+  }
+  // hits / misses count the history rows (not the current token) read from the
+  // previous rows / from the slab; only lane 0 of each half-warp counts.
+  __device__ __forceinline__ bool locate(int s, int i, const uint4*& kp, const uint4*& vp,
+                                         int64_t& pos, int& hits, int& misses) const {
     if (i >= union_count[s]) {
       kp = cur_k + (int64_t)s * kVecPerRow;
       vp = cur_v + (int64_t)s * kVecPerRow;
+      pos = old_length;
       return true;
     }
-    const int64_t pos = union_pos[(int64_t)s * pos_stride + i];
+    pos = union_pos[(int64_t)s * pos_stride + i];
     if (pos < 0 || pos >= old_length) {
       if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
       return false;
     }
+    if (row_map) {
+      const int64_t j = previous_row(s, pos);
+      if (j >= 0) {
+        kp = prev_k + j * kVecPerRow;
+        vp = prev_v + j * kVecPerRow;
+        hits += (threadIdx.x & 15) == 0;
+        return true;
+      }
+    }
+    misses += (threadIdx.x & 15) == 0;
     const int64_t e = (int64_t)first_entry + s;
     if (dirs) {
       kp = reinterpret_cast<const uint4*>(dirs[e]) + pos * kVecPerRow;
@@ -136,7 +199,8 @@ __device__ __forceinline__ float weight(float m, float M) {
 // block of rows are computed first (4-step shuffle reduction inside the
 // half-warp), then one online-softmax update per block.  The 8 warps are
 // combined in shared memory; with several splits the last split CTA of the
-// segment merges all partials in parallel (threads over (head, channel)).
+// segment merges all partials in parallel (threads over (head, float4 column,
+// split subset)).
 template <typename T, int R, typename OutT, typename Rows>
 __global__ void __launch_bounds__(kAttnThreads)
 attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_splits,
@@ -149,6 +213,7 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
   __shared__ float s_l[kWarps][R];
   __shared__ float s_o[kWarps][R][kHeadDim];
   __shared__ float s_M[R], s_L[R];
+  __shared__ float s_wt[kMergeChunk][R];
   __shared__ bool s_last;
 
   const int s = blockIdx.y;
@@ -179,6 +244,7 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
   }
 
   const int warp_row0 = split * kAttnChunk + warp * kRowsPerWarp;
+  int n_hit = 0, n_miss = 0;
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
     uint4 kr[kRowsPerHalf], vr[kRowsPerHalf];
@@ -190,10 +256,12 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
       kr[j] = make_uint4(0, 0, 0, 0);
       vr[j] = kr[j];
       const uint4 *kp, *vp;
-      if (i < seg_len && rows.locate(s, i, kp, vp)) {
+      int64_t pos;
+      if (i < seg_len && rows.locate(s, i, kp, vp, pos, n_hit, n_miss)) {
         kr[j] = __ldcs(kp + l16);
         vr[j] = __ldcs(vp + l16);
         ok[j] = true;
+        rows.keep(s, i, pos, l16, kr[j], vr[j]);
       }
     }
     float sc[kRowsPerHalf][R];
@@ -239,6 +307,8 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
       }
     }
   }
+
+  rows.count(s, n_hit, n_miss);
 
   // Combine the two half-warps (they hold disjoint rows, same channels).
 #pragma unroll
@@ -325,17 +395,57 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
     }
   }
   __syncthreads();
-  for (int idx = tid; idx < R * kHeadDim; idx += kAttnThreads) {
-    const int r = idx / kHeadDim;
-    const int d = idx % kHeadDim;
-    const float M = s_M[r];
-    float O = 0.0f;
-#pragma unroll 4
-    for (int j = 0; j < nsplit; ++j) {
-      const float f = weight(__ldcg(ml + ((int64_t)j * R + r) * 2), M);
-      O += f * __ldcg(po_all + ((int64_t)j * R + r) * kHeadDim + d);
+  // Weighted sum of the partial outputs.  A thread owns one float4 column
+  // (head r, channels 4*d4..4*d4+3) and every kTpp-th split of a chunk; the
+  // split weights of the chunk are computed once into shared memory, and the
+  // unrolled loop keeps 8 independent partial loads in flight per thread.  The
+  // kTpp threads of a column are adjacent lanes, summed by a shuffle tree.
+  constexpr int kPairs = R * (kHeadDim / 4);
+  constexpr int kTpp = kAttnThreads / kPairs >= 8 ? 8
+                       : kAttnThreads / kPairs >= 4 ? 4
+                       : kAttnThreads / kPairs >= 2 ? 2 : 1;
+  static_assert(kPairs <= kAttnThreads, "one float4 column per thread at most");
+  const int pair = tid / kTpp;
+  const int sub = tid % kTpp;
+  const bool has_pair = pair < kPairs;
+  const int pr = has_pair ? pair / (kHeadDim / 4) : 0;
+  const int d4 = pair % (kHeadDim / 4);
+  float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int j0 = 0; j0 < nsplit; j0 += kMergeChunk) {
+    const int n = min(kMergeChunk, nsplit - j0);
+    for (int idx = tid; idx < n * R; idx += kAttnThreads) {
+      const int jj = idx / R, rr = idx % R;
+      s_wt[jj][rr] = weight(__ldcg(ml + ((int64_t)(j0 + jj) * R + rr) * 2), s_M[rr]);
     }
-    write_final<OutT>(out, lse, s, r, R, d, M, s_L[r], O);
+    __syncthreads();
+    if (has_pair) {
+      const float4* col = reinterpret_cast<const float4*>(po_all + ((int64_t)j0 * R + pr) * kHeadDim) + d4;
+      const int64_t jstride = (int64_t)R * kHeadDim / 4;
+#pragma unroll 8
+      for (int jj = sub; jj < n; jj += kTpp) {
+        const float w = s_wt[jj][pr];
+        const float4 o = __ldcg(col + jj * jstride);
+        acc4.x = fmaf(w, o.x, acc4.x);
+        acc4.y = fmaf(w, o.y, acc4.y);
+        acc4.z = fmaf(w, o.z, acc4.z);
+        acc4.w = fmaf(w, o.w, acc4.w);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int off = kTpp / 2; off > 0; off >>= 1) {
+    acc4.x += __shfl_xor_sync(0xffffffffu, acc4.x, off);
+    acc4.y += __shfl_xor_sync(0xffffffffu, acc4.y, off);
+    acc4.z += __shfl_xor_sync(0xffffffffu, acc4.z, off);
+    acc4.w += __shfl_xor_sync(0xffffffffu, acc4.w, off);
+  }
+  if (has_pair && sub == 0) {
+    const float M = s_M[pr], L = s_L[pr];
+    write_final<OutT>(out, lse, s, pr, R, 4 * d4 + 0, M, L, acc4.x);
+    write_final<OutT>(out, lse, s, pr, R, 4 * d4 + 1, M, L, acc4.y);
+    write_final<OutT>(out, lse, s, pr, R, 4 * d4 + 2, M, L, acc4.z);
+    write_final<OutT>(out, lse, s, pr, R, 4 * d4 + 3, M, L, acc4.w);
   }
   if (tid == 0) ws.counters[s] = 0u;
 }
@@ -401,6 +511,7 @@ extern "C" int tw_decode_attention(const void* q, const void* k, const void* v,
   const size_t need = attn_ws_bytes(segments, heads_per_segment, max_splits, &ws,
                                     reinterpret_cast<char*>(workspace));
   if (max_splits > 1 && (!workspace || workspace_bytes < need)) return TW_ERR_CAPACITY;
+  if (max_splits > 1 && ((uintptr_t)workspace & 15) != 0) return TW_ERR_BAD_ARG;  // float4 merge
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == TW_F16) {
@@ -430,7 +541,7 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
                                const void* q, int heads_per_group, int max_rows_per_group,
                                int head_dim, int dtype, float softmax_scale, void* out,
                                int out_dtype, float* lse, int32_t* error_flag, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+                               size_t workspace_bytes, const tw_row_reuse* reuse, void* stream) {
   if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
   if ((!entry_dirs && (!slab_k || !slab_v)) || !union_pos || !union_count || !cur_k || !cur_v ||
       !q || !out || groups <= 0 || groups > 65535 || heads_per_group <= 0 || first_entry < 0 ||
@@ -449,10 +560,46 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
   const size_t need = attn_ws_bytes(groups, heads_per_group, max_splits, &ws,
                                     reinterpret_cast<char*>(workspace));
   if (max_splits > 1 && (!workspace || workspace_bytes < need)) return TW_ERR_CAPACITY;
+  if (max_splits > 1 && ((uintptr_t)workspace & 15) != 0) return TW_ERR_BAD_ARG;  // float4 merge
   UnionRows rows{(const uint4*)slab_k, (const uint4*)slab_v,
                  (const unsigned long long*)entry_dirs, n_entries, max_len, first_entry,
                  old_length, union_pos, pos_stride, union_count, (const uint4*)cur_k,
-                 (const uint4*)cur_v, error_flag};
+                 (const uint4*)cur_v, error_flag,
+                 nullptr, 0, 0u, 0u, nullptr, nullptr, 0, nullptr, nullptr, 0, nullptr};
+  if (reuse) {
+    const size_t next_bytes = (size_t)groups * reuse->rows_stride * kHeadDim * 2;
+    const size_t prev_bytes = (size_t)reuse->prev_rows * kHeadDim * 2;
+    auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+      const char* x = (const char*)a;
+      const char* y = (const char*)b;
+      return x < y + nb && y < x + na;
+    };
+    if (!reuse->row_map || reuse->map_stride <= old_length || !reuse->next_k || !reuse->next_v ||
+        reuse->rows_stride < max_rows_per_group || reuse->next_tag == 0 ||
+        reuse->next_tag == reuse->prev_tag ||
+        (((uintptr_t)reuse->next_k | (uintptr_t)reuse->next_v) & 15) != 0 ||
+        overlap(reuse->next_k, next_bytes, reuse->next_v, next_bytes))
+      return TW_ERR_BAD_ARG;
+    if (reuse->prev_tag != 0 &&
+        (!reuse->prev_k || !reuse->prev_v || reuse->prev_rows <= 0 ||
+         (((uintptr_t)reuse->prev_k | (uintptr_t)reuse->prev_v) & 15) != 0 ||
+         overlap(reuse->prev_k, prev_bytes, reuse->next_k, next_bytes) ||
+         overlap(reuse->prev_k, prev_bytes, reuse->next_v, next_bytes) ||
+         overlap(reuse->prev_v, prev_bytes, reuse->next_k, next_bytes) ||
+         overlap(reuse->prev_v, prev_bytes, reuse->next_v, next_bytes)))
+      return TW_ERR_BAD_ARG;
+    rows.row_map = (unsigned long long*)reuse->row_map;
+    rows.map_stride = reuse->map_stride;
+    rows.prev_tag = reuse->prev_tag;
+    rows.next_tag = reuse->next_tag;
+    rows.prev_k = (const uint4*)reuse->prev_k;
+    rows.prev_v = (const uint4*)reuse->prev_v;
+    rows.prev_rows = reuse->prev_tag != 0 ? reuse->prev_rows : 0;
+    rows.next_k = (uint4*)reuse->next_k;
+    rows.next_v = (uint4*)reuse->next_v;
+    rows.rows_stride = reuse->rows_stride;
+    rows.row_counts = reuse->row_counts;
+  }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == TW_F16) {

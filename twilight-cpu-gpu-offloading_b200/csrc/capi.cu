@@ -37,7 +37,7 @@ int launch_int4_qk(const void* q, int q_dtype, const uint8_t* packed, const void
 extern "C" int tw_attend_union(const void*, const void*, const uint64_t*, int64_t, int64_t, int,
                                int, int64_t, const int32_t*, int64_t, const int32_t*, const void*,
                                const void*, const void*, int, int, int, int, float, void*, int,
-                               float*, int32_t*, void*, size_t, void*);
+                               float*, int32_t*, void*, size_t, const tw_row_reuse*, void*);
 extern "C" int tw_append_token(void*, void*, const uint64_t*, int64_t, int64_t, int, int, int64_t,
                                const void*, const void*, int, int, int, int, void*, void*, int64_t,
                                uint8_t*, void*, void*, int, void*);
@@ -58,7 +58,7 @@ extern "C" const char* tw_status_string(int status) {
 
 extern "C" int tw_last_cuda_error(void) { return g_last_cuda_error; }
 
-extern "C" int tw_abi_version(void) { return 1; }
+extern "C" int tw_abi_version(void) { return 2; }
 
 extern "C" int tw_host_alloc_mapped(size_t bytes, void** host_ptr, void** device_ptr) {
   if (!host_ptr || !device_ptr || bytes == 0) return TW_ERR_BAD_ARG;
@@ -147,6 +147,8 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
 
 extern "C" size_t tw_decode_layer_args_size(void) { return sizeof(tw_decode_layer_args); }
 
+extern "C" size_t tw_row_reuse_size(void) { return sizeof(tw_row_reuse); }
+
 extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* stream) {
   if (!a) return TW_ERR_BAD_ARG;
   if (a->dtype != TW_F16 && a->dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
@@ -189,7 +191,8 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
                        a->union_pos, a->pos_stride, a->union_count, a->k_new, a->v_new, a->q, R,
                        a->max_rows_per_group, kHeadDim, a->dtype,
                        1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
-                       a->error_flag, a->attn_workspace, a->attn_workspace_bytes, stream);
+                       a->error_flag, a->attn_workspace, a->attn_workspace_bytes, a->reuse,
+                       stream);
   if (rc != TW_OK || !a->append) return rc;
   return tw_append_token(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
                          a->first_entry, G, a->old_length,

@@ -74,6 +74,31 @@ __device__ __forceinline__ void entry_rows(const uint4* slab_k, const uint4* sla
   }
 }
 
+// Previous-token row reuse for the union gather: a direct-addressed row map
+// per group ((tag << 32) | row per position) points into the previous step's
+// kept rows; this gather keeps its own output rows and records them with
+// next_tag.  row_map == nullptr: no reuse.
+struct GatherReuse {
+  unsigned long long* row_map;
+  int64_t map_stride;
+  unsigned prev_tag;
+  unsigned next_tag;
+  const uint4* k;
+  const uint4* v;
+  int64_t prev_rows;
+  int32_t* row_counts;
+  // Previous row of position p of group g, or -1; lane 0 of the 16-lane row
+  // group reads the entry and broadcasts it.
+  __device__ __forceinline__ int64_t row_of(int g, int64_t p) const {
+    const unsigned half_mask = 0xffffu << (threadIdx.x & 16);
+    unsigned long long e = 0;
+    if ((threadIdx.x & 15) == 0) e = row_map[(int64_t)g * map_stride + p];
+    e = __shfl_sync(half_mask, e, 0, 16);
+    const int64_t row = (int64_t)(e & 0xffffffffull);
+    return (prev_tag != 0 && (unsigned)(e >> 32) == prev_tag && row < prev_rows) ? row : -1;
+  }
+};
+
 template <int kVec>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
@@ -83,8 +108,10 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
                     const int32_t* __restrict__ union_count, const uint4* __restrict__ cur_k,
                     const uint4* __restrict__ cur_v, uint4* __restrict__ out_k,
                     uint4* __restrict__ out_v, int64_t rows_cap, int32_t* __restrict__ cu_seqlens,
-                    int32_t* error_flag) {
+                    int32_t* error_flag, GatherReuse prev) {
+  static_assert(kVec == 16, "a row is one 16-lane half-warp");
   __shared__ int64_t off[kMaxGroups + 1];
+  __shared__ int s_hits[kMaxGroups], s_misses[kMaxGroups];
   if (threadIdx.x == 0) {
     int64_t acc = 0;
     for (int g = 0; g < groups; ++g) {
@@ -97,6 +124,10 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
       if (acc > rows_cap && error_flag) atomicExch(error_flag, TW_ERR_CAPACITY);
     }
   }
+  if (threadIdx.x < kMaxGroups) {
+    s_hits[threadIdx.x] = 0;
+    s_misses[threadIdx.x] = 0;
+  }
   __syncthreads();
   const int64_t total = min(off[groups], rows_cap);
   constexpr int rows_per_cta = kGatherThreads / kVec;
@@ -106,13 +137,16 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
   for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + sub_row; base < total;
        base += stride * kGatherUnroll) {
     uint4 kv[kGatherUnroll], vv[kGatherUnroll];
-    int64_t t[kGatherUnroll];
+    int64_t t[kGatherUnroll], tpos[kGatherUnroll];
+    int tg[kGatherUnroll];
 #pragma unroll
     for (int u = 0; u < kGatherUnroll; ++u) {
       t[u] = base + u * stride;
+      tpos[u] = -1;
       if (t[u] >= total) continue;
       int g = 0;
       while (g + 1 < groups && off[g + 1] <= t[u]) ++g;
+      tg[u] = g;
       const int64_t i = t[u] - off[g];
       const int32_t cnt = union_count[g];
       if (i < cnt) {
@@ -122,12 +156,23 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
           kv[u] = make_uint4(0, 0, 0, 0);
           vv[u] = kv[u];
         } else {
-          const uint4 *kb, *vb;
-          entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec, kb, vb);
-          kv[u] = __ldcs(kb + pos * kVec + col);
-          vv[u] = __ldcs(vb + pos * kVec + col);
+          tpos[u] = pos;
+          const int64_t j = prev.row_map ? prev.row_of(g, pos) : -1;
+          if (j >= 0) {
+            kv[u] = __ldcs(prev.k + j * kVec + col);
+            vv[u] = __ldcs(prev.v + j * kVec + col);
+            if (col == 0 && prev.row_counts) atomicAdd(&s_hits[g], 1);
+          } else {
+            const uint4 *kb, *vb;
+            entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec,
+                       kb, vb);
+            kv[u] = __ldcs(kb + pos * kVec + col);
+            vv[u] = __ldcs(vb + pos * kVec + col);
+            if (col == 0 && prev.row_counts) atomicAdd(&s_misses[g], 1);
+          }
         }
       } else {
+        tpos[u] = old_length;
         kv[u] = cur_k[(int64_t)g * kVec + col];
         vv[u] = cur_v[(int64_t)g * kVec + col];
       }
@@ -137,6 +182,16 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
       if (t[u] >= total) continue;
       out_k[t[u] * kVec + col] = kv[u];
       out_v[t[u] * kVec + col] = vv[u];
+      if (prev.row_map && col == 0 && tpos[u] >= 0)
+        prev.row_map[(int64_t)tg[u] * prev.map_stride + tpos[u]] =
+            ((unsigned long long)prev.next_tag << 32) | (unsigned long long)t[u];
+    }
+  }
+  if (prev.row_counts) {
+    __syncthreads();
+    if (threadIdx.x < groups && (s_hits[threadIdx.x] | s_misses[threadIdx.x])) {
+      atomicAdd(&prev.row_counts[2 * threadIdx.x], s_hits[threadIdx.x]);
+      atomicAdd(&prev.row_counts[2 * threadIdx.x + 1], s_misses[threadIdx.x]);
     }
   }
 }
@@ -245,7 +300,7 @@ extern "C" int tw_gather_union(const void* slab_k, const void* slab_v,
                                const int32_t* union_count, const void* cur_k, const void* cur_v,
                                int head_dim, int dtype, void* out_k, void* out_v,
                                int64_t rows_cap, int32_t* cu_seqlens, int32_t* error_flag,
-                               void* stream) {
+                               const tw_row_reuse* reuse, void* stream) {
   if (head_dim != kHeadDim || (dtype != TW_F16 && dtype != TW_BF16)) return TW_ERR_UNSUPPORTED;
   if ((!entry_dirs && (!slab_k || !slab_v)) || !union_pos || !union_count || !cur_k || !cur_v ||
       !out_k || !out_v || !cu_seqlens || groups <= 0 || groups > kMaxGroups || first_entry < 0 ||
@@ -255,13 +310,43 @@ extern "C" int tw_gather_union(const void* slab_k, const void* slab_v,
   if (!aligned16(slab_k) || !aligned16(slab_v) || !aligned16(cur_k) || !aligned16(cur_v) ||
       !aligned16(out_k) || !aligned16(out_v))
     return TW_ERR_BAD_ARG;
+  GatherReuse prev{nullptr, 0, 0u, 0u, nullptr, nullptr, 0, nullptr};
+  if (reuse) {
+    // the kept rows are out_k / out_v themselves (packed)
+    const size_t out_bytes = (size_t)rows_cap * kHeadDim * 2;
+    const size_t prev_bytes = (size_t)reuse->prev_rows * kHeadDim * 2;
+    auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+      const char* x = (const char*)a;
+      const char* y = (const char*)b;
+      return x < y + nb && y < x + na;
+    };
+    if (reuse->next_k || reuse->next_v || !reuse->row_map || reuse->map_stride <= old_length ||
+        reuse->next_tag == 0 || reuse->next_tag == reuse->prev_tag || rows_cap > 0xffffffffll)
+      return TW_ERR_BAD_ARG;
+    if (reuse->prev_tag != 0 &&
+        (!reuse->prev_k || !reuse->prev_v || reuse->prev_rows <= 0 ||
+         !aligned16(reuse->prev_k) || !aligned16(reuse->prev_v) ||
+         overlap(reuse->prev_k, prev_bytes, out_k, out_bytes) ||
+         overlap(reuse->prev_k, prev_bytes, out_v, out_bytes) ||
+         overlap(reuse->prev_v, prev_bytes, out_k, out_bytes) ||
+         overlap(reuse->prev_v, prev_bytes, out_v, out_bytes)))
+      return TW_ERR_BAD_ARG;
+    prev.row_map = (unsigned long long*)reuse->row_map;
+    prev.map_stride = reuse->map_stride;
+    prev.prev_tag = reuse->prev_tag;
+    prev.next_tag = reuse->next_tag;
+    prev.k = (const uint4*)reuse->prev_k;
+    prev.v = (const uint4*)reuse->prev_v;
+    prev.prev_rows = reuse->prev_tag != 0 ? reuse->prev_rows : 0;
+    prev.row_counts = reuse->row_counts;
+  }
   constexpr int kVec = kHeadDim * 2 / 16;  // 16 vectors per 256-byte row
   const int grid = gather_grid(rows_cap, kGatherThreads / kVec);
   gather_union_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
       (const uint4*)slab_k, (const uint4*)slab_v, (const unsigned long long*)entry_dirs,
       n_entries, max_len, first_entry, groups, old_length,
       union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
-      (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens, error_flag);
+      (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens, error_flag, prev);
   return check_launch();
 }
 

@@ -213,11 +213,13 @@ def attend_union(slab, first_entry: int, old_length: int, union_pos: torch.Tenso
                  error_flag: torch.Tensor, out: torch.Tensor | None = None,
                  out_dtype: torch.dtype | None = None, lse: torch.Tensor | None = None,
                  softmax_scale: float | None = None,
-                 entry_dirs: torch.Tensor | None = None) -> torch.Tensor:
+                 entry_dirs: torch.Tensor | None = None,
+                 reuse: "_lib.RowReuse | None" = None) -> torch.Tensor:
     """Fused union gather + decode attention straight from the mapped slab (or,
     with entry_dirs [2, E] int64 row-0 addresses, from each entry's placement).
     q [G,R,D] (K/V dtype), cur_k/cur_v [G,D], union_pos [G, stride] int32,
-    union_count [G] int32 -> out [G,R,D]."""
+    union_count [G] int32 -> out [G,R,D].  reuse (row_reuse()): read rows of
+    the previous step from device memory and keep this step's rows."""
     _cuda(union_pos, union_count, cur_k, cur_v, q, workspace, error_flag, out, lse)
     G, R, D = q.shape
     out_dtype = out_dtype or q.dtype
@@ -230,6 +232,40 @@ def attend_union(slab, first_entry: int, old_length: int, union_pos: torch.Tenso
         old_length, _ptr(union_pos), union_pos.shape[-1], _ptr(union_count), _ptr(cur_k),
         _ptr(cur_v), _ptr(q), R, int(max_rows_per_group), D, _kv_code(q.dtype),
         ctypes.c_float(scale), _ptr(out), DTYPE_CODES[out.dtype], _ptr(lse), _ptr(error_flag),
-        _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(q.device)),
+        _ptr(workspace), workspace.numel() * workspace.element_size(),
+        ctypes.byref(reuse) if reuse is not None else None, _stream(q.device)),
         "attend_union")
     return out
+
+
+def row_reuse(row_map: torch.Tensor, next_tag: int, *, next_k: torch.Tensor | None = None,
+              next_v: torch.Tensor | None = None, prev_tag: int = 0,
+              prev_k: torch.Tensor | None = None, prev_v: torch.Tensor | None = None,
+              row_counts: torch.Tensor | None = None) -> "_lib.RowReuse":
+    """tw_row_reuse for attend_union / decode_layer (next_k / next_v
+    [G, S, D] receive this step's rows) or tw_gather_union (no next rows: its
+    output is kept).  row_map [G, stride] int64 (zeroed before first use) maps
+    positions to (tag << 32) | row of the kept rows; prev_k / prev_v [rows, D]
+    (any leading shape) are the rows kept under prev_tag (0: none).
+    row_counts [G, 2] int32 accumulates (hit rows, miss rows)."""
+    _cuda(row_map, next_k, next_v, prev_k, prev_v, row_counts)
+    if row_map.dtype != torch.int64 or row_map.dim() != 2:
+        raise ValueError("row_map must be int64 [G, stride]")
+    r = _lib.RowReuse()
+    r.row_map, r.map_stride = row_map.data_ptr(), row_map.shape[1]
+    r.next_tag, r.prev_tag = int(next_tag), int(prev_tag)
+    if next_k is not None or next_v is not None:
+        if next_k is None or next_v is None or next_k.dim() != 3 or next_k.shape != next_v.shape:
+            raise ValueError("next_k / next_v must be [G, S, D]")
+        r.next_k, r.next_v = next_k.data_ptr(), next_v.data_ptr()
+        r.rows_stride = next_k.shape[1]
+    if prev_tag:
+        if prev_k is None or prev_v is None or prev_k.shape != prev_v.shape:
+            raise ValueError("prev_tag needs prev_k and prev_v of one shape")
+        r.prev_k, r.prev_v = prev_k.data_ptr(), prev_v.data_ptr()
+        r.prev_rows = prev_k.numel() // prev_k.shape[-1]
+    if row_counts is not None:
+        if row_counts.dtype != torch.int32 or row_counts.shape != (row_map.shape[0], 2):
+            raise ValueError("row_counts must be int32 [G, 2]")
+        r.row_counts = row_counts.data_ptr()
+    return r
