@@ -90,6 +90,7 @@ class QuestTopKOffloadedCache:
                                      max_cache_len=max_cache_len, head_dim=head_dim)
         self.dtype = dtype
         self.device = device
+        self._device_index = device.index
         self.allocated_capacity = max_cache_len
         self.num_query_heads_per_kv = num_query_heads_per_kv
         self.sink_tokens = sink_tokens
@@ -133,6 +134,7 @@ class QuestTopKOffloadedCache:
         self._page_min = torch.empty((E, self.page_capacity, D), dtype=dtype, device=device)
         self._page_max = torch.empty_like(self._page_min)
         self._meta_pages = [0] * E  # prompt pages with metadata per entry
+        self._meta_version = 0      # bumped whenever _meta_pages changes
         max_pages = math.ceil(max(0, max_cache_len - sink_tokens) / block_size)
         self.max_selected_tokens_per_query_head = min(
             max_cache_len,
@@ -256,6 +258,7 @@ class QuestTopKOffloadedCache:
                 self._page_min[entry].data_ptr() + off, self._page_max[entry].data_ptr() + off,
                 self.page_capacity * HEAD_DIM, self._stream()), "quest_page_metadata")
         self._meta_pages[entry] = complete
+        self._meta_version += 1
 
     def _schedule_d2h(self, entry: int, start: int, key_states, value_states) -> None:
         n = int(key_states.shape[-2])
@@ -606,6 +609,16 @@ class _RowReusePool:
         self.tag = 0
         self.log_chunks: list[torch.Tensor] = []
         self.log_used = 0
+        self.slot_ptrs: list[tuple[int, int]] = []  # (K rows, V rows) device addresses
+
+    def log_row_ptr(self) -> tuple[int, int]:
+        """log_row as a device address: (address of the [G, 2] counter, log index)."""
+        chunk, row = divmod(self.log_used, 1024)
+        if chunk == len(self.log_chunks):
+            self.log_chunks.append(torch.zeros((1024, self.groups, 2), dtype=torch.int32,
+                                               device=self.device))
+        self.log_used += 1
+        return self.log_chunks[chunk].data_ptr() + row * self.groups * 8, self.log_used - 1
 
     def begin(self, first: int) -> tuple[Optional[tuple[torch.Tensor, int]], int, int]:
         """(previous (kv, tag) of the layer or None, reserved slot, its tag)."""
@@ -613,11 +626,13 @@ class _RowReusePool:
             idx = self.free.pop()
         else:
             G = self.groups
+            kv = torch.empty((2, G * self.rows_per_group, HEAD_DIM), dtype=self.dtype,
+                             device=self.device)
             self.slots.append({
-                "kv": torch.empty((2, G * self.rows_per_group, HEAD_DIM), dtype=self.dtype,
-                                  device=self.device),
+                "kv": kv,
                 "cu": torch.zeros(G + 1, dtype=torch.int32, device=self.device),
             })
+            self.slot_ptrs.append((kv[0].data_ptr(), kv[1].data_ptr()))
             idx = len(self.slots) - 1
         self.tag = self.tag + 1 if self.tag < 0xFFFFFFFF else 1
         state = self.layers.get(first)
@@ -726,6 +741,7 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         self._reuse_trace: list[dict[str, Any]] = []
         self._reuse_pending: list[tuple[dict[str, Any], int, int]] = []  # (row, G, log row)
         self._row_map: Optional[torch.Tensor] = None  # [E, L] int64 (tag << 32) | kept row
+        self._plans: dict[tuple[int, ...], dict[str, Any]] = {}
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
                cache_kwargs: Optional[dict[str, Any]] = None):
@@ -1066,13 +1082,14 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         attend_layer.  queries may be the reference's list of [1, R, 1, D]
         tensors or one [G, R, D] tensor; key_states / value_states lists of
         [1, 1, 1, D] or [G, D] tensors."""
-        G = len(entries)
+        key = tuple(entries)
+        plan = self._plans.get(key)
+        if plan is None:
+            plan = self._make_plan(entries)
+        G, first = plan["G"], plan["first"]
         R = self.num_query_heads_per_kv
-        first = _contiguous_entries(entries)
         if isinstance(queries, torch.Tensor):
             q = queries
-            if tuple(q.shape) != (G, R, HEAD_DIM):
-                raise ValueError("queries must be [G, R, D]")
         else:
             self._validate_layer(entries, queries)
             q = torch.stack([query[0, :, 0] for query in queries], dim=0)
@@ -1080,84 +1097,151 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             [k.reshape(1, HEAD_DIM) for k in key_states], dim=0)
         v_new = value_states if isinstance(value_states, torch.Tensor) else torch.cat(
             [v.reshape(1, HEAD_DIM) for v in value_states], dim=0)
-        if tuple(k_new.shape) != (G, HEAD_DIM) or k_new.shape != v_new.shape:
-            raise ValueError("new K/V must be [G, D]")
-        for t in (q, k_new, v_new):
-            if t.dtype != self.dtype or not t.is_cuda or not t.is_contiguous():
-                raise ValueError("queries and new K/V must be contiguous CUDA tensors of the K/V dtype")
-        old_length = self._layer_old_length(entries)
+        dt = self.dtype
+        if (q.shape != plan["q_shape"] or k_new.shape != plan["kv_shape"]
+                or v_new.shape != plan["kv_shape"]):
+            raise ValueError("queries must be [G, R, D] and new K/V [G, D]")
+        if (q.dtype != dt or k_new.dtype != dt or v_new.dtype != dt
+                or not (q.is_cuda and k_new.is_cuda and v_new.is_cuda)
+                or not (q.is_contiguous() and k_new.is_contiguous() and v_new.is_contiguous())):
+            raise ValueError("queries and new K/V must be contiguous CUDA tensors of the K/V dtype")
+        old_length = self._bookkeeping.check_block(first, G)
         if self._prompt_length is None:
             raise RuntimeError("Twilight prompt metadata is missing")
-        w = self._window(old_length)
-        candidate_pages = min(w["candidate_pages"], self._metadata_pages(entries, old_length))
-        b0_pages = min(candidate_pages, max(1, math.ceil(self.candidate_token_budget / self.block_size)),
-                       self.b0_page_capacity)
-        if candidate_pages == 0 or b0_pages == 0 or self._tracing():
+        sink_end = min(self.sink_tokens, old_length)
+        recent_start = max(sink_end, old_length - max(0, self.recent_tokens - 1))
+        if self.incremental_page_metadata:
+            meta = max(0, old_length - self.sink_tokens) // self.block_size
+        else:
+            if plan["meta_version"] != self._meta_version:
+                plan["meta_pages"] = min(self._meta_pages[e] for e in entries)
+                plan["meta_version"] = self._meta_version
+            meta = plan["meta_pages"]
+        candidate_pages = min((recent_start - sink_end) // self.block_size, meta)
+        b0_pages = min(candidate_pages, plan["b0_budget"])
+        if candidate_pages <= 0 or b0_pages <= 0 or self._tracing():
             # protected-only windows and traced runs take the two-call path
             self.prepare_layer_selection(entries=entries, queries=[q[g].view(1, R, 1, HEAD_DIM) for g in range(G)])
             return self.attend_layer(key_states=[k_new[g].view(1, 1, 1, HEAD_DIM) for g in range(G)],
                                      value_states=[v_new[g].view(1, 1, 1, HEAD_DIM) for g in range(G)],
                                      queries=[q[g].view(1, R, 1, HEAD_DIM) for g in range(G)],
                                      entries=entries, out=out)
-        bufs = self._buffers(first, G)
         if out is None:
-            out = torch.empty((G, R, HEAD_DIM), dtype=self.dtype, device=self.device)
-        args = bufs.get("layer_args")
-        if args is None:
-            args = _lib.DecodeLayerArgs()
-            args.slab_k = self._slab.key_device_ptr
-            args.slab_v = self._slab.value_device_ptr
-            args.entry_dirs = self._dirs.data_ptr()
-            args.n_entries = self.geometry.num_entries
-            args.max_len = self.geometry.max_cache_len
-            args.groups = G
-            args.heads_per_group = R
-            args.dtype = ops._kv_code(self.dtype)
-            args.page_min = self._page_min.data_ptr()
-            args.page_max = self._page_max.data_ptr()
-            args.page_capacity = self.page_capacity
-            args.packed = self._packed.data_ptr()
-            args.scale = self._scale.data_ptr()
-            args.minimum = self._minimum.data_ptr()
-            args.int4_group_size = self.int4_group_size
-            args.sink = self.sink_tokens
-            args.block_size = self.block_size
-            args.top_p = self.top_p
-            args.append = 1
-            args.pages = bufs["pages"].data_ptr()
-            args.union_pos = bufs["union_pos"].data_ptr()
-            args.pos_stride = self.geometry.max_cache_len
-            args.union_count = bufs["union_count"].data_ptr()
-            args.head_count = bufs["head_count"].data_ptr()
-            args.head_pos = None
-            args.error_flag = self._error_flag.data_ptr()
-            args.select_workspace = bufs["workspace"].data_ptr()
-            args.select_workspace_bytes = bufs["workspace"].numel()
-            args.attn_workspace = bufs["attn_workspace"].data_ptr()
-            args.attn_workspace_bytes = bufs["attn_workspace"].numel()
-            bufs["layer_args"] = args
-        reuse, slot = self._reuse_begin(first, G, old_length, staged=False)
-        args.reuse = ctypes.addressof(reuse) if reuse is not None else None
-        args.first_entry = first
+            out = torch.empty(plan["q_shape"], dtype=dt, device=self.device)
+        elif out.shape != plan["q_shape"] or not out.is_cuda or not out.is_contiguous():
+            raise ValueError("out must be a contiguous CUDA tensor [G, R, D]")
+        args = plan["args"]
         args.n_pages = candidate_pages
         args.b0_pages = b0_pages
         args.old_length = old_length
-        args.sink_end = w["sink_end"]
-        args.recent_start = w["recent_start"]
+        args.sink_end = sink_end
+        args.recent_start = recent_start
         args.q = q.data_ptr()
         args.k_new = k_new.data_ptr()
         args.v_new = v_new.data_ptr()
         args.out = out.data_ptr()
         args.out_dtype = ops.DTYPE_CODES[out.dtype]
-        args.max_rows_per_group = min(bufs["per_group_cap"], old_length + 1)
-        start = self._phase_start()
-        status = _lib.load().tw_twilight_decode_layer(ctypes.byref(args), self._stream())
-        args.reuse = None
-        self._reuse_end(first, G, slot, status == _lib.TW_OK)
-        _lib.check(status, "twilight_decode_layer")
-        self._phase_end("decode_layer", start)
-        self._advance_layer(entries)
+        args.max_rows_per_group = min(plan["per_group_cap"], old_length + 1)
+        pool = plan["pool"]
+        if pool is not None:
+            reuse = plan["reuse"]
+            prev, idx, tag = pool.begin(first)
+            reuse.next_tag = tag
+            reuse.next_k, reuse.next_v = pool.slot_ptrs[idx]
+            if prev is None:
+                reuse.prev_tag = 0
+                reuse.prev_k = reuse.prev_v = None
+            else:
+                reuse.prev_tag = prev[1]
+                reuse.prev_k, reuse.prev_v = pool.slot_ptrs[pool.layers[first][0]]
+            if self._reuse_trace_enabled:
+                counts, log_idx = pool.log_row_ptr()
+                reuse.row_counts = counts
+                self._reuse_pending.append(({
+                    "decode_step": old_length - (self._prompt_length or 0) + 1,
+                    "layer": first // G, "reuse_active": prev is not None}, G, log_idx))
+            else:
+                reuse.row_counts = None
+        start = self._phase_start() if self.metrics_enabled else None
+        status = plan["fn"](plan["args_ref"], torch._C._cuda_getCurrentRawStream(self._device_index))
+        if pool is not None:
+            if status == _lib.TW_OK:
+                pool.commit(first, idx, tag)
+            else:
+                pool.abort(idx)
+        if status != _lib.TW_OK:
+            _lib.check(status, "twilight_decode_layer")
+        if start is not None:
+            self._phase_end("decode_layer", start)
+        self._bookkeeping.commit_block(first, G, old_length)
+        self._initialized[first:first + G] = plan["initialized"]
+        self._seen_tokens = self._bookkeeping.seen_tokens
         return out
+
+    def _make_plan(self, entries: list[int]) -> dict[str, Any]:
+        """Per-layer constants of decode_layer: the argument struct with its fixed
+        fields, buffer addresses, shapes and the library entry point."""
+        G = len(entries)
+        if G == 0 or len(set(entries)) != G:
+            raise ValueError("layer entries must be non-empty and unique")
+        first = _contiguous_entries(entries)
+        if first + G > self.geometry.num_entries:
+            raise ValueError("layer entries outside the cache")
+        R = self.num_query_heads_per_kv
+        bufs = self._buffers(first, G)
+        args = _lib.DecodeLayerArgs()
+        args.slab_k = self._slab.key_device_ptr
+        args.slab_v = self._slab.value_device_ptr
+        args.entry_dirs = self._dirs.data_ptr()
+        args.n_entries = self.geometry.num_entries
+        args.max_len = self.geometry.max_cache_len
+        args.first_entry = first
+        args.groups = G
+        args.heads_per_group = R
+        args.dtype = ops._kv_code(self.dtype)
+        args.page_min = self._page_min.data_ptr()
+        args.page_max = self._page_max.data_ptr()
+        args.page_capacity = self.page_capacity
+        args.packed = self._packed.data_ptr()
+        args.scale = self._scale.data_ptr()
+        args.minimum = self._minimum.data_ptr()
+        args.int4_group_size = self.int4_group_size
+        args.sink = self.sink_tokens
+        args.block_size = self.block_size
+        args.top_p = self.top_p
+        args.append = 1
+        args.pages = bufs["pages"].data_ptr()
+        args.union_pos = bufs["union_pos"].data_ptr()
+        args.pos_stride = self.geometry.max_cache_len
+        args.union_count = bufs["union_count"].data_ptr()
+        args.head_count = bufs["head_count"].data_ptr()
+        args.head_pos = None
+        args.error_flag = self._error_flag.data_ptr()
+        args.select_workspace = bufs["workspace"].data_ptr()
+        args.select_workspace_bytes = bufs["workspace"].numel()
+        args.attn_workspace = bufs["attn_workspace"].data_ptr()
+        args.attn_workspace_bytes = bufs["attn_workspace"].numel()
+        pool = reuse = None
+        if self.previous_token_resident_cache:
+            pool = self._reuse_pool(G)
+            reuse = _lib.RowReuse()
+            reuse.row_map = self._row_map[first].data_ptr()
+            reuse.map_stride = self.geometry.max_cache_len
+            reuse.prev_rows = G * pool.rows_per_group
+            reuse.rows_stride = pool.rows_per_group
+            args.reuse = ctypes.addressof(reuse)
+        plan = {
+            "G": G, "first": first, "args": args, "args_ref": ctypes.byref(args),
+            "fn": _lib.load().tw_twilight_decode_layer, "bufs": bufs,
+            "q_shape": torch.Size((G, R, HEAD_DIM)), "kv_shape": torch.Size((G, HEAD_DIM)),
+            "per_group_cap": bufs["per_group_cap"],
+            "b0_budget": min(max(1, math.ceil(self.candidate_token_budget / self.block_size)),
+                             self.b0_page_capacity),
+            "meta_version": -1, "meta_pages": 0, "pool": pool, "reuse": reuse,
+            "initialized": [True] * G,
+        }
+        self._plans[tuple(entries)] = plan
+        return plan
 
     # ------------------------------------------------------------- hashes ----
     def selected_positions_sha256(self) -> str:

@@ -259,9 +259,9 @@ gather_quest_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
 }
 
 int gather_grid(int64_t rows, int rows_per_cta) {
-  int device = 0, sms = 148;
-  cudaGetDevice(&device);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  static int sm_cache[kMaxDevices];
+  int sms = 148;
+  if (cached_device_attribute(cudaDevAttrMultiProcessorCount, sm_cache, sms) != TW_OK) sms = 148;
   const int64_t want = (rows + (int64_t)rows_per_cta * kGatherUnroll - 1) /
                        ((int64_t)rows_per_cta * kGatherUnroll);
   const int64_t cap = (int64_t)sms * 8;

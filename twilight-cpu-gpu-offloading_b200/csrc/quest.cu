@@ -229,13 +229,10 @@ constexpr int kTopkMaxN = 16384;
 int launch_topk_pages(const float* scores, int rows, int n, int k, int32_t* out,
                       cudaStream_t stream) {
   const size_t smem = (size_t)n * sizeof(uint32_t);
-  cudaError_t err = cudaFuncSetAttribute(topk_pages_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTopkMaxN * (int)sizeof(uint32_t));
-  if (err != cudaSuccess) {
-    set_last_cuda_error(err);
-    return TW_ERR_CUDA;
-  }
+  static DynSmemOptIn opt_in;
+  const int st = ensure_dyn_smem((const void*)topk_pages_kernel, opt_in,
+                                 kTopkMaxN * (int)sizeof(uint32_t));
+  if (st != TW_OK) return st;
   topk_pages_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, n, k, out);
   return check_launch();
 }

@@ -447,23 +447,32 @@ size_t top_p_smem_bytes(int n, int64_t old_length) {
 int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
   const int n = args.b0 * args.block;
   const size_t smem = top_p_smem_bytes(n, args.old_length);
-  int device = 0;
-  cudaGetDevice(&device);
+  static int optin_cache[kMaxDevices];
+  static int static_smem_cache[kMaxDevices];
+  static DynSmemOptIn opt_in;
   int max_optin = 0;
-  cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-  cudaFuncAttributes fa{};
-  cudaError_t err = cudaFuncGetAttributes(&fa, top_p_union_kernel);
+  int st = cached_device_attribute(cudaDevAttrMaxSharedMemoryPerBlockOptin, optin_cache, max_optin);
+  if (st != TW_OK) return st;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) {
     set_last_cuda_error(err);
     return TW_ERR_CUDA;
   }
-  if (smem + fa.sharedSizeBytes > (size_t)max_optin) return TW_ERR_CAPACITY;
-  err = cudaFuncSetAttribute(top_p_union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-  if (err != cudaSuccess) {
-    set_last_cuda_error(err);
-    return TW_ERR_CUDA;
+  int static_smem = (device >= 0 && device < kMaxDevices) ? static_smem_cache[device] : 0;
+  if (static_smem <= 0) {
+    cudaFuncAttributes fa{};
+    err = cudaFuncGetAttributes(&fa, top_p_union_kernel);
+    if (err != cudaSuccess) {
+      set_last_cuda_error(err);
+      return TW_ERR_CUDA;
+    }
+    static_smem = (int)fa.sharedSizeBytes;
+    if (device >= 0 && device < kMaxDevices) static_smem_cache[device] = static_smem;
   }
+  if (smem + (size_t)static_smem > (size_t)max_optin) return TW_ERR_CAPACITY;
+  st = ensure_dyn_smem((const void*)top_p_union_kernel, opt_in, (int)smem);
+  if (st != TW_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(groups * args.R, 1, 1);
   cfg.blockDim = dim3(kTopPThreads, 1, 1);

@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/twilight_b200.h"
 
 namespace tw {
@@ -22,6 +24,53 @@ inline int check_launch() {
     set_last_cuda_error(err);
     return TW_ERR_CUDA;
   }
+  return TW_OK;
+}
+
+// Launch-time state kept per device so that the per-call path makes no
+// attribute queries: the dynamic shared memory a kernel has been opted into,
+// and device attributes read once.
+constexpr int kMaxDevices = 64;
+
+struct DynSmemOptIn {
+  std::mutex mu;
+  int bytes[kMaxDevices] = {};
+};
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) only when this launch needs
+// more than the function was opted into on the current device.
+inline int ensure_dyn_smem(const void* func, DynSmemOptIn& st, int bytes) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    std::lock_guard<std::mutex> lk(st.mu);
+    if (st.bytes[dev] >= bytes) return TW_OK;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess) st.bytes[dev] = bytes;
+  } else if (err == cudaSuccess) {
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  }
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}
+
+// Device attribute `attr` of the current device, queried once per device.
+inline int cached_device_attribute(cudaDeviceAttr attr, int (&cache)[kMaxDevices], int& value) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err == cudaSuccess && dev >= 0 && dev < kMaxDevices && cache[dev] > 0) {
+    value = cache[dev];
+    return TW_OK;
+  }
+  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&value, attr, dev);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  if (dev >= 0 && dev < kMaxDevices) cache[dev] = value;  // benign race: same value
   return TW_OK;
 }
 

@@ -90,6 +90,35 @@ class SequentialCacheState:
         self.expected_next_entry = (entry_idx + 1) % self.num_entries
         return old_length, new_length
 
+    def check_block(self, first: int, count: int) -> int:
+        """The checks of advance(e, 1) for e = first .. first + count - 1 in order,
+        for entries of one logical length; returns that old length."""
+        if first != self.expected_next_entry:
+            raise ValueError("strict sequential head-wise update violated: "
+                             f"expected {self.expected_next_entry}, got {first}")
+        lengths = self.logical_lengths
+        old_length = lengths[first]
+        if first + count > self.num_entries or lengths[first:first + count].count(old_length) != count:
+            raise AssertionError("layer KV entries have unequal logical lengths")
+        if old_length + 1 > self.allocated_capacity:
+            raise RuntimeError(f"cache capacity exceeded: {old_length} + 1 > "
+                               f"{self.allocated_capacity}")
+        return old_length
+
+    def commit_block(self, first: int, count: int, old_length: int) -> None:
+        """The updates of advance(e, 1) for the block check_block accepted."""
+        lengths = self.logical_lengths
+        lengths[first:first + count] = [old_length + 1] * count
+        self.write_position = old_length
+        if first == 0:
+            self.seen_tokens += 1
+        self.expected_next_entry = (first + count) % self.num_entries
+
+    def advance_block(self, first: int, count: int) -> int:
+        old_length = self.check_block(first, count)
+        self.commit_block(first, count, old_length)
+        return old_length
+
     @property
     def uniform(self) -> bool:
         return len(set(self.logical_lengths)) == 1
