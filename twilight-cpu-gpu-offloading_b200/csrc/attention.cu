@@ -205,6 +205,8 @@ template <typename T, int R, typename OutT, typename Rows>
 __global__ void __launch_bounds__(kAttnThreads)
 attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_splits,
                  AttnWorkspace ws, OutT* __restrict__ out, float* __restrict__ lse) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int kWarps = kAttnThreads / 32;
   constexpr int kRowsPerWarp = kAttnChunk / kWarps;
   constexpr int kRowsPerHalf = (R <= 4) ? 8 : 4;
@@ -456,9 +458,8 @@ int launch_rows(const Rows& rows, const void* q, int S, int R, int max_splits, f
   dim3 grid(max_splits, S);
 #define TW_ATTN_CASE(RR)                                                                    \
   case RR:                                                                                  \
-    attention_kernel<T, RR, OutT, Rows><<<grid, kAttnThreads, 0, stream>>>(                 \
-        rows, (const T*)q, scale_log2, max_splits, ws, (OutT*)out, lse);                    \
-    return check_launch();
+    return launch_pdl(attention_kernel<T, RR, OutT, Rows>, grid, dim3(kAttnThreads), 0,     \
+                      stream, rows, (const T*)q, scale_log2, max_splits, ws, (OutT*)out, lse);
   switch (R) {
     TW_ATTN_CASE(1)
     TW_ATTN_CASE(2)

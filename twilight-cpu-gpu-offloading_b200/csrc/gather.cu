@@ -110,6 +110,8 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
                     uint4* __restrict__ out_v, int64_t rows_cap, int32_t* __restrict__ cu_seqlens,
                     int32_t* error_flag, GatherReuse prev) {
   static_assert(kVec == 16, "a row is one 16-lane half-warp");
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ int64_t off[kMaxGroups + 1];
   __shared__ int s_hits[kMaxGroups], s_misses[kMaxGroups];
   if (threadIdx.x == 0) {
@@ -342,12 +344,12 @@ extern "C" int tw_gather_union(const void* slab_k, const void* slab_v,
   }
   constexpr int kVec = kHeadDim * 2 / 16;  // 16 vectors per 256-byte row
   const int grid = gather_grid(rows_cap, kGatherThreads / kVec);
-  gather_union_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
-      (const uint4*)slab_k, (const uint4*)slab_v, (const unsigned long long*)entry_dirs,
-      n_entries, max_len, first_entry, groups, old_length,
-      union_pos, pos_stride, union_count, (const uint4*)cur_k, (const uint4*)cur_v,
-      (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens, error_flag, prev);
-  return check_launch();
+  return launch_pdl(gather_union_kernel<kVec>, dim3(grid), dim3(kGatherThreads), 0,
+                    (cudaStream_t)stream, (const uint4*)slab_k, (const uint4*)slab_v,
+                    (const unsigned long long*)entry_dirs, n_entries, max_len, first_entry, groups,
+                    old_length, union_pos, pos_stride, union_count, (const uint4*)cur_k,
+                    (const uint4*)cur_v, (uint4*)out_k, (uint4*)out_v, rows_cap, cu_seqlens,
+                    error_flag, prev);
 }
 
 extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v,

@@ -84,6 +84,8 @@ int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
                int64_t entry_stride, const int32_t* __restrict__ pages, int R, int b0,
                int block, int sink, int group_size, float inv_sqrt_d,
                float* __restrict__ logits, int tokens_per_cta) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.y;  // g*R + r
   const int g = row / R;
   const int lane = threadIdx.x & 31;
@@ -146,6 +148,8 @@ __global__ void append_token_kernel(uint4* __restrict__ slab_k, uint4* __restric
                                     int64_t meta_entry_stride, uint8_t* __restrict__ packed,
                                     T* __restrict__ scale, T* __restrict__ minimum, int group_size,
                                     int scale_div) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int g = blockIdx.x;
   const int entry = first_entry + g;
   const int d = threadIdx.x;
@@ -262,14 +266,13 @@ int launch_int4_qk(const void* q, int q_dtype, const uint8_t* packed, const void
   if (q_dtype != TW_F32 && q_dtype != dtype) return TW_ERR_BAD_ARG;
   TW_DISPATCH_KV_DTYPE(dtype, T, {
     if (q_dtype == TW_F32)
-      int4_qk_kernel<T, float><<<grid, kThreads, 0, stream>>>(
-          (const float*)q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages,
-          R, b0_pages, block_size, sink, group_size, inv, logits, kTokensPerCta);
-    else
-      int4_qk_kernel<T, T><<<grid, kThreads, 0, stream>>>(
-          (const T*)q, packed, (const T*)scale, (const T*)minimum, entry_stride_tokens, pages, R,
-          b0_pages, block_size, sink, group_size, inv, logits, kTokensPerCta);
-    return check_launch();
+      return launch_pdl(int4_qk_kernel<T, float>, grid, dim3(kThreads), 0, stream,
+                        (const float*)q, packed, (const T*)scale, (const T*)minimum,
+                        entry_stride_tokens, pages, R, b0_pages, block_size, sink, group_size, inv,
+                        logits, kTokensPerCta);
+    return launch_pdl(int4_qk_kernel<T, T>, grid, dim3(kThreads), 0, stream, (const T*)q, packed,
+                      (const T*)scale, (const T*)minimum, entry_stride_tokens, pages, R, b0_pages,
+                      block_size, sink, group_size, inv, logits, kTokensPerCta);
   });
 }
 
@@ -307,11 +310,11 @@ extern "C" int tw_append_token(void* slab_k, void* slab_v, const uint64_t* entry
   if ((slab_k && ((uintptr_t)slab_k & 15)) || ((uintptr_t)cur_k & 15) || ((uintptr_t)cur_v & 15))
     return TW_ERR_BAD_ARG;
   TW_DISPATCH_KV_DTYPE(dtype, T, {
-    append_token_kernel<T><<<groups, kHeadDim, 0, (cudaStream_t)stream>>>(
-        (uint4*)slab_k, (uint4*)slab_v, (const unsigned long long*)entry_dirs, n_entries, max_len,
-        first_entry, position, (const T*)cur_k,
-        (const T*)cur_v, sink, block_size, (T*)page_min, (T*)page_max, meta_entry_stride,
-        packed, (T*)scale, (T*)minimum, packed ? group_size : 128, kScaleReciprocal);
-    return check_launch();
+    return launch_pdl(append_token_kernel<T>, dim3(groups), dim3(kHeadDim), 0,
+                      (cudaStream_t)stream, (uint4*)slab_k, (uint4*)slab_v,
+                      (const unsigned long long*)entry_dirs, n_entries, max_len, first_entry,
+                      position, (const T*)cur_k, (const T*)cur_v, sink, block_size, (T*)page_min,
+                      (T*)page_max, meta_entry_stride, packed, (T*)scale, (T*)minimum,
+                      packed ? group_size : 128, (int)kScaleReciprocal);
   });
 }

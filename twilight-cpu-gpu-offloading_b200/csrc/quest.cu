@@ -39,6 +39,8 @@ template <typename T, int R, typename QT>
 __global__ void quest_score_kernel(const QT* __restrict__ q, const T* __restrict__ pmin,
                                    const T* __restrict__ pmax, int n_pages,
                                    int64_t meta_group_stride, float* __restrict__ scores) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int g = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -82,6 +84,8 @@ constexpr int kTopkThreads = 512;
 
 __global__ void __launch_bounds__(kTopkThreads)
 topk_pages_kernel(const float* __restrict__ scores, int n, int k, int32_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ uint32_t keys[];  // n keys
   __shared__ uint32_t hist[256];
   __shared__ uint32_t scan_scratch[32];
@@ -191,9 +195,8 @@ int launch_quest_score_r(const void* q, const void* pmin, const void* pmax, int 
   const int warps = kThreads / 32;
   int blocks_x = (n_pages + warps - 1) / warps;
   dim3 grid(blocks_x, groups);
-  quest_score_kernel<T, R, QT><<<grid, kThreads, 0, stream>>>(
-      (const QT*)q, (const T*)pmin, (const T*)pmax, n_pages, stride, scores);
-  return check_launch();
+  return launch_pdl(quest_score_kernel<T, R, QT>, grid, dim3(kThreads), 0, stream,
+                    (const QT*)q, (const T*)pmin, (const T*)pmax, n_pages, stride, scores);
 }
 
 template <typename T, typename QT>
@@ -233,8 +236,8 @@ int launch_topk_pages(const float* scores, int rows, int n, int k, int32_t* out,
   const int st = ensure_dyn_smem((const void*)topk_pages_kernel, opt_in,
                                  kTopkMaxN * (int)sizeof(uint32_t));
   if (st != TW_OK) return st;
-  topk_pages_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, n, k, out);
-  return check_launch();
+  return launch_pdl(topk_pages_kernel, dim3(rows), dim3(kTopkThreads), smem, stream, scores, n, k,
+                    out);
 }
 
 }  // namespace tw

@@ -80,6 +80,8 @@ constexpr int kTopPSmallBin = 256;
 
 __global__ void __launch_bounds__(kTopPThreads)
 top_p_union_kernel(TopPArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ unsigned long long bin_mass[kTopPBins];
@@ -94,6 +96,7 @@ top_p_union_kernel(TopPArgs a) {
   __shared__ uint32_t s_prefix, s_cnt_gt, s_kmax, s_kmin, s_list_n;
   __shared__ unsigned long long s_mass_gt, s_target;
   __shared__ int s_bstar, s_count;
+  __shared__ uint32_t s_woff[kTopPThreads];
 
   const int R = a.R;
   const int rank = (int)cluster.block_rank();  // query head within the group
@@ -419,22 +422,26 @@ top_p_union_kernel(TopPArgs a) {
   cluster.sync();
 
   if (rank != 0) return;
-  // Leader: sorted union by popcount scan over contiguous word segments.
-  const int wseg = (words + blockDim.x - 1) / blockDim.x;
-  const int wbeg = min(words, tid * wseg);
-  const int wend = min(words, wbeg + wseg);
-  uint32_t cnt = 0u;
-  for (int w = wbeg; w < wend; ++w) cnt += __popc(bitmap[w]);
-  uint32_t total_union;
-  uint32_t out = block_exclusive_scan(cnt, scan_scratch, &total_union);
+  // Leader: sorted union.  Words are taken 1024 at a time (one per thread):
+  // an exclusive scan of their popcounts gives each word's output offset, then
+  // warp w writes word (32 * pass + w)'s set bits, one lane per bit, so a
+  // word's positions go to consecutive addresses in one coalesced store.
   int32_t* dst = a.union_pos + (int64_t)g * a.pos_stride;
-  for (int w = wbeg; w < wend; ++w) {
-    uint32_t bits = bitmap[w];
-    while (bits) {
-      const int b = __ffs(bits) - 1;
-      bits &= bits - 1;
-      dst[out++] = w * 32 + b;
+  uint32_t total_union = 0u;
+  for (int c0 = 0; c0 < words; c0 += kTopPThreads) {
+    const int w = c0 + tid;
+    const uint32_t bits = w < words ? bitmap[w] : 0u;
+    uint32_t chunk_total;
+    s_woff[tid] = total_union + block_exclusive_scan((uint32_t)__popc(bits), scan_scratch, &chunk_total);
+    __syncthreads();
+    const int chunk_words = min(kTopPThreads, words - c0);
+    for (int j = warp; j < chunk_words; j += nwarps) {
+      const uint32_t word = bitmap[c0 + j];
+      if ((word >> lane) & 1u)
+        dst[s_woff[j] + __popc(word & ((1u << lane) - 1u))] = (c0 + j) * 32 + lane;
     }
+    total_union += chunk_total;
+    __syncthreads();
   }
   if (tid == 0) a.union_count[g] = (int32_t)total_union;
 }
@@ -478,13 +485,15 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
   cfg.blockDim = dim3(kTopPThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = args.R;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   err = cudaLaunchKernelEx(&cfg, top_p_union_kernel, args);
   if (err != cudaSuccess) {
     set_last_cuda_error(err);

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <utility>
 
 #include "../../include/twilight_b200.h"
 
@@ -72,6 +73,39 @@ inline int cached_device_attribute(cudaDeviceAttr attr, int (&cache)[kMaxDevices
   }
   if (dev >= 0 && dev < kMaxDevices) cache[dev] = value;  // benign race: same value
   return TW_OK;
+}
+
+// Programmatic dependent launch.  The decode-path kernels are launched with
+// launch_pdl, so each may be scheduled while the previous kernel of the stream
+// is still running; every such kernel calls pdl_wait() before its first
+// global memory access (the wait returns once the previous grid has completed
+// and its writes are visible; without a programmatic predecessor it returns at
+// once), then pdl_launch_dependents() so that the next kernel can be
+// scheduled early.  Launch gaps between the kernels of a layer-step vanish.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  return check_launch();
 }
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);
