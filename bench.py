@@ -466,7 +466,14 @@ def run_ours(args) -> int:
                 "peak_source": "pinned H2D cudaMemcpyAsync measured in this run (256 MiB, best of 6)",
                 "unit": "GB/s",
                 "frac": round(gather_gbs / pinned, 4),
-                "traffic": None,
+                # dram__bytes_read.sum + dram__bytes_write.sum of this kernel, one ncu
+                # --set full capture (profiles/cfg2_attention_union_full.md); the
+                # host-link bytes are the sysmem read sectors of the same capture
+                "traffic": (29492224 if step.reuse else 369408) if step.fused else None,
+                "traffic_host_link": (4210176 if step.reuse else 35748352) if step.fused else None,
+                "traffic_source": ("ncu capture of attention_kernel<UnionRows> (one launch, same "
+                                   "workload); see profiles/cfg2_attention_union_full.md")
+                                  if step.fused else None,
                 "mapped_read_peak_gbs": round(mapped, 2),
             },
             "roofline_step": {
