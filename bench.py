@@ -466,14 +466,13 @@ def run_ours(args) -> int:
                 "peak_source": "pinned H2D cudaMemcpyAsync measured in this run (256 MiB, best of 6)",
                 "unit": "GB/s",
                 "frac": round(gather_gbs / pinned, 4),
-                # dram__bytes_read.sum + dram__bytes_write.sum of this kernel, one ncu
-                # --set full capture (profiles/cfg2_attention_union_full.md); the
-                # host-link bytes are the sysmem read sectors of the same capture
+                # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one
+                # ncu --set full capture of a launch of this workload; the host-link
+                # bytes are the sysmem read sectors (x 32 B) of the same capture
                 "traffic": (29492224 if step.reuse else 369408) if step.fused else None,
                 "traffic_host_link": (4210176 if step.reuse else 35748352) if step.fused else None,
-                "traffic_source": ("ncu capture of attention_kernel<UnionRows> (one launch, same "
-                                   "workload); see profiles/cfg2_attention_union_full.md")
-                                  if step.fused else None,
+                "traffic_source": ("ncu --set full, one launch of attention_kernel<UnionRows> on "
+                                   "this workload (profiles/)") if step.fused else None,
                 "mapped_read_peak_gbs": round(mapped, 2),
             },
             "roofline_step": {
