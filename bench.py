@@ -312,7 +312,11 @@ class DeviceStep:
 
 
 def l2_flush(buf: torch.Tensor) -> None:
+    """Flush L2 (126 MB) with a write of a 512 MiB buffer, then read the buffer
+    back so that the lines left in L2 are clean: the next step finds none of
+    its data in L2 and pays no write-back of the flush's dirty lines."""
     buf.add_(1)
+    torch.sum(buf.view(torch.int32), dtype=torch.int32)
 
 
 def run_ours(args) -> int:
@@ -444,7 +448,8 @@ def run_ours(args) -> int:
                 "workload": "cfg2: one layer, 8 KV x 4 Q heads, D 128, ctx 32768, fp16 K/V "
                             "in a pinned mapped host slab, 4 lognormal outlier channels, INT4 g32, "
                             "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
-                "l2": "flushed before every timed step (512 MiB device write, outside the events)",
+                "l2": "flushed before every timed step (512 MiB device write, then read back so "
+                      "the remaining lines are clean; outside the events)",
                 "parallelism": f"request-sharded replicas x{world}",
                 "path": ("fused gather+attention" if step.fused else "staged gather then attention")
                         + (" + previous-token row reuse" if step.reuse else ""),
@@ -802,6 +807,179 @@ def run_cfg5(args) -> int:
     return 0
 
 
+CFG3 = dict(layers=32, hidden=4096, heads=32, kv_heads=8, intermediate=14336, vocab=128256,
+            length=32768, b0_tokens=2048, top_p=0.95, int4_group=32, resident_heads=(0, 1),
+            rope_theta=500000.0, tokens=32)
+
+
+class Llama8BDecoder:
+    """a Llama-3-8B-shaped decoder (32 layers, 32 / 8 heads, D 128,
+    hidden 4096, MLP 14336, vocab 128256) with random-init bf16 weights, decoding
+    one token per step through the sparse path: RMSNorm, tw_qkv_rope (q / k / v
+    projection + RoPE), TwilightMatchedBudgetOffloadedCache.decode_layer (Quest +
+    INT4 + top-p + union + zero-copy attention + append), then o_proj and the
+    SiLU MLP as cuBLAS GEMVs (torch), and greedy argmax over the LM head."""
+
+    def __init__(self, tw, device, *, reuse: bool, extra_tokens: int) -> None:
+        c = CFG3
+        self.tw, self.device = tw, device
+        H, nq, nkv, I = c["hidden"], c["heads"], c["kv_heads"], c["intermediate"]
+        self.H, self.nq, self.nkv, self.R = H, nq, nkv, nq // nkv
+        dt = torch.bfloat16
+        g = torch.Generator(device=device).manual_seed(3)
+
+        def w(rows, cols):
+            return (torch.randn(rows, cols, generator=g, device=device) * cols ** -0.5).to(dt)
+
+        self.embed = (torch.randn(c["vocab"], H, generator=g, device=device) * 0.02).to(dt)
+        self.layers = []
+        for _ in range(c["layers"]):
+            self.layers.append(dict(
+                wq=w(nq * 128, H), wk=w(nkv * 128, H), wv=w(nkv * 128, H), wo=w(H, nq * 128),
+                wg=w(I, H), wu=w(I, H), wd=w(H, I),
+                n1=torch.ones(H, dtype=dt, device=device), n2=torch.ones(H, dtype=dt, device=device)))
+        self.norm = torch.ones(H, dtype=dt, device=device)
+        self.lm_head = w(c["vocab"], H)
+        L = c["length"]
+        E = c["layers"] * nkv
+        resident = [li * nkv + h for li in range(c["layers"]) for h in c["resident_heads"]]
+        self.cache = tw.TwilightMatchedBudgetOffloadedCache(
+            num_cache_entries=E, max_cache_len=L + extra_tokens + 16, head_dim=128,
+            num_query_heads_per_kv=self.R, dtype=dt, device=device,
+            candidate_token_budget=c["b0_tokens"], top_p=c["top_p"], budget_mode="dynamic",
+            layer_batched_selection=True, gqa_groupwise_execution=True, qk_backend="cuda",
+            int4_group_size=c["int4_group"], resident_entries=resident,
+            previous_token_resident_cache=reuse)
+        self.cache.enable_resident_reuse_trace(reuse)
+        # Prompt K / V "as in config 2": N(0,1) with 4 lognormal outlier channels per
+        # head, plus 8 needle rows per head (x4 norm, random direction) at uniform
+        # random positions.  Seeded, generated on the GPU, written through update().
+        for e in range(E):
+            ge = torch.Generator(device=device).manual_seed(100_000 + e)
+            k = torch.randn(L, 128, generator=ge, device=device)
+            ch = torch.randperm(128, generator=ge, device=device)[:4]
+            k[:, ch] *= torch.exp(torch.randn(4, generator=ge, device=device))
+            pos = torch.randint(0, L, (8,), generator=ge, device=device)
+            k[pos] *= 4.0
+            v = torch.randn(L, 128, generator=ge, device=device)
+            self.cache.update(k.to(dt).view(1, 1, L, 128), v.to(dt).view(1, 1, L, 128), e)
+        torch.cuda.synchronize()
+        inv = 1.0 / (c["rope_theta"] ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+        self.inv_freq = inv.to(device)
+        self.position = L
+        self.q = torch.empty((nq, 128), dtype=dt, device=device)
+        self.k = torch.empty((nkv, 128), dtype=dt, device=device)
+        self.v = torch.empty((nkv, 128), dtype=dt, device=device)
+        self.attn = torch.empty((nkv, self.R, 128), dtype=dt, device=device)
+        self.entries = [list(range(li * nkv, (li + 1) * nkv)) for li in range(c["layers"])]
+
+    def step(self, token: torch.Tensor) -> torch.Tensor:
+        """One decode step: token [1] int64 on the device -> next token [1]."""
+        F = torch.nn.functional
+        ops = self.tw.ops
+        freqs = self.position * self.inv_freq
+        emb = torch.cat((freqs, freqs))
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        h = self.embed[token].view(self.H)
+        for li, p in enumerate(self.layers):
+            x = F.rms_norm(h, (self.H,), p["n1"], 1e-5)
+            ops.qkv_rope(x, p["wq"], p["wk"], p["wv"], cos, sin, q_out=self.q, k_out=self.k,
+                         v_out=self.v)
+            self.cache.decode_layer(queries=self.q.view(self.nkv, self.R, 128), key_states=self.k,
+                                    value_states=self.v, entries=self.entries[li], out=self.attn)
+            h = h + F.linear(self.attn.view(-1), p["wo"])
+            x = F.rms_norm(h, (self.H,), p["n2"], 1e-5)
+            h = h + F.linear(F.silu(F.linear(x, p["wg"])) * F.linear(x, p["wu"]), p["wd"])
+        logits = F.linear(F.rms_norm(h, (self.H,), self.norm, 1e-5), self.lm_head)
+        self.position += 1
+        return logits.argmax().view(1)
+
+
+def run_cfg3(args) -> int:
+    """Full-model decode TPOT on one GPU, timed as the
+    reference times it (scripts/run_ruler_partial_h2d_tpot_case_v1.py:1303-1323):
+    decode step D1 is the warm-up, then a synchronized wall over D2..D32."""
+    _, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if rank != 0:
+        return 0
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    n_tok = CFG3["tokens"]
+    model = Llama8BDecoder(tw, device, reuse=args.reuse, extra_tokens=n_tok + 4)
+    token = torch.zeros(1, dtype=torch.int64, device=device)
+    token = model.step(token)  # D1
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    s.record()
+    out = []
+    for _ in range(n_tok - 1):  # D2..D32
+        token = model.step(token)
+        out.append(token)
+    e.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clocks = sampler.stop()
+    dev_ms = s.elapsed_time(e)
+    model.cache.synchronize()
+    steps = n_tok - 1
+    # front-end kernel alone (layer 0 weights, L2 flushed before each call)
+    p0 = model.layers[0]
+    x = torch.randn(model.H, device=device).to(torch.bfloat16)
+    cs = torch.ones(128, dtype=torch.bfloat16, device=device)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    fe_ms = []
+    for i in range(12):
+        l2_flush(flush)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        tw.ops.qkv_rope(x, p0["wq"], p0["wk"], p0["wv"], cs, cs, q_out=model.q, k_out=model.k,
+                        v_out=model.v)
+        b.record()
+        b.synchronize()
+        if i >= 2:
+            fe_ms.append(a.elapsed_time(b))
+    fe_bytes = sum(p0[k].numel() * 2 for k in ("wq", "wk", "wv"))
+    fe_us = float(np.median(fe_ms)) * 1e3
+    peaks = measured_peaks()
+    hbm_peak = peaks.get("hbm_gbs") or 6650.0
+    del flush
+    line = {
+        "metric": METRIC, "workload": "cfg3",
+        "value": round(steps / wall, 3), "unit": "tokens/s",
+        "ms_per_token": round(wall / steps * 1e3, 4),
+        "device_ms_per_token": round(dev_ms / steps, 4),
+        "us_per_layer_step": round(wall / steps / CFG3["layers"] * 1e6, 2),
+        "n_gpus": 1, "steps": steps, "warmup": 1, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "bf16 weights and K/V, fp32 math",
+        "data": "synthetic (random-init Llama-3-8B-shaped weights; seeded K/V with outliers and needles)",
+        "config": {"workload": "cfg3: 32 layers, 32/8 heads, D 128, hidden 4096, MLP 14336, ctx 32768, "
+                               "2 of 8 KV heads per layer GPU-resident, B0 2048, top-p 0.95, INT4 g32",
+                   "timing": "D1 warm-up, synchronized wall over D2..D32 (the reference's TPOT protocol)",
+                   "row_reuse": bool(args.reuse),
+                   "model_gemms": "torch / cuBLAS (o_proj, MLP, LM head); q/k/v projection + RoPE is "
+                                  "tw_qkv_rope"},
+        "clocks": clocks,
+        "gpu_launches_per_token": CFG3["layers"] * 7,
+        "front_end": {"kernel": "qkv_rope_kernel (q/k/v GEMV + RoPE, one launch per layer)",
+                      "us": round(fe_us, 2), "bytes": fe_bytes,
+                      "achieved_gbs": round(fe_bytes / (fe_us * 1e-6) / 1e9, 1),
+                      "peak_gbs": hbm_peak,
+                      "frac": round(fe_bytes / (fe_us * 1e-6) / 1e9 / hbm_peak, 4)},
+    }
+    if args.reuse:
+        rows = model.cache.resident_reuse_trace()
+        rows = [r for r in rows if r["decode_step"] > 1]
+        hist = sum(r["history_rows"] for r in rows)
+        line["row_reuse_hit_ratio"] = round(sum(r["hit_rows"] for r in rows) / max(1, hist), 4)
+    print(json.dumps(line), flush=True)
+    model.cache.close()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -811,8 +989,9 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
-                    help="cfg2 (default, the metric's configuration) or cfg5 (head-sharded 70B layer)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2",
+                    help="cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
+                         "decode, TPOT) or cfg5 (head-sharded 70B layer)")
     ap.add_argument("--reuse", action="store_true",
                     help="previous-token row reuse (fused path) with AR(1) query continuity")
     ap.add_argument("--reuse-rho", type=float, default=0.98,
@@ -826,6 +1005,8 @@ def main() -> int:
         return run_reference(args)
     if args.workload == "cfg5":
         return run_cfg5(args)
+    if args.workload == "cfg3":
+        return run_cfg3(args)
     return run_ours(args)
 
 

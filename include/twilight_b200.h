@@ -367,6 +367,22 @@ size_t tw_decode_layer_args_size(void);
 /* sizeof(tw_row_reuse), for binding-layout checks. */
 size_t tw_row_reuse_size(void);
 
+/* ---- decode-layer front end: q / k / v projection + rotary embedding -------------------------
+ * One token (batch 1): q[h] = RoPE(W_q[h] . hidden), k[h] = RoPE(W_k[h] . hidden),
+ * v[h] = W_v[h] . hidden, for n_q_heads / n_kv_heads heads of head_dim 128.
+ * Replaces the layer-batched grouped projection + apply_rotary_pos_emb of
+ * LlamaAttention_fast_forward (hi/mp.py:90-237) and its graph replay
+ * (hi/twilight_projection_graph.py:12-41).  w_q [n_q_heads*128][hidden],
+ * w_k / w_v [n_kv_heads*128][hidden] (the row-major nn.Linear weights), hidden
+ * [hidden_size], cos / sin [128] for the token's position, all in `dtype`
+ * (TW_F16 / TW_BF16), 16-byte aligned; hidden_size a multiple of 256, <= 16384.
+ * Outputs q_out [n_q_heads][128] (= [G][R][128]), k_out / v_out
+ * [n_kv_heads][128] in `dtype`.  Dot products accumulate in fp32 and are
+ * rounded to `dtype`; the rotation rounds each product and the sum to `dtype`. */
+int tw_qkv_rope(const void* hidden, const void* w_q, const void* w_k, const void* w_v,
+                int hidden_size, int n_q_heads, int n_kv_heads, int head_dim, const void* cos,
+                const void* sin, int dtype, void* q_out, void* k_out, void* v_out, void* stream);
+
 /* ---- allocation-free decode attention ---------------------------------------------------------------
  * No counterpart in the reference: an addition of this library.  Same
  * computation, arguments and result as tw_decode_attention, but the caller

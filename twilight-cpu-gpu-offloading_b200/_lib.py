@@ -97,6 +97,7 @@ SIGNATURES = {
     "tw_twilight_decode_layer": (I32, [ctypes.POINTER(DecodeLayerArgs), P]),
     "tw_decode_layer_args_size": (SZ, []),
     "tw_row_reuse_size": (SZ, []),
+    "tw_qkv_rope": (I32, [P, P, P, P, I32, I32, I32, I32, P, P, I32, P, P, P, P]),
     "tw_decode_attention_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, FLT, P, I32, P, P]),
 }
 

@@ -18,7 +18,8 @@ PKG = Path(__file__).resolve().parent
 REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtwilight_b200.so"
-SOURCES = ["quest.cu", "int4.cu", "topp_union.cu", "gather.cu", "attention.cu", "capi.cu"]
+SOURCES = ["quest.cu", "int4.cu", "topp_union.cu", "gather.cu", "attention.cu", "frontend.cu",
+           "capi.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

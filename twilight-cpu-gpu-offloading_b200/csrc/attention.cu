@@ -43,26 +43,6 @@ inline size_t attn_ws_bytes(int S, int R, int max_splits, AttnWorkspace* ws, cha
   return c_bytes + ml_bytes + o_bytes;
 }
 
-template <typename T> __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]);
-template <> __device__ __forceinline__ void unpack8<__half>(const uint4& u, float (&f)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
-template <> __device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4& u, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
-
 // Rows already gathered into device memory: segment s = rows [cu[s], cu[s+1]).
 struct FlatRows {
   const uint4* k;

@@ -269,3 +269,28 @@ def row_reuse(row_map: torch.Tensor, next_tag: int, *, next_k: torch.Tensor | No
             raise ValueError("row_counts must be int32 [G, 2]")
         r.row_counts = row_counts.data_ptr()
     return r
+
+
+def qkv_rope(hidden: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor,
+             cos: torch.Tensor, sin: torch.Tensor, *, q_out: torch.Tensor | None = None,
+             k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None):
+    """Decode-layer front end (tw_qkv_rope): hidden [H] and the nn.Linear weights
+    w_q [n_q*128, H], w_k / w_v [n_kv*128, H] -> q [n_q, 128] (rotated), k
+    [n_kv, 128] (rotated), v [n_kv, 128]; cos / sin [128] of the token's position."""
+    _cuda(hidden, w_q, w_k, w_v, cos, sin, q_out, k_out, v_out)
+    dt = hidden.dtype
+    if any(t.dtype != dt for t in (w_q, w_k, w_v, cos, sin)):
+        raise ValueError("hidden, weights and cos / sin must share one dtype")
+    H = hidden.numel()
+    if w_q.shape[1] != H or w_k.shape != w_v.shape or w_k.shape[1] != H or \
+            w_q.shape[0] % HEAD_DIM or w_k.shape[0] % HEAD_DIM or cos.numel() != HEAD_DIM or \
+            sin.numel() != HEAD_DIM:
+        raise ValueError("weights must be [heads*128, hidden], cos / sin [128]")
+    n_q, n_kv = w_q.shape[0] // HEAD_DIM, w_k.shape[0] // HEAD_DIM
+    q_out = q_out if q_out is not None else torch.empty((n_q, HEAD_DIM), dtype=dt, device=hidden.device)
+    k_out = k_out if k_out is not None else torch.empty((n_kv, HEAD_DIM), dtype=dt, device=hidden.device)
+    v_out = v_out if v_out is not None else torch.empty((n_kv, HEAD_DIM), dtype=dt, device=hidden.device)
+    _lib.check(lib().tw_qkv_rope(
+        _ptr(hidden), _ptr(w_q), _ptr(w_k), _ptr(w_v), H, n_q, n_kv, HEAD_DIM, _ptr(cos), _ptr(sin),
+        _kv_code(dt), _ptr(q_out), _ptr(k_out), _ptr(v_out), _stream(hidden.device)), "qkv_rope")
+    return q_out, k_out, v_out
