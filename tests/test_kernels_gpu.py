@@ -242,12 +242,25 @@ def test_select_layer_matches_reference_golden(tw, cuda, name, cfg):
     tw.ops.top_p_union(logits, pages, block_size=cfg["block"], sink=cfg["sink"], top_p=cfg["top_p"],
                        old_length=L, sink_end=w.sink_end, recent_start=w.recent_start,
                        union_pos=union_pos, union_count=union_count, head_count=head_count)
+    # the same layer through tw_select_layer (the fused one-launch selection)
+    f_pos = torch.zeros_like(union_pos)
+    f_cnt = torch.zeros_like(union_count)
+    f_hc = torch.zeros_like(head_count)
+    f_pages = tw.ops.select_layer(q, pmin, pmax, w.candidate_pages, packed, scale, minimum,
+                                  b0_pages=w.b0_pages, block_size=cfg["block"], sink=cfg["sink"],
+                                  top_p=cfg["top_p"], old_length=L, sink_end=w.sink_end,
+                                  recent_start=w.recent_start, union_pos=f_pos, union_count=f_cnt,
+                                  head_count=f_hc)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(head_count.cpu().numpy(), golden["desired"])
+    np.testing.assert_array_equal(f_hc.cpu().numpy(), golden["desired"])
+    assert torch.equal(f_pages, pages)
     for gi in range(G):
         n = int(union_count[gi])
         np.testing.assert_array_equal(union_pos[gi, :n].cpu().numpy(),
                                       golden["unions"][gi][: golden["union_counts"][gi]])
+        assert int(f_cnt[gi]) == n
+        assert torch.equal(f_pos[gi, :n], union_pos[gi, :n])
 
 
 def test_gather_kv_contract(tw, cuda):
@@ -414,3 +427,56 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
     torch.cuda.synchronize()
     assert int(err.item()) == tw._lib.TW_ERR_INVALID_INDEX
     slab.close()
+
+
+@pytest.mark.parametrize("R", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("dtype,group", [("float16", 32), ("bfloat16", 128), ("bfloat16", 64)])
+def test_select_layer_fused_equals_stages(tw, cuda, R, dtype, group):
+    """tw_select_layer (one cluster launch per layer when R divides the cluster)
+    gives the per-stage kernels' pages, per-head counts and positions and the
+    union, bit for bit; R = 3 exercises the per-stage fallback."""
+    G, L, sink, recent, block = 3, 3000 + 7 * R, 64, 256, 16
+    layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=dtype, seed=70 + R,
+                             workload="needles" if R % 2 else "outliers", sink=sink,
+                             recent=recent, block=block, n_needles=6)
+    dt = layer.keys.dtype
+    keys = layer.keys.to(cuda)
+    cap = (L + 64 - sink) // block + 1
+    pmin = torch.zeros((G, cap, 128), dtype=dt, device=cuda)
+    pmax = torch.zeros_like(pmin)
+    P_built = tw.ops.quest_page_metadata(keys, sink=sink, block_size=block, page_min=pmin,
+                                         page_max=pmax)
+    packed = torch.zeros((G, L + 64, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((G, L + 64, 128 // group), dtype=dt, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys, group_size=group, packed=packed, scale=scale, minimum=minimum)
+    w = torch_ref.window(L, sink=sink, recent=recent, block=block, candidate_token_budget=768,
+                         metadata_pages=P_built)
+    q = layer.queries.float().to(cuda)
+    n = w.b0_pages * block
+    outs = []
+    for fused in (False, True):
+        upos = torch.full((G, L + 64), -1, dtype=torch.int32, device=cuda)
+        ucnt = torch.zeros(G, dtype=torch.int32, device=cuda)
+        hc = torch.zeros((G, R), dtype=torch.int32, device=cuda)
+        hp = torch.full((G, R, n), -1, dtype=torch.int32, device=cuda)
+        if fused:
+            pg = tw.ops.select_layer(q, pmin, pmax, w.candidate_pages, packed, scale, minimum,
+                                     b0_pages=w.b0_pages, block_size=block, sink=sink, top_p=0.9,
+                                     old_length=L, sink_end=w.sink_end, recent_start=w.recent_start,
+                                     union_pos=upos, union_count=ucnt, head_count=hc, head_pos=hp)
+        else:
+            scores = tw.ops.quest_score(q, pmin, pmax, w.candidate_pages)
+            pg = tw.ops.topk_pages(scores, w.b0_pages)
+            logits = tw.ops.int4_qk(q, packed, scale, minimum, pg, block_size=block, sink=sink)
+            tw.ops.top_p_union(logits, pg, block_size=block, sink=sink, top_p=0.9, old_length=L,
+                               sink_end=w.sink_end, recent_start=w.recent_start, union_pos=upos,
+                               union_count=ucnt, head_count=hc, head_pos=hp)
+        torch.cuda.synchronize()
+        outs.append((pg, upos, ucnt, hc, hp))
+    (pg0, up0, uc0, hc0, hp0), (pg1, up1, uc1, hc1, hp1) = outs
+    assert torch.equal(pg0, pg1)
+    assert torch.equal(uc0, uc1)
+    assert torch.equal(hc0, hc1)
+    assert torch.equal(up0, up1)
+    assert torch.equal(hp0, hp1)

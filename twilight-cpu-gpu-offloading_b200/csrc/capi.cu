@@ -25,6 +25,14 @@ extern "C" int tw_top_p_union(const float*, const int32_t*, int, int, int, int, 
                               int32_t*, int32_t*, void*);
 
 namespace tw {
+int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void* pmax,
+                       int64_t meta_stride, int n_pages, const uint8_t* packed, const void* scale,
+                       const void* minimum, int64_t entry_stride, int groups, int R, int b0,
+                       int block, int sink, int group_size, int dtype, double top_p,
+                       int64_t old_length, int64_t sink_end, int64_t recent_start,
+                       int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
+                       int32_t* union_count, int32_t* head_count, int32_t* head_pos,
+                       int32_t* error_flag, cudaStream_t stream);
 int quest_score_dispatch(const void* q, int q_dtype, const void* pmin, const void* pmax, int groups,
                          int R, int n_pages, int64_t stride, int dtype, float* scores,
                          cudaStream_t stream);
@@ -127,11 +135,20 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
       tw_select_layer_workspace_size(groups, heads_per_group, n_pages, b0_pages, block_size);
   if (need == 0) return TW_ERR_BAD_ARG;
   if (!workspace || workspace_bytes < need) return TW_ERR_CAPACITY;
+  if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
+  int st = select_layer_fused(q, TW_F32, page_min, page_max, meta_group_stride, n_pages, packed,
+                              scale, minimum, entry_stride_tokens, groups, heads_per_group,
+                              b0_pages, block_size, sink, group_size, dtype, top_p, old_length,
+                              sink_end, recent_start, pages_out, union_pos, pos_stride,
+                              union_count, head_count, head_pos, error_flag,
+                              (cudaStream_t)stream);
+  if (st != TW_ERR_UNSUPPORTED) return st;
+  // per-stage kernels (shapes the fused selection does not serve)
   const size_t rows = (size_t)groups * heads_per_group;
   float* scores = reinterpret_cast<float*>(workspace);
   float* logits = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
                                            align256(rows * (size_t)n_pages * sizeof(float)));
-  int st = tw_quest_score(q, page_min, page_max, groups, heads_per_group, n_pages,
+  st = tw_quest_score(q, page_min, page_max, groups, heads_per_group, n_pages,
                           meta_group_stride, head_dim, dtype, scores, stream);
   if (st != TW_OK) return st;
   st = tw_topk_pages(scores, (int)rows, n_pages, b0_pages, pages_out, stream);
@@ -148,6 +165,29 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
 extern "C" size_t tw_decode_layer_args_size(void) { return sizeof(tw_decode_layer_args); }
 
 extern "C" size_t tw_row_reuse_size(void) { return sizeof(tw_row_reuse); }
+
+// The four per-stage selection kernels of a layer-step (shapes the fused
+// selection does not serve); pmin .. minimum are the first entry's arrays.
+static int select_stages(const tw_decode_layer_args* a, const void* pmin, const void* pmax,
+                         const uint8_t* packed, const void* scale, const void* minimum,
+                         cudaStream_t st) {
+  const int G = a->groups, R = a->heads_per_group;
+  const size_t rows = (size_t)G * R;
+  float* scores = reinterpret_cast<float*>(a->select_workspace);
+  float* logits = reinterpret_cast<float*>(reinterpret_cast<char*>(a->select_workspace) +
+                                           align256(rows * (size_t)a->n_pages * sizeof(float)));
+  int rc = quest_score_dispatch(a->q, a->dtype, pmin, pmax, G, R, a->n_pages,
+                                a->page_capacity * kHeadDim, a->dtype, scores, st);
+  if (rc != TW_OK) return rc;
+  rc = tw_topk_pages(scores, (int)rows, a->n_pages, a->b0_pages, a->pages, st);
+  if (rc != TW_OK) return rc;
+  rc = launch_int4_qk(a->q, a->dtype, packed, scale, minimum, a->max_len, a->pages, G, R,
+                      a->b0_pages, a->block_size, a->sink, a->int4_group_size, a->dtype, logits, st);
+  if (rc != TW_OK) return rc;
+  return tw_top_p_union(logits, a->pages, G, R, a->b0_pages, a->block_size, a->sink, a->top_p,
+                        a->old_length, a->sink_end, a->recent_start, a->union_pos, a->pos_stride,
+                        a->union_count, a->head_count, a->head_pos, a->error_flag, st);
+}
 
 extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* stream) {
   if (!a) return TW_ERR_BAD_ARG;
@@ -170,21 +210,12 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
   const uint8_t* packed = a->packed + e0 * a->max_len * (kHeadDim / 2);
   const char* scale = (const char*)a->scale + e0 * a->max_len * ngroups * elem;
   const char* minimum = (const char*)a->minimum + e0 * a->max_len * ngroups * elem;
-  const size_t rows = (size_t)G * R;
-  float* scores = reinterpret_cast<float*>(a->select_workspace);
-  float* logits = reinterpret_cast<float*>(reinterpret_cast<char*>(a->select_workspace) +
-                                           align256(rows * (size_t)a->n_pages * sizeof(float)));
-  int rc = quest_score_dispatch(a->q, a->dtype, pmin, pmax, G, R, a->n_pages,
-                                a->page_capacity * kHeadDim, a->dtype, scores, st);
-  if (rc != TW_OK) return rc;
-  rc = tw_topk_pages(scores, (int)rows, a->n_pages, a->b0_pages, a->pages, stream);
-  if (rc != TW_OK) return rc;
-  rc = launch_int4_qk(a->q, a->dtype, packed, scale, minimum, a->max_len, a->pages, G, R,
-                      a->b0_pages, a->block_size, a->sink, a->int4_group_size, a->dtype, logits, st);
-  if (rc != TW_OK) return rc;
-  rc = tw_top_p_union(logits, a->pages, G, R, a->b0_pages, a->block_size, a->sink, a->top_p,
-                      a->old_length, a->sink_end, a->recent_start, a->union_pos, a->pos_stride,
-                      a->union_count, a->head_count, a->head_pos, a->error_flag, stream);
+  int rc = select_layer_fused(a->q, a->dtype, pmin, pmax, a->page_capacity * kHeadDim, a->n_pages,
+                              packed, scale, minimum, a->max_len, G, R, a->b0_pages, a->block_size,
+                              a->sink, a->int4_group_size, a->dtype, a->top_p, a->old_length,
+                              a->sink_end, a->recent_start, a->pages, a->union_pos, a->pos_stride,
+                              a->union_count, a->head_count, a->head_pos, a->error_flag, st);
+  if (rc == TW_ERR_UNSUPPORTED) rc = select_stages(a, pmin, pmax, packed, scale, minimum, st);
   if (rc != TW_OK) return rc;
   rc = tw_attend_union(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
                        a->first_entry, G, a->old_length,

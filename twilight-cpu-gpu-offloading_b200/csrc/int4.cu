@@ -3,7 +3,7 @@
 // Reference: affine_int4_pack / affine_int4_dequantize
 // (hi/twilight_offload_cache.py:25-47), fused_affine_int4_qk
 // (hi/twilight_fused_qk.py:13-55), logits /= sqrt(D) (hi/twilight_offload_cache.py:1261).
-#include "tw_common.cuh"
+#include "select_math.cuh"
 
 namespace tw {
 
@@ -113,25 +113,11 @@ int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
       const int64_t pos = (int64_t)sink + (int64_t)page * block + (n % block);
       const int64_t tr = ebase + pos;
       const uint4 c = __ldg(reinterpret_cast<const uint4*>(packed + tr * (kHeadDim / 2)) + sub);
-      const float s = to_f32(scale[tr * ngroups + grp]);
-      const float m = to_f32(minimum[tr * ngroups + grp]);
-      const uint32_t words[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t byte = (words[w] >> (8 * b)) & 0xffu;
-          const int i = 8 * w + 2 * b;
-          const float k0 = __fadd_rn(__fmul_rn((float)(byte & 15u), s), m);
-          acc = __fadd_rn(acc, __fmul_rn(k0, qr[i]));
-          const float k1 = __fadd_rn(__fmul_rn((float)(byte >> 4), s), m);
-          acc = __fadd_rn(acc, __fmul_rn(k1, qr[i + 1]));
-        }
-      }
+      acc = int4_dot32(c, to_f32(scale[tr * ngroups + grp]), to_f32(minimum[tr * ngroups + grp]),
+                       qr);
     }
-    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
-    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (valid && sub == 0) logits[(int64_t)row * n_cand + n] = __fmul_rn(acc, inv_sqrt_d);
+    const float logit = int4_logit(acc, inv_sqrt_d);
+    if (valid && sub == 0) logits[(int64_t)row * n_cand + n] = logit;
   }
 }
 
@@ -244,13 +230,6 @@ extern "C" int tw_int4_pack_ex(const void* keys, int64_t key_entry_stride, int n
   return tw_int4_pack_mode(keys, key_entry_stride, n_entries, n_tokens, head_dim, group_size,
                            dtype, packed, scale, minimum, out_entry_stride, out_row_offset,
                            scale_div, stream);
-}
-
-// 1/sqrt(D) as torch on CUDA applies `logits /= math.sqrt(D)`: the double
-// divisor is narrowed to fp32 and its fp32 reciprocal multiplies.
-float inv_sqrt_head_dim(int head_dim) {
-  const float d = (float)sqrt((double)head_dim);
-  return 1.0f / d;
 }
 
 // q in fp32 (q_dtype TW_F32) or in the K dtype (converted exactly on load).

@@ -3,7 +3,7 @@
 // Reference: hi/quest_offload_cache.py:276-289 (metadata),
 // hi/twilight_fused_quest.py:13-46 (score and its summation order),
 // hi/twilight_offload_cache.py:1136-1166 (top-k + B0 expansion).
-#include "tw_common.cuh"
+#include "select_math.cuh"
 
 namespace tw {
 
@@ -54,24 +54,11 @@ __global__ void quest_score_kernel(const QT* __restrict__ q, const T* __restrict
   const T* gmin = pmin + g * meta_group_stride;
   const T* gmax = pmax + g * meta_group_stride;
   for (int p = blockIdx.x * warps + warp; p < n_pages; p += gridDim.x * warps) {
-    float lo[4], hi[4];
+    float sc[R];
+    quest_page_score<T, R>(qr, gmin, gmax, p, lane, sc);
+    if (lane == 0) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      lo[c] = to_f32(gmin[(int64_t)p * kHeadDim + lane + 32 * c]);
-      hi[c] = to_f32(gmax[(int64_t)p * kHeadDim + lane + 32 * c]);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float acc = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float e = qr[r][c] > 0.0f ? hi[c] : lo[c];
-        acc = __fadd_rn(acc, __fmul_rn(e, qr[r][c]));
-      }
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1)
-        acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, off));
-      if (lane == 0) scores[((int64_t)g * R + r) * n_pages + p] = acc;
+      for (int r = 0; r < R; ++r) scores[((int64_t)g * R + r) * n_pages + p] = sc[r];
     }
   }
 }

@@ -1,0 +1,116 @@
+// Per-element arithmetic of the selection stage, shared by the per-stage
+// kernels (quest.cu, int4.cu) and the fused whole-layer selection
+// (topp_union.cu) so that both compute bit-identical scores and logits.
+#pragma once
+
+#include "tw_common.cuh"
+
+namespace tw {
+
+// Quest upper-bound score of page p for R query heads (warp-wide).  Lane l
+// holds channels l, l+32, l+64, l+96; per head the products are added in that
+// order (mul and add separately rounded), then reduced by shfl-down 1..16,
+// the order of hi/twilight_fused_quest.py:13-46.  The result is valid in lane 0.
+template <typename T, int R>
+__device__ __forceinline__ void quest_page_score(const float (&qr)[R][4], const T* __restrict__ gmin,
+                                                 const T* __restrict__ gmax, int64_t p, int lane,
+                                                 float (&out)[R]) {
+  float lo[4], hi[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    lo[c] = to_f32(gmin[p * kHeadDim + lane + 32 * c]);
+    hi[c] = to_f32(gmax[p * kHeadDim + lane + 32 * c]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float e = qr[r][c] > 0.0f ? hi[c] : lo[c];
+      acc = __fadd_rn(acc, __fmul_rn(e, qr[r][c]));
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1)
+      acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, off));
+    out[r] = acc;
+  }
+}
+
+// quest_page_score for two pages at once (both pages' loads issued first).
+template <typename T, int R>
+__device__ __forceinline__ void quest_page_score2(const float (&qr)[R][4], const T* __restrict__ gmin,
+                                                  const T* __restrict__ gmax, int64_t p, int64_t p2,
+                                                  int lane, float (&out)[R], float (&out2)[R]) {
+  float lo[4], hi[4], lo2[4], hi2[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    lo[c] = to_f32(gmin[p * kHeadDim + lane + 32 * c]);
+    hi[c] = to_f32(gmax[p * kHeadDim + lane + 32 * c]);
+    lo2[c] = to_f32(gmin[p2 * kHeadDim + lane + 32 * c]);
+    hi2[c] = to_f32(gmax[p2 * kHeadDim + lane + 32 * c]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float acc = 0.0f, acc2 = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      acc = __fadd_rn(acc, __fmul_rn(qr[r][c] > 0.0f ? hi[c] : lo[c], qr[r][c]));
+      acc2 = __fadd_rn(acc2, __fmul_rn(qr[r][c] > 0.0f ? hi2[c] : lo2[c], qr[r][c]));
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, off));
+      acc2 = __fadd_rn(acc2, __shfl_down_sync(0xffffffffu, acc2, off));
+    }
+    out[r] = acc;
+    out2[r] = acc2;
+  }
+}
+
+// INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
+// covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
+// k = code * s + m (separately rounded), acc += k * q in channel order.
+// A code v in 0..15 as float, exactly: the bits 0x4B0000vv are the float
+// 2^23 + v, from which 2^23 is subtracted (exact).  One byte permute puts
+// byte b of `nibbles` (one code per byte) under the exponent 0x4B.
+__device__ __forceinline__ float nibble_float(uint32_t nibbles, int b) {
+  return __fsub_rn(__int_as_float(__byte_perm(nibbles, 0x4B000000u, 0x7440u | (uint32_t)b)),
+                   8388608.0f);
+}
+
+__device__ __forceinline__ float int4_dot32(const uint4& codes, float s, float m,
+                                            const float (&qr)[32]) {
+  const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+  float acc = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t lo = words[w] & 0x0f0f0f0fu;         // even channels, one per byte
+    const uint32_t hi = (words[w] >> 4) & 0x0f0f0f0fu;  // odd channels
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int i = 8 * w + 2 * b;
+      const float k0 = __fadd_rn(__fmul_rn(nibble_float(lo, b), s), m);
+      acc = __fadd_rn(acc, __fmul_rn(k0, qr[i]));
+      const float k1 = __fadd_rn(__fmul_rn(nibble_float(hi, b), s), m);
+      acc = __fadd_rn(acc, __fmul_rn(k1, qr[i + 1]));
+    }
+  }
+  return acc;
+}
+
+// Sum of the 4 lanes' partial dot products ((a0 + a1) + (a2 + a3), in lane
+// 0 of the group) times 1/sqrt(D): the candidate's estimated logit.
+__device__ __forceinline__ float int4_logit(float acc, float inv_sqrt_d) {
+  acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+  acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+  return __fmul_rn(acc, inv_sqrt_d);
+}
+
+// 1/sqrt(D) as torch on CUDA applies `logits /= math.sqrt(D)`: the double
+// divisor is narrowed to fp32 and its fp32 reciprocal multiplies.
+inline float inv_sqrt_head_dim(int head_dim) {
+  const float d = (float)sqrt((double)head_dim);
+  return 1.0f / d;
+}
+
+}  // namespace tw

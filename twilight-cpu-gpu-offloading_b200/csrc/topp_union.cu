@@ -24,7 +24,7 @@
 // the leader writes the sorted union by a popcount scan.
 #include <cooperative_groups.h>
 
-#include "tw_common.cuh"
+#include "select_math.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -78,12 +78,12 @@ __device__ __forceinline__ unsigned long long target_of(unsigned long long z, do
 constexpr int kTopPBins = 2048;
 constexpr int kTopPSmallBin = 256;
 
-__global__ void __launch_bounds__(kTopPThreads)
-top_p_union_kernel(TopPArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+// Top-p count and selection of one row, by the whole CTA (kTopPThreads threads).
+// lrow: the row's n logits (global or shared memory); keys may alias lrow
+// (each thread overwrites only the logits it has read).  On return sel[i] = 1
+// for the selected candidates; returns the count.
+__device__ int top_p_row(const float* lrow, int n, double top_p, uint32_t* keys,
+                         unsigned long long* mass, unsigned char* sel) {
   __shared__ unsigned long long bin_mass[kTopPBins];
   __shared__ uint32_t bin_cnt[kTopPBins];
   __shared__ unsigned long long list[kTopPSmallBin];
@@ -96,34 +96,10 @@ top_p_union_kernel(TopPArgs a) {
   __shared__ uint32_t s_prefix, s_cnt_gt, s_kmax, s_kmin, s_list_n;
   __shared__ unsigned long long s_mass_gt, s_target;
   __shared__ int s_bstar, s_count;
-  __shared__ uint32_t s_woff[kTopPThreads];
-
-  const int R = a.R;
-  const int rank = (int)cluster.block_rank();  // query head within the group
-  const int g = blockIdx.x / R;
-  const int row = g * R + rank;
-  const int n = a.b0 * a.block;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int nwarps = blockDim.x >> 5;
-
-  const int64_t L = a.old_length;
-  const int words = (int)((L + 31) >> 5);
-  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);
-  unsigned long long* mass =
-      reinterpret_cast<unsigned long long*>(smem_raw + align16((size_t)n * 4));
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + top_p_head_bytes(n));
-  unsigned char* sel = reinterpret_cast<unsigned char*>(bitmap + words);
-
-  // Leader: clear the bitmap and set the protected sink / recent ranges.
-  if (rank == 0) {
-    const int64_t sink_hi = min(a.sink_end, L);
-    for (int w = tid; w < words; w += blockDim.x) {
-      const int64_t lo = (int64_t)w * 32;
-      bitmap[w] = bits_below(sink_hi, lo) | (bits_below(L, lo) & ~bits_below(a.recent_start, lo));
-    }
-  }
   for (int b = tid; b < kTopPBins; b += blockDim.x) {
     bin_mass[b] = 0ull;
     bin_cnt[b] = 0u;
@@ -135,9 +111,6 @@ top_p_union_kernel(TopPArgs a) {
     s_bstar = -1;
   }
   __syncthreads();
-
-  const float* lrow = a.logits + (int64_t)row * n;
-  const int32_t* prow = a.pages + (int64_t)row * a.b0;
 
   // 1. keys, row max and min.
   uint32_t kmax = 0u, kmin = 0xffffffffu;
@@ -173,7 +146,7 @@ top_p_union_kernel(TopPArgs a) {
   }
   unsigned long long z;
   block_exclusive_scan_u64(part, scan64, &z);
-  const unsigned long long target = target_of(z, a.top_p);
+  const unsigned long long target = target_of(z, top_p);
 
   // 3. crossing bin: bins in order (highest logits first), two per thread.
   constexpr int kBinsPerThread = kTopPBins / kTopPThreads;
@@ -369,6 +342,85 @@ top_p_union_kernel(TopPArgs a) {
   }
   __syncthreads();
 
+  return count;
+}
+
+// ORs the row's selected positions (sel over its candidate pages prow) into
+// the cluster leader's bitmap over distributed shared memory, one remote OR
+// per selected page (its block_size candidates are consecutive positions);
+// pages wider than 32 positions OR per candidate.  Returns true when a
+// position fell outside [0, L).
+__device__ bool or_selection(uint32_t* leader_bitmap, const int32_t* prow, const unsigned char* sel,
+                             int b0, int block, int sink, int64_t L) {
+  bool bad = false;
+  for (int pg = threadIdx.x; pg < b0; pg += blockDim.x) {
+    const int64_t pos0 = (int64_t)sink + (int64_t)prow[pg] * block;
+    if (block <= 32) {
+      uint32_t m32 = 0u;
+      for (int j = 0; j < block; ++j) m32 |= (uint32_t)sel[pg * block + j] << j;
+      if (!m32) continue;
+      if (pos0 < 0 || pos0 + block > L) {
+        bad = true;
+        continue;
+      }
+      const uint32_t sh = (uint32_t)(pos0 & 31);
+      atomicOr(&leader_bitmap[pos0 >> 5], m32 << sh);
+      if (sh + (uint32_t)block > 32u && (m32 >> (32u - sh)))
+        atomicOr(&leader_bitmap[(pos0 >> 5) + 1], m32 >> (32u - sh));
+    } else {
+      for (int j = 0; j < block; ++j) {
+        if (!sel[pg * block + j]) continue;
+        const int64_t pos = pos0 + j;
+        if (pos < 0 || pos >= L) {
+          bad = true;
+          continue;
+        }
+        atomicOr(&leader_bitmap[pos >> 5], 1u << (pos & 31));
+      }
+    }
+  }
+  return bad;
+}
+
+__global__ void __launch_bounds__(kTopPThreads)
+top_p_union_kernel(TopPArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint32_t scan_scratch[32];
+  __shared__ uint32_t s_woff[kTopPThreads];
+
+  const int R = a.R;
+  const int rank = (int)cluster.block_rank();  // query head within the group
+  const int g = blockIdx.x / R;
+  const int row = g * R + rank;
+  const int n = a.b0 * a.block;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+
+  const int64_t L = a.old_length;
+  const int words = (int)((L + 31) >> 5);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);
+  unsigned long long* mass =
+      reinterpret_cast<unsigned long long*>(smem_raw + align16((size_t)n * 4));
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + top_p_head_bytes(n));
+  unsigned char* sel = reinterpret_cast<unsigned char*>(bitmap + words);
+
+  // Leader: clear the bitmap and set the protected sink / recent ranges.
+  if (rank == 0) {
+    const int64_t sink_hi = min(a.sink_end, L);
+    for (int w = tid; w < words; w += blockDim.x) {
+      const int64_t lo = (int64_t)w * 32;
+      bitmap[w] = bits_below(sink_hi, lo) | (bits_below(L, lo) & ~bits_below(a.recent_start, lo));
+    }
+  }
+  const float* lrow = a.logits + (int64_t)row * n;
+  const int32_t* prow = a.pages + (int64_t)row * a.b0;
+  const int count = top_p_row(lrow, n, a.top_p, keys, mass, sel);
+
   // Per-row outputs: the count and (optionally) the selected positions in
   // candidate order, i.e. ascending positions (pages are ascending).
   if (tid == 0) a.head_count[row] = count;
@@ -388,36 +440,8 @@ top_p_union_kernel(TopPArgs a) {
   // All rows are final and the leader's bitmap is initialised.
   cluster.sync();
 
-  // One remote OR per selected page (its block_size candidates are
-  // consecutive positions); pages wider than 32 positions OR per candidate.
   uint32_t* leader_bitmap = cluster.map_shared_rank(bitmap, 0);
-  bool bad = false;
-  for (int pg = tid; pg < a.b0; pg += blockDim.x) {
-    const int64_t pos0 = (int64_t)a.sink + (int64_t)prow[pg] * a.block;
-    if (a.block <= 32) {
-      uint32_t m32 = 0u;
-      for (int j = 0; j < a.block; ++j) m32 |= (uint32_t)sel[pg * a.block + j] << j;
-      if (!m32) continue;
-      if (pos0 < 0 || pos0 + a.block > L) {
-        bad = true;
-        continue;
-      }
-      const uint32_t sh = (uint32_t)(pos0 & 31);
-      atomicOr(&leader_bitmap[pos0 >> 5], m32 << sh);
-      if (sh + (uint32_t)a.block > 32u && (m32 >> (32u - sh)))
-        atomicOr(&leader_bitmap[(pos0 >> 5) + 1], m32 >> (32u - sh));
-    } else {
-      for (int j = 0; j < a.block; ++j) {
-        if (!sel[pg * a.block + j]) continue;
-        const int64_t pos = pos0 + j;
-        if (pos < 0 || pos >= L) {
-          bad = true;
-          continue;
-        }
-        atomicOr(&leader_bitmap[pos >> 5], 1u << (pos & 31));
-      }
-    }
-  }
+  const bool bad = or_selection(leader_bitmap, prow, sel, a.b0, a.block, a.sink, L);
   if (bad && a.error_flag) atomicExch(a.error_flag, TW_ERR_INVALID_INDEX);
   cluster.sync();
 
@@ -500,6 +524,494 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
     return TW_ERR_CUDA;
   }
   return check_launch();
+}
+
+// ---- whole-layer selection in one launch --------------------------------------------------
+// One thread-block cluster of C CTAs per KV group (C = 16, the largest
+// cluster B200 schedules, when every group's cluster fits at once, else 8)
+// runs the four
+// selection stages with every intermediate in shared memory:
+//  1. Quest scores: all CTAs of the cluster split the candidate pages; each
+//     page's R scores go to the shared memory of the R row owners (CTA r owns
+//     query head r) over distributed shared memory;
+//  2. top-k pages: each owner radix-selects its row in its own shared memory
+//     (as topk_pages_kernel);
+//  3. INT4 estimate: the row's candidates are split over the C / R
+//     CTAs with rank % R == r; logits go to the owner's shared memory;
+//  4. top-p and the union, as top_p_union_kernel, with the leader (CTA 0)
+//     holding the bitmap;
+//  5. the sorted union is written by all CTAs, each a slice of the leader's
+//     bitmap words.
+// Scores, pages, logits and selections are bit-identical to the per-stage
+// kernels (same arithmetic, select_math.cuh).
+constexpr int kSelCluster = 8;      // portable cluster size
+constexpr int kSelClusterWide = 16; // non-portable cluster size
+constexpr int kSelUnroll = 2;  // candidates per 4-lane group in flight (INT4 stage)
+
+struct SelectArgs {
+  const void* q;          // [G][R][D], QT
+  const void* pmin;       // first group's page min / max, K dtype
+  const void* pmax;
+  int64_t meta_stride;    // elements between consecutive groups' page arrays
+  int n_pages;
+  const uint8_t* packed;  // first group's INT4 codes
+  const void* scale;
+  const void* minimum;
+  int64_t entry_stride;   // tokens between consecutive groups' code rows
+  int group_size;
+  int b0;
+  int block;
+  int sink;
+  double top_p;
+  int64_t old_length;
+  int64_t sink_end;
+  int64_t recent_start;
+  float inv_sqrt_d;
+  int32_t* pages_out;     // [G][R][b0]
+  int32_t* union_pos;
+  int64_t pos_stride;
+  int32_t* union_count;
+  int32_t* head_count;
+  int32_t* head_pos;
+  int32_t* error_flag;
+};
+
+// Dynamic shared memory: scores f32[P] | pages i32[b0] | logits f32[n] (keys
+// alias them) | mass u64[n] | bitmap u32[words] | sel u8[n].
+__host__ __device__ __forceinline__ size_t select_smem_bytes(int P, int b0, int n, int64_t L) {
+  const size_t words = (size_t)((L + 31) / 32);
+  return align16((size_t)P * 4) + align16((size_t)b0 * 4) + align16((size_t)n * 4) +
+         (size_t)n * 8 + align16(words * 4) + (size_t)n;
+}
+
+template <typename T, typename QT, int R>
+__global__ void __launch_bounds__(kTopPThreads)
+select_layer_kernel(SelectArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ uint32_t scan_scratch[32];
+  __shared__ uint32_t s_hist[256];
+  __shared__ uint32_t s_prefix, s_remaining;
+  __shared__ uint32_t s_woff[kTopPThreads];
+  __shared__ uint32_t s_base;
+
+  const int C = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const int g = blockIdx.x / C;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int P = a.n_pages;
+  const int n = a.b0 * a.block;
+  const int64_t L = a.old_length;
+  const int words = (int)((L + 31) >> 5);
+
+  unsigned char* cur = smem_raw;
+  float* s_score = reinterpret_cast<float*>(cur);
+  cur += align16((size_t)P * 4);
+  int32_t* s_pages = reinterpret_cast<int32_t*>(cur);
+  cur += align16((size_t)a.b0 * 4);
+  float* s_logit = reinterpret_cast<float*>(cur);
+  cur += align16((size_t)n * 4);
+  unsigned long long* mass = reinterpret_cast<unsigned long long*>(cur);
+  cur += (size_t)n * 8;
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(cur);
+  cur += align16((size_t)words * 4);
+  unsigned char* sel = cur;
+
+  // Leader: clear the bitmap and set the protected sink / recent ranges.
+  if (crank == 0) {
+    const int64_t sink_hi = min(a.sink_end, L);
+    for (int w = tid; w < words; w += blockDim.x) {
+      const int64_t lo = (int64_t)w * 32;
+      bitmap[w] = bits_below(sink_hi, lo) | (bits_below(L, lo) & ~bits_below(a.recent_start, lo));
+    }
+  }
+
+  // 1. Quest scores of the group's R heads.
+  {
+    const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)g * R * kHeadDim;
+    float qr[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) qr[r][c] = to_f32(qg[r * kHeadDim + lane + 32 * c]);
+    const T* gmin = reinterpret_cast<const T*>(a.pmin) + (int64_t)g * a.meta_stride;
+    const T* gmax = reinterpret_cast<const T*>(a.pmax) + (int64_t)g * a.meta_stride;
+    float* owner_scores[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) owner_scores[r] = cluster.map_shared_rank(s_score, r);
+    // two pages per warp and pass: both pages' loads are issued together
+    const int stride = C * nwarps;
+    for (int p = crank * nwarps + warp; p < P; p += 2 * stride) {
+      const int p2 = p + stride;
+      float sc[R], sc2[R];
+      if (p2 < P) {
+        quest_page_score2<T, R>(qr, gmin, gmax, p, p2, lane, sc, sc2);
+      } else {
+        quest_page_score<T, R>(qr, gmin, gmax, p, lane, sc);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          owner_scores[r][p] = sc[r];
+          if (p2 < P) owner_scores[r][p2] = sc2[r];
+        }
+      }
+    }
+  }
+  cluster.sync();
+
+  const bool owner = crank < R;
+  const int row = g * R + crank;
+  // 2. top-k pages of the owner's row (the radix select of topk_pages_kernel).
+  if (owner) {
+    uint32_t* keys = reinterpret_cast<uint32_t*>(s_score);
+    for (int i = tid; i < P; i += blockDim.x) keys[i] = float_key(s_score[i]);
+    if (tid == 0) {
+      s_prefix = 0u;
+      s_remaining = (uint32_t)a.b0;
+    }
+    __syncthreads();
+    uint32_t mask = 0u;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int b = tid; b < 256; b += blockDim.x) s_hist[b] = 0u;
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      for (int i = tid; i < P; i += blockDim.x) {
+        const uint32_t key = keys[i];
+        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        uint32_t local[8];
+        uint32_t sum = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          local[j] = s_hist[8 * lane + j];
+          sum += local[j];
+        }
+        uint32_t suffix = sum;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, off);
+          if (lane + off < 32) suffix += y;
+        }
+        const uint32_t above = suffix - sum;
+        const uint32_t need = s_remaining;
+        __syncwarp();
+        if (above < need && need <= suffix) {
+          uint32_t acc = above;
+          for (int j = 7; j >= 0; --j) {
+            if (acc + local[j] >= need) {
+              s_prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
+              s_remaining = need - acc;
+              break;
+            }
+            acc += local[j];
+          }
+        }
+      }
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    const uint32_t kth = s_prefix;
+    const uint32_t ties = s_remaining;
+    const int seg = (P + blockDim.x - 1) / blockDim.x;
+    const int beg = min(P, tid * seg);
+    const int end = min(P, beg + seg);
+    uint32_t gt = 0u, eq = 0u;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t key = keys[i];
+      gt += key > kth;
+      eq += key == kth;
+    }
+    uint32_t total;
+    const uint32_t eq_before = block_exclusive_scan(eq, scan_scratch, &total);
+    const uint32_t take_eq = (eq_before >= ties) ? 0u : min(eq, ties - eq_before);
+    const uint32_t base = block_exclusive_scan(gt + take_eq, scan_scratch, &total);
+    int32_t* gout = a.pages_out + (int64_t)row * a.b0;
+    uint32_t slot = base, eq_seen = 0u;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t key = keys[i];
+      bool take = key > kth;
+      if (key == kth) {
+        take = eq_seen < take_eq;
+        ++eq_seen;
+      }
+      if (take) {
+        s_pages[slot] = i;
+        gout[slot] = i;
+        ++slot;
+      }
+    }
+  }
+  cluster.sync();
+
+  // 3. INT4 estimate: CTAs with rank % R == r share row r's candidates.
+  {
+    const int r = crank % R;
+    const int part = crank / R;
+    const int parts = C / R;
+    if (!owner) {  // this CTA's copy of row r's pages (the loop reads them per candidate)
+      const int32_t* src = cluster.map_shared_rank(s_pages, r);
+      for (int i = tid; i < a.b0; i += blockDim.x) s_pages[i] = src[i];
+    }
+    __syncthreads();
+    const int chunk = (n + parts - 1) / parts;
+    const int c_beg = min(n, part * chunk);
+    const int c_end = min(n, c_beg + chunk);
+    const int sub = lane & 3;
+    const int tok = lane >> 2;
+    const QT* qrow = reinterpret_cast<const QT*>(a.q) + ((int64_t)g * R + r) * kHeadDim + 32 * sub;
+    float qr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qr[i] = to_f32(qrow[i]);
+    const int ngroups = kHeadDim / a.group_size;
+    const int grp = (32 * sub) / a.group_size;
+    const int32_t* prow = s_pages;
+    float* lout = cluster.map_shared_rank(s_logit, r);
+    const int64_t ebase = (int64_t)g * a.entry_stride;
+    const T* scale = reinterpret_cast<const T*>(a.scale);
+    const T* minimum = reinterpret_cast<const T*>(a.minimum);
+    constexpr int kStep = kTopPThreads / 4;  // candidates per pass of the CTA
+    // base is warp-uniform (all lanes run every pass: int4_logit shuffles)
+    for (int base = c_beg + warp * 8; base < c_end; base += kStep * kSelUnroll) {
+      uint4 codes[kSelUnroll];
+      float sv[kSelUnroll], mv[kSelUnroll];
+#pragma unroll
+      for (int u = 0; u < kSelUnroll; ++u) {
+        const int i = base + tok + u * kStep;
+        codes[u] = make_uint4(0u, 0u, 0u, 0u);
+        sv[u] = 0.0f;
+        mv[u] = 0.0f;
+        if (i < c_end) {
+          const int64_t pos = (int64_t)a.sink + (int64_t)prow[i / a.block] * a.block + (i % a.block);
+          const int64_t tr = ebase + pos;
+          codes[u] = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
+          sv[u] = to_f32(scale[tr * ngroups + grp]);
+          mv[u] = to_f32(minimum[tr * ngroups + grp]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kSelUnroll; ++u) {
+        const int i = base + tok + u * kStep;
+        const float logit = int4_logit(int4_dot32(codes[u], sv[u], mv[u], qr), a.inv_sqrt_d);
+        if (i < c_end && sub == 0) lout[i] = logit;
+      }
+    }
+  }
+  cluster.sync();
+
+  // 4. top-p of the owner's row, then its selection into the leader's bitmap.
+  if (owner) {
+    const int count = top_p_row(s_logit, n, a.top_p, reinterpret_cast<uint32_t*>(s_logit), mass, sel);
+    if (tid == 0) a.head_count[row] = count;
+    if (a.head_pos) {
+      const int seg = (n + blockDim.x - 1) / blockDim.x;
+      const int beg = min(n, tid * seg);
+      const int end = min(n, beg + seg);
+      uint32_t c = 0u;
+      for (int i = beg; i < end; ++i) c += sel[i];
+      uint32_t total;
+      uint32_t slot = block_exclusive_scan(c, scan_scratch, &total);
+      int32_t* hp = a.head_pos + (int64_t)row * n;
+      for (int i = beg; i < end; ++i)
+        if (sel[i]) hp[slot++] = (int32_t)cand_position(s_pages, i, a.block, a.sink);
+    }
+  }
+  cluster.sync();
+  uint32_t* leader_bitmap = cluster.map_shared_rank(bitmap, 0);
+  if (owner && or_selection(leader_bitmap, s_pages, sel, a.b0, a.block, a.sink, L) && a.error_flag)
+    atomicExch(a.error_flag, TW_ERR_INVALID_INDEX);
+  cluster.sync();
+
+  // 5. Sorted union: CTA c writes the positions of words [c*ws, (c+1)*ws).
+  {
+    const int ws = (words + C - 1) / C;
+    const int w_beg = min(words, crank * ws);
+    const int w_end = min(words, w_beg + ws);
+    uint32_t before = 0u;
+    for (int w = tid; w < w_beg; w += blockDim.x) before += __popc(leader_bitmap[w]);
+    uint32_t total_before;
+    block_exclusive_scan(before, scan_scratch, &total_before);
+    if (tid == 0) s_base = total_before;
+    __syncthreads();
+    int32_t* dst = a.union_pos + (int64_t)g * a.pos_stride;
+    uint32_t running = s_base;
+    for (int c0 = w_beg; c0 < w_end; c0 += kTopPThreads) {
+      const int w = c0 + tid;
+      const uint32_t bits = w < w_end ? leader_bitmap[w] : 0u;
+      uint32_t chunk_total;
+      s_woff[tid] = running + block_exclusive_scan((uint32_t)__popc(bits), scan_scratch, &chunk_total);
+      __syncthreads();
+      const int chunk_words = min(kTopPThreads, w_end - c0);
+      for (int j = warp; j < chunk_words; j += nwarps) {
+        const uint32_t word = leader_bitmap[c0 + j];
+        if ((word >> lane) & 1u)
+          dst[s_woff[j] + __popc(word & ((1u << lane) - 1u))] = (c0 + j) * 32 + lane;
+      }
+      running += chunk_total;
+      __syncthreads();
+    }
+    if (crank == C - 1 && tid == 0) a.union_count[g] = (int32_t)running;
+  }
+  cluster.sync();  // the leader's bitmap is read until here
+}
+
+// Whether the fused selection serves this shape (R dividing the cluster, and
+// the shared memory fitting one CTA).
+bool select_fused_supported(int R, int P, int b0, int block, int64_t L, size_t* smem) {
+  if (R <= 0 || kSelCluster % R != 0 || b0 <= 0 || P <= 0) return false;  // R | 8 | 16
+  const int64_t n = (int64_t)b0 * block;
+  if (n > 65536 || L > ((int64_t)1 << 30)) return false;
+  *smem = select_smem_bytes(P, b0, (int)n, L);
+  return *smem <= 160 * 1024;
+}
+
+// Clusters of 16 CTAs when the device can run at least `groups` of them at
+// once (queried once per device and kernel; the kernel needs one SM per CTA
+// at the shared memory the fused selection may use), else clusters of 8.
+template <typename T, typename QT, int R>
+int select_cluster_size(int groups) {
+  static int wide_clusters[kMaxDevices];  // 0: not queried, -1: none
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kSelCluster;
+  std::lock_guard<std::mutex> lk(mu);
+  if (wide_clusters[dev] == 0) {
+    int n = -1;
+    const void* fn = (const void*)select_layer_kernel<T, QT, R>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
+            cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(kSelClusterWide, 1, 1);
+      cfg.blockDim = dim3(kTopPThreads, 1, 1);
+      cfg.dynamicSmemBytes = 160 * 1024;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kSelClusterWide;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int count = 0;
+      if (cudaOccupancyMaxActiveClusters(&count, fn, &cfg) == cudaSuccess && count > 0) n = count;
+    }
+    cudaGetLastError();  // a refused query leaves no error behind
+    wide_clusters[dev] = n;
+  }
+  return wide_clusters[dev] >= groups ? kSelClusterWide : kSelCluster;
+}
+
+template <typename T, typename QT, int R>
+int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t stream) {
+  static DynSmemOptIn opt_in;
+  const int cluster = select_cluster_size<T, QT, R>(groups);
+  const int st = ensure_dyn_smem((const void*)select_layer_kernel<T, QT, R>, opt_in, (int)smem);
+  if (st != TW_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups * cluster, 1, 1);
+  cfg.blockDim = dim3(kTopPThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, select_layer_kernel<T, QT, R>, a);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  return check_launch();
+}
+
+template <typename T, typename QT>
+int launch_select_t(const SelectArgs& a, int groups, int R, size_t smem, cudaStream_t stream) {
+  switch (R) {
+    case 1: return launch_select_r<T, QT, 1>(a, groups, smem, stream);
+    case 2: return launch_select_r<T, QT, 2>(a, groups, smem, stream);
+    case 4: return launch_select_r<T, QT, 4>(a, groups, smem, stream);
+    case 8: return launch_select_r<T, QT, 8>(a, groups, smem, stream);
+    default: return TW_ERR_UNSUPPORTED;
+  }
+}
+
+// The fused selection (q in fp32 or in the K dtype).
+int launch_select_fused(const SelectArgs& a, int groups, int R, int q_dtype, int dtype, size_t smem,
+                        cudaStream_t stream) {
+  if (dtype == TW_F16)
+    return q_dtype == TW_F32 ? launch_select_t<__half, float>(a, groups, R, smem, stream)
+                             : launch_select_t<__half, __half>(a, groups, R, smem, stream);
+  if (dtype == TW_BF16)
+    return q_dtype == TW_F32 ? launch_select_t<__nv_bfloat16, float>(a, groups, R, smem, stream)
+                             : launch_select_t<__nv_bfloat16, __nv_bfloat16>(a, groups, R, smem, stream);
+  return TW_ERR_UNSUPPORTED;
+}
+
+// The whole Twilight selection of one layer in one launch when the shape
+// allows it (R dividing kSelCluster, shared memory fitting a CTA); returns
+// TW_ERR_UNSUPPORTED otherwise, and the caller runs the per-stage kernels.
+// Same arguments and checks as tw_select_layer's stages; q in fp32 or the K dtype.
+int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void* pmax,
+                       int64_t meta_stride, int n_pages, const uint8_t* packed, const void* scale,
+                       const void* minimum, int64_t entry_stride, int groups, int R, int b0,
+                       int block, int sink, int group_size, int dtype, double top_p,
+                       int64_t old_length, int64_t sink_end, int64_t recent_start,
+                       int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
+                       int32_t* union_count, int32_t* head_count, int32_t* head_pos,
+                       int32_t* error_flag, cudaStream_t stream) {
+  if (!q || !pmin || !pmax || !packed || !scale || !minimum || !pages_out || !union_pos ||
+      !union_count || !head_count || groups <= 0 || groups > (1 << 27) || R <= 0 ||
+      n_pages <= 0 || b0 <= 0 || b0 > n_pages || block <= 0 || sink < 0 || old_length < 0 ||
+      !(top_p > 0.0 && top_p <= 1.0) || sink_end < 0 || sink_end > old_length ||
+      recent_start < sink_end || recent_start > old_length || pos_stride < old_length)
+    return TW_ERR_BAD_ARG;
+  if (R > kMaxHeadsPerGroup) return TW_ERR_UNSUPPORTED;
+  if (group_size != 32 && group_size != 64 && group_size != 128) return TW_ERR_UNSUPPORTED;
+  if (dtype != TW_F16 && dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
+  if (q_dtype != TW_F32 && q_dtype != dtype) return TW_ERR_BAD_ARG;
+  size_t smem = 0;
+  if (!select_fused_supported(R, n_pages, b0, block, old_length, &smem)) return TW_ERR_UNSUPPORTED;
+  SelectArgs a{};
+  a.q = q;
+  a.pmin = pmin;
+  a.pmax = pmax;
+  a.meta_stride = meta_stride;
+  a.n_pages = n_pages;
+  a.packed = packed;
+  a.scale = scale;
+  a.minimum = minimum;
+  a.entry_stride = entry_stride;
+  a.group_size = group_size;
+  a.b0 = b0;
+  a.block = block;
+  a.sink = sink;
+  a.top_p = top_p;
+  a.old_length = old_length;
+  a.sink_end = sink_end;
+  a.recent_start = recent_start;
+  a.inv_sqrt_d = inv_sqrt_head_dim(kHeadDim);
+  a.pages_out = pages_out;
+  a.union_pos = union_pos;
+  a.pos_stride = pos_stride;
+  a.union_count = union_count;
+  a.head_count = head_count;
+  a.head_pos = head_pos;
+  a.error_flag = error_flag;
+  return launch_select_fused(a, groups, R, q_dtype, dtype, smem, stream);
 }
 
 }  // namespace tw

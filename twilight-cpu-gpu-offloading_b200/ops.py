@@ -150,6 +150,36 @@ def top_p_union(logits: torch.Tensor, pages: torch.Tensor, *, block_size: int, s
         _ptr(head_pos), _ptr(error_flag), _stream(logits.device)), "top_p_union")
 
 
+def select_layer(q: torch.Tensor, page_min: torch.Tensor, page_max: torch.Tensor, n_pages: int,
+                 packed: torch.Tensor, scale: torch.Tensor, minimum: torch.Tensor, *, b0_pages: int,
+                 block_size: int, sink: int, top_p: float, old_length: int, sink_end: int,
+                 recent_start: int, union_pos: torch.Tensor, union_count: torch.Tensor,
+                 head_count: torch.Tensor, head_pos: torch.Tensor | None = None,
+                 error_flag: torch.Tensor | None = None,
+                 pages: torch.Tensor | None = None) -> torch.Tensor:
+    """Both Twilight selection stages of one layer (tw_select_layer: Quest score,
+    top-k pages, INT4 estimate, top-p + GQA union; one fused launch where the
+    shape allows).  q [G,R,D] fp32, metadata / codes as quest_score / int4_qk.
+    Returns the B0 pages [G,R,b0] int32; the union and counts go to the outputs."""
+    _cuda(q, page_min, page_max, packed, scale, minimum, union_pos, union_count, head_count,
+          head_pos, error_flag, pages)
+    G, R, D = q.shape
+    if q.dtype != torch.float32:
+        raise ValueError("select_layer expects fp32 q [G,R,D]")
+    if pages is None:
+        pages = torch.empty((G, R, b0_pages), device=q.device, dtype=torch.int32)
+    ws_bytes = select_layer_workspace_bytes(G, R, n_pages, b0_pages, block_size)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+    _lib.check(lib().tw_select_layer(
+        _ptr(q), _ptr(page_min), _ptr(page_max), page_min.shape[1] * D, n_pages, _ptr(packed),
+        _ptr(scale), _ptr(minimum), packed.shape[1], G, R, b0_pages, block_size, sink, D,
+        D // scale.shape[-1], _kv_code(scale.dtype), float(top_p), old_length, sink_end,
+        recent_start, _ptr(pages), _ptr(union_pos), union_pos.shape[-1], _ptr(union_count),
+        _ptr(head_count), _ptr(head_pos), _ptr(error_flag), _ptr(ws), ws.numel(),
+        _stream(q.device)), "select_layer")
+    return pages
+
+
 def select_layer_workspace_bytes(groups: int, heads: int, n_pages: int, b0_pages: int,
                                  block_size: int) -> int:
     return int(lib().tw_select_layer_workspace_size(groups, heads, n_pages, b0_pages, block_size))
