@@ -429,13 +429,15 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
     slab.close()
 
 
-@pytest.mark.parametrize("R", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("R,L,budget", [(1, 3007, 768), (2, 3014, 768), (3, 3021, 768),
+                                         (4, 3028, 768), (8, 3056, 768), (8, 131072, 4096)])
 @pytest.mark.parametrize("dtype,group", [("float16", 32), ("bfloat16", 128), ("bfloat16", 64)])
-def test_select_layer_fused_equals_stages(tw, cuda, R, dtype, group):
+def test_select_layer_fused_equals_stages(tw, cuda, R, L, budget, dtype, group):
     """tw_select_layer (one cluster launch per layer when R divides the cluster)
     gives the per-stage kernels' pages, per-head counts and positions and the
-    union, bit for bit; R = 3 exercises the per-stage fallback."""
-    G, L, sink, recent, block = 3, 3000 + 7 * R, 64, 256, 16
+    union, bit for bit; R = 3 exercises the per-stage fallback, 131072 tokens
+    with B0 4096 the config-5 shape."""
+    G, sink, recent, block = 3 if L < 100000 else 2, 64, 256, 16
     layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=dtype, seed=70 + R,
                              workload="needles" if R % 2 else "outliers", sink=sink,
                              recent=recent, block=block, n_needles=6)
@@ -450,7 +452,7 @@ def test_select_layer_fused_equals_stages(tw, cuda, R, dtype, group):
     scale = torch.zeros((G, L + 64, 128 // group), dtype=dt, device=cuda)
     minimum = torch.zeros_like(scale)
     tw.ops.int4_pack(keys, group_size=group, packed=packed, scale=scale, minimum=minimum)
-    w = torch_ref.window(L, sink=sink, recent=recent, block=block, candidate_token_budget=768,
+    w = torch_ref.window(L, sink=sink, recent=recent, block=block, candidate_token_budget=budget,
                          metadata_pages=P_built)
     q = layer.queries.float().to(cuda)
     n = w.b0_pages * block

@@ -69,7 +69,8 @@ __device__ __forceinline__ void quest_page_score2(const float (&qr)[R][4], const
 
 // INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
 // covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
-// k = code * s + m (separately rounded), acc += k * q in channel order.
+// k = code * s + m (the values of separately rounded mul and add), acc += k * q
+// (separately rounded) in channel order.  s and m are fp16 / bf16 values.
 // A code v in 0..15 as float, exactly: the bits 0x4B0000vv are the float
 // 2^23 + v, from which 2^23 is subtracted (exact).  One byte permute puts
 // byte b of `nibbles` (one code per byte) under the exponent 0x4B.
@@ -89,9 +90,12 @@ __device__ __forceinline__ float int4_dot32(const uint4& codes, float s, float m
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       const int i = 8 * w + 2 * b;
-      const float k0 = __fadd_rn(__fmul_rn(nibble_float(lo, b), s), m);
+      // code * s is exact in fp32 (a 4-bit integer times a value of at most
+      // 11 significant bits), so the fused multiply-add rounds exactly as the
+      // separately rounded code * s + m does.
+      const float k0 = __fmaf_rn(nibble_float(lo, b), s, m);
       acc = __fadd_rn(acc, __fmul_rn(k0, qr[i]));
-      const float k1 = __fadd_rn(__fmul_rn(nibble_float(hi, b), s), m);
+      const float k1 = __fmaf_rn(nibble_float(hi, b), s, m);
       acc = __fadd_rn(acc, __fmul_rn(k1, qr[i + 1]));
     }
   }

@@ -644,10 +644,14 @@ select_layer_kernel(SelectArgs a) {
     float* owner_scores[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) owner_scores[r] = cluster.map_shared_rank(s_score, r);
+    // CTA crank scores the contiguous pages [p_beg, p_end)
+    const int per_cta = (P + C - 1) / C;
+    const int p_beg = min(P, crank * per_cta);
+    const int p_end = min(P, p_beg + per_cta);
     // two pages per warp and pass: both pages' loads are issued together
-    const int stride = C * nwarps;
-    for (int p = crank * nwarps + warp; p < P; p += 2 * stride) {
-      const int p2 = p + stride;
+    const int stride = nwarps;
+    for (int p = p_beg + warp; p < p_end; p += 2 * stride) {
+      const int p2 = p + stride < p_end ? p + stride : P;
       float sc[R], sc2[R];
       if (p2 < P) {
         quest_page_score2<T, R>(qr, gmin, gmax, p, p2, lane, sc, sc2);
