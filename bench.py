@@ -157,7 +157,7 @@ class DeviceStep:
     """The hot path launched through the C ABI on fixed device buffers."""
 
     def __init__(self, tw, layer, device: torch.device, fused: bool = True,
-                 reuse: bool = False, n_steps: int = 0) -> None:
+                 reuse: bool = False, n_steps: int = 0, numa=None) -> None:
         self.tw = tw
         self.fused = fused
         self.reuse = reuse
@@ -169,7 +169,7 @@ class DeviceStep:
         self.device = device
         self.max_len = L + 64
         geom = tw.SlabGeometry(num_entries=G, batch_size=1, max_cache_len=self.max_len, head_dim=128)
-        self.slab = tw.MappedHostSlab(geom, torch.float16)
+        self.slab = tw.MappedHostSlab(geom, torch.float16, numa_node=numa)
         self.slab.rows[0, :, :L].copy_(layer.keys)
         self.slab.rows[1, :, :L].copy_(layer.values)
         sink, block = CFG["sink"], CFG["block"]
@@ -211,7 +211,8 @@ class DeviceStep:
         self.q16 = torch.empty((G, R, 128), dtype=torch.float16, device=device)
         self.k_new = layer.key_new.to(device)
         self.v_new = layer.value_new.to(device)
-        self.launches_per_step = 6 if fused else 7
+        # fused selection (1 launch) + fused attention or gather + attention + append
+        self.launches_per_step = 3 if fused else 4
         self.t = 0
         if reuse:
             # ping-pong: step t keeps its rows in slot t % 2 under tag t + 1 and
@@ -333,7 +334,7 @@ def run_ours(args) -> int:
     B = min(K, 10)  # extra steps with per-stage events (kept out of the timed steps)
     layer, queries = build_workload(tw, device, seed=rank, n_queries=K + W + B, rho=rho)
     step = DeviceStep(tw, layer, device, fused=not args.staged, reuse=args.reuse,
-                      n_steps=K + W + B)
+                      n_steps=K + W + B, numa=args.numa)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     torch.cuda.synchronize()
 
@@ -410,7 +411,8 @@ def run_ours(args) -> int:
     if rank == 0:
         pinned = pinned_h2d_peak_gbs(device)
         mapped = mapped_read_peak_gbs(tw, step, device)
-        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W, reuse=args.reuse)
+        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W, reuse=args.reuse,
+                                               numa=args.numa)
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
     if world > 1:
@@ -456,6 +458,8 @@ def run_ours(args) -> int:
                 "mean_union_rows": avg["union_rows"],
                 "queries": (f"AR(1) rho={rho} (step-to-step continuity)" if step.reuse
                             else "independent N(0,1) per step"),
+                "slab_numa": {"requested": args.numa, "bound_node": step.slab.numa_node,
+                              "page_node": step.slab.page_node(0)},
             },
             "clocks": clocks,
             "gpu_launches": step.launches_per_step * K * world,
@@ -525,7 +529,7 @@ def mapped_read_peak_gbs(tw, step: DeviceStep, device) -> float:
     return best
 
 
-def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False) -> dict:
+def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False, numa=None) -> dict:
     """Same step through the public cache API with host buffers: per step H2D of
     the query and the new token's K/V from pinned memory, prepare_layer_selection
     + attend_layer, D2H of the attention output."""
@@ -535,7 +539,8 @@ def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False) -> dict:
         dtype=torch.float16, device=device, sink_tokens=CFG["sink"], recent_tokens=CFG["recent"],
         block_size=CFG["block"], candidate_token_budget=CFG["b0_tokens"], top_p=CFG["top_p"],
         budget_mode="dynamic", layer_batched_selection=True, gqa_groupwise_execution=True,
-        qk_backend="cuda", int4_group_size=CFG["int4_group"], previous_token_resident_cache=reuse)
+        qk_backend="cuda", int4_group_size=CFG["int4_group"], previous_token_resident_cache=reuse,
+        host_numa_node=numa)
     for e in range(G):
         cache.update(layer.keys[e].view(1, 1, L, 128).to(device),
                      layer.values[e].view(1, 1, L, 128).to(device), e)
@@ -800,10 +805,112 @@ def run_cfg5(args) -> int:
                                    "INT4 g32, B0 4096, top-p 0.95, KV heads 0-1 resident, "
                                    f"{layers} layers cycled",
                        "parallelism": f"KV-head sharded over {world} GPU(s) + NCCL all-gather"},
-            "gpu_launches": 6 * K * world}), flush=True)
+            "gpu_launches": 3 * K * world}), flush=True)
     cache.synchronize()
     cache.close()
     dist.destroy_process_group()
+    return 0
+
+
+CFG4 = dict(requests=16, per_gpu=2, kv_heads=8, heads=4, ctx_lo=8192, ctx_hi=131072,
+            dtype="bfloat16", b0_tokens=2048, top_p=0.9, int4_group=32)
+
+
+def cfg4_contexts() -> list[int]:
+    """The 16 request contexts of config 4: seeded U[8192, 131072], rounded down
+    to a multiple of 16."""
+    g = torch.Generator().manual_seed(4)
+    raw = torch.randint(CFG4["ctx_lo"], CFG4["ctx_hi"] + 1, (CFG4["requests"],), generator=g)
+    return [int(x) // 16 * 16 for x in raw]
+
+
+def run_cfg4(args) -> int:
+    """batched multi-request decode sharded by request.  Rank
+    r serves requests 2r and 2r+1 of the 16 (weak scaling: N = 8 covers all 16),
+    each request one layer of 8 KV x 4 Q heads over its own pinned slab; a step
+    runs one sparse layer-step (decode_layer) per request.  bf16 K/V ~ N(0,1)
+    with 8 needle rows (x4) per head at seeded random positions."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    K, W = args.steps, args.warmup
+    G, R = CFG4["kv_heads"], CFG4["heads"]
+    ctxs = cfg4_contexts()
+    mine = [(2 * rank + i) % CFG4["requests"] for i in range(CFG4["per_gpu"])]
+    caches, steps = [], []
+    gen = torch.Generator(device=device).manual_seed(400 + rank)
+    for req in mine:
+        L = ctxs[req]
+        cache = tw.TwilightMatchedBudgetOffloadedCache(
+            num_cache_entries=G, max_cache_len=L + K + W + 16, head_dim=128,
+            num_query_heads_per_kv=R, dtype=torch.bfloat16, device=device,
+            candidate_token_budget=CFG4["b0_tokens"], top_p=CFG4["top_p"], budget_mode="dynamic",
+            layer_batched_selection=True, gqa_groupwise_execution=True, qk_backend="cuda",
+            int4_group_size=CFG4["int4_group"], host_numa_node=args.numa)
+        for h in range(G):
+            gh = torch.Generator(device=device).manual_seed(1_000 * req + h)
+            k = torch.randn(L, 128, generator=gh, device=device)
+            pos = torch.randint(0, L, (8,), generator=gh, device=device)
+            k[pos] *= 4.0
+            v = torch.randn(L, 128, generator=gh, device=device)
+            cache.update(k.to(torch.bfloat16).view(1, 1, L, 128), v.to(torch.bfloat16).view(1, 1, L, 128), h)
+            del k, v
+        caches.append(cache)
+        steps.append([(torch.randn(G, R, 128, generator=gen, device=device).to(torch.bfloat16),
+                       torch.randn(G, 128, generator=gen, device=device).to(torch.bfloat16),
+                       torch.randn(G, 128, generator=gen, device=device).to(torch.bfloat16))
+                      for _ in range(K + W)])
+    outs = [torch.empty((G, R, 128), dtype=torch.bfloat16, device=device) for _ in caches]
+    entries = list(range(G))
+    torch.cuda.synchronize()
+    for i in range(W):
+        for c, st, o in zip(caches, steps, outs):
+            c.decode_layer(queries=st[i][0], key_states=st[i][1], value_states=st[i][2],
+                           entries=entries, out=o)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(K):
+        for c, st, o in zip(caches, steps, outs):
+            c.decode_layer(queries=st[W + i][0], key_states=st[W + i][1], value_states=st[W + i][2],
+                           entries=entries, out=o)
+    e.record()
+    torch.cuda.synchronize()
+    total_ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    for c in caches:
+        c.synchronize()
+    if rank == 0:
+        n_steps = K * len(mine) * world
+        print(json.dumps({
+            "metric": METRIC, "workload": "cfg4", "value": round(n_steps / (total_ms * 1e-3), 3),
+            "unit": "layer-steps/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(total_ms / K, 5),
+            "us_per_layer_step": round(total_ms / K / len(mine) * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 K/V, fp32 math", "data": "synthetic (seeded torch.randn on the GPU, needles)",
+            "config": {"workload": "cfg4: 2 requests per GPU of 16, ctx U[8192,131072] (seeded) "
+                                   "rounded to 16, 8 KV x 4 Q heads, bf16, INT4 g32, B0 2048, "
+                                   "top-p 0.9, one layer-step per request per step",
+                       "contexts_rank0": [ctxs[r] for r in mine],
+                       "parallelism": f"request-sharded over {world} GPU(s), no collective"},
+            "gpu_launches": 3 * n_steps}), flush=True)
+    for c in caches:
+        c.close()
+    if world > 1:
+        dist.destroy_process_group()
     return 0
 
 
@@ -963,7 +1070,7 @@ def run_cfg3(args) -> int:
                    "model_gemms": "torch / cuBLAS (o_proj, MLP, LM head); q/k/v projection + RoPE is "
                                   "tw_qkv_rope"},
         "clocks": clocks,
-        "gpu_launches_per_token": CFG3["layers"] * 7,
+        "gpu_launches_per_token": CFG3["layers"] * 4,  # qkv_rope + decode_layer's 3
         "front_end": {"kernel": "qkv_rope_kernel (q/k/v GEMV + RoPE, one launch per layer)",
                       "us": round(fe_us, 2), "bytes": fe_bytes,
                       "achieved_gbs": round(fe_bytes / (fe_us * 1e-6) / 1e9, 1),
@@ -989,13 +1096,17 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2",
                     help="cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
-                         "decode, TPOT) or cfg5 (head-sharded 70B layer)")
+                         "decode, TPOT), cfg4 (request-sharded batch of 16 requests) or cfg5 "
+                         "(head-sharded 70B layer)")
     ap.add_argument("--reuse", action="store_true",
                     help="previous-token row reuse (fused path) with AR(1) query continuity")
     ap.add_argument("--reuse-rho", type=float, default=0.98,
                     help="AR(1) coefficient of the query sequence under --reuse")
+    ap.add_argument("--numa", default=None,
+                    help="pin the K/V slab on a host NUMA node: 'auto' (the GPU's closest node) "
+                         "or a node id; default: cudaHostAlloc's placement")
     ap.add_argument("--staged", action="store_true",
                     help="time the staged path (gather to HBM, then attention) instead of the fused kernel")
     args = ap.parse_args()
@@ -1007,6 +1118,8 @@ def main() -> int:
         return run_cfg5(args)
     if args.workload == "cfg3":
         return run_cfg3(args)
+    if args.workload == "cfg4":
+        return run_cfg4(args)
     return run_ours(args)
 
 

@@ -66,6 +66,18 @@ int tw_abi_version(void);
  * cudaHostGetDevicePointer mapping of its zero-copy path
  * (hi/resident_zero_copy.py:15-29).  *device_ptr is what kernels read. */
 int tw_host_alloc_mapped(size_t bytes, void** host_ptr, void** device_ptr);
+/* The same on one host NUMA node: anonymous memory bound to `numa_node` (-1:
+ * the node closest to the current device, cudaDevAttrHostNumaId) before
+ * first touch, then page-locked and mapped with cudaHostRegister.  The slab
+ * placement of the reference's multi-GPU plan (each GPU's slab on its own
+ * NUMA node; hi/slab_cache.py:37-74 allocates without placement).
+ * *bound_node (nullable) receives the node the memory was bound to, or -1
+ * when the system refused the binding (the memory is then placed by the
+ * default policy).  Freed with tw_host_free. */
+int tw_host_alloc_mapped_numa(size_t bytes, int numa_node, void** host_ptr, void** device_ptr,
+                              int* bound_node);
+/* Host NUMA node holding the page at host_ptr (TW_ERR_UNSUPPORTED without NUMA). */
+int tw_host_numa_node(const void* host_ptr, int* node);
 int tw_host_free(void* host_ptr);
 /* Device address of memory that is already pinned (e.g. torch pin_memory). */
 int tw_host_device_pointer(void* host_ptr, void** device_ptr);

@@ -70,6 +70,9 @@ SIGNATURES = {
     "tw_last_cuda_error": (I32, []),
     "tw_abi_version": (I32, []),
     "tw_host_alloc_mapped": (I32, [SZ, ctypes.POINTER(P), ctypes.POINTER(P)]),
+    "tw_host_alloc_mapped_numa": (I32, [SZ, I32, ctypes.POINTER(P), ctypes.POINTER(P),
+                                        ctypes.POINTER(I32T)]),
+    "tw_host_numa_node": (I32, [P, ctypes.POINTER(I32T)]),
     "tw_host_free": (I32, [P]),
     "tw_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "tw_quest_page_metadata": (I32, [P, I64, I32, I32, I32, I32, I32, I32, I32, P, P, I64, P]),

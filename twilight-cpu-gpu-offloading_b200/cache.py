@@ -46,6 +46,9 @@ class QuestTopKOffloadedCache:
     GPU-resident heads; all other entries live in the pinned, mapped host slab).
     Kernels find each entry's rows through a device directory [2, E] of row-0
     addresses, so resident and offloaded heads share one code path.
+    ``host_numa_node`` ("auto" or a node id) pins the slab on that host NUMA
+    node ("auto": the node closest to the cache's GPU) instead of the default
+    cudaHostAlloc placement.
     """
 
     def __init__(self, *, num_cache_entries: int, max_cache_len: int, head_dim: int,
@@ -57,7 +60,8 @@ class QuestTopKOffloadedCache:
                  sparse_gather_stabilized: bool = False,
                  per_head_varlen_attention_reference: bool = False,
                  incremental_page_metadata: bool = False,
-                 resident_entries: Optional[Any] = None, **ignored: Any) -> None:
+                 resident_entries: Optional[Any] = None,
+                 host_numa_node: Optional[Any] = None, **ignored: Any) -> None:
         device = torch.device(device)
         if device.type != "cuda" or not torch.cuda.is_available():
             raise ValueError("an operational CUDA device is required")
@@ -111,7 +115,7 @@ class QuestTopKOffloadedCache:
         self._seen_tokens = 0
         self._prompt_length: Optional[int] = None
 
-        self._slab = MappedHostSlab(self.geometry, dtype)
+        self._slab = MappedHostSlab(self.geometry, dtype, numa_node=host_numa_node)
         res = sorted(set(int(e) for e in (resident_entries or ())))
         if any(not 0 <= e < num_cache_entries for e in res):
             raise ValueError("resident_entries outside [0, num_cache_entries)")
@@ -522,6 +526,7 @@ class QuestTopKOffloadedCache:
             "allocated_capacity": self.allocated_capacity,
             "initialized_entries": sum(self._initialized),
             "host_slab_bytes": self._slab.nbytes,
+            "host_slab_numa_node": self._slab.numa_node,
             "host_slab_pinned": True,
             "host_slab_device_mapped": True,
             "metadata_gpu_bytes": 2 * self._page_min.numel() * self._page_min.element_size(),

@@ -1,5 +1,11 @@
 // C ABI glue: status text, mapped host slab allocation and the whole-layer
 // Twilight selection that chains the Quest and INT4/top-p kernels.
+#include <sys/mman.h>
+#include <sys/syscall.h>
+#include <unistd.h>
+
+#include <unordered_map>
+
 #include "tw_common.cuh"
 
 namespace tw {
@@ -90,8 +96,100 @@ extern "C" int tw_host_alloc_mapped(size_t bytes, void** host_ptr, void** device
   return TW_OK;
 }
 
+// ---- NUMA-placed slabs -----------------------------------------------------------------------
+// Anonymous memory bound to one host NUMA node (mbind before first touch),
+// then page-locked and mapped for the GPU with cudaHostRegister.  Regions are
+// remembered so that tw_host_free unregisters and unmaps them.
+namespace tw {
+namespace {
+std::mutex g_numa_mu;
+std::unordered_map<void*, size_t> g_numa_regions;
+constexpr long kMpolBind = 2;      // MPOL_BIND
+constexpr long kMpolFNode = 1;     // MPOL_F_NODE
+constexpr long kMpolFAddr = 2;     // MPOL_F_ADDR
+}  // namespace
+}  // namespace tw
+
+extern "C" int tw_host_alloc_mapped_numa(size_t bytes, int numa_node, void** host_ptr,
+                                         void** device_ptr, int* bound_node) {
+  if (!host_ptr || !device_ptr || bytes == 0) return TW_ERR_BAD_ARG;
+  *host_ptr = nullptr;
+  *device_ptr = nullptr;
+  if (bound_node) *bound_node = -1;
+  int node = numa_node;
+  if (node < 0) {
+    int dev = 0, id = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&id, cudaDevAttrHostNumaId, dev) == cudaSuccess)
+      node = id;
+    cudaGetLastError();
+  }
+  const size_t align = (size_t)2 << 20;
+  const size_t len = (bytes + align - 1) / align * align;
+  void* h = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+  if (h == MAP_FAILED) return TW_ERR_CAPACITY;
+  madvise(h, len, MADV_HUGEPAGE);
+  if (node >= 0 && node < 1024) {
+    unsigned long mask[1024 / (8 * sizeof(unsigned long))] = {};
+    mask[node / (8 * sizeof(unsigned long))] = 1ul << (node % (8 * sizeof(unsigned long)));
+    if (syscall(SYS_mbind, h, len, kMpolBind, mask, (unsigned long)(node + 2), 0ul) == 0 &&
+        bound_node)
+      *bound_node = node;
+  }
+  cudaError_t err = cudaHostRegister(h, len, cudaHostRegisterMapped | cudaHostRegisterPortable);
+  if (err != cudaSuccess) {
+    munmap(h, len);
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  void* d = nullptr;
+  err = cudaHostGetDevicePointer(&d, h, 0);
+  if (err != cudaSuccess) {
+    cudaHostUnregister(h);
+    munmap(h, len);
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_numa_mu);
+    g_numa_regions[h] = len;
+  }
+  *host_ptr = h;
+  *device_ptr = d;
+  return TW_OK;
+}
+
+extern "C" int tw_host_numa_node(const void* host_ptr, int* node) {
+  if (!host_ptr || !node) return TW_ERR_BAD_ARG;
+  int n = -1;
+  if (syscall(SYS_get_mempolicy, &n, nullptr, 0ul, host_ptr, kMpolFNode | kMpolFAddr) != 0) {
+    *node = -1;
+    return TW_ERR_UNSUPPORTED;
+  }
+  *node = n;
+  return TW_OK;
+}
+
 extern "C" int tw_host_free(void* host_ptr) {
   if (!host_ptr) return TW_OK;
+  size_t numa_len = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_numa_mu);
+    auto it = g_numa_regions.find(host_ptr);
+    if (it != g_numa_regions.end()) {
+      numa_len = it->second;
+      g_numa_regions.erase(it);
+    }
+  }
+  if (numa_len) {
+    const cudaError_t e = cudaHostUnregister(host_ptr);
+    munmap(host_ptr, numa_len);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return TW_ERR_CUDA;
+    }
+    return TW_OK;
+  }
   cudaError_t err = cudaFreeHost(host_ptr);
   if (err != cudaSuccess) {
     set_last_cuda_error(err);

@@ -130,7 +130,10 @@ class MappedHostSlab:
     ``host`` is a CPU tensor over the pinned pages; ``device_ptr`` is the address
     kernels use.  Freed with ``close()`` (or when garbage collected)."""
 
-    def __init__(self, geometry: SlabGeometry, dtype: torch.dtype) -> None:
+    def __init__(self, geometry: SlabGeometry, dtype: torch.dtype,
+                 numa_node: int | str | None = None) -> None:
+        """numa_node: None = cudaHostAlloc's default placement; "auto" = the host
+        NUMA node closest to the current GPU; an int = that node."""
         self.geometry = geometry
         self.dtype = dtype
         itemsize = torch.tensor([], dtype=dtype).element_size()
@@ -138,8 +141,17 @@ class MappedHostSlab:
         lib = _lib.load()
         host = ctypes.c_void_p()
         dev = ctypes.c_void_p()
-        _lib.check(lib.tw_host_alloc_mapped(self.nbytes, ctypes.byref(host), ctypes.byref(dev)),
-                   "tw_host_alloc_mapped")
+        self.numa_node: int | None = None
+        if numa_node is None:
+            _lib.check(lib.tw_host_alloc_mapped(self.nbytes, ctypes.byref(host), ctypes.byref(dev)),
+                       "tw_host_alloc_mapped")
+        else:
+            want = -1 if numa_node == "auto" else int(numa_node)
+            bound = ctypes.c_int32(-1)
+            _lib.check(lib.tw_host_alloc_mapped_numa(self.nbytes, want, ctypes.byref(host),
+                                                     ctypes.byref(dev), ctypes.byref(bound)),
+                       "tw_host_alloc_mapped_numa")
+            self.numa_node = bound.value if bound.value >= 0 else None
         self._host_ptr = host.value
         self.device_ptr = dev.value
         buf = (ctypes.c_uint8 * self.nbytes).from_address(self._host_ptr)
@@ -147,6 +159,12 @@ class MappedHostSlab:
         self.host = torch.frombuffer(buf, dtype=torch.uint8).view(dtype)
         self.rows = self.host.view(2, geometry.num_entries, geometry.max_cache_len,
                                    geometry.head_dim)
+
+    def page_node(self, offset: int = 0) -> int | None:
+        """Host NUMA node of the page holding byte `offset` of the slab, if known."""
+        node = ctypes.c_int32(-1)
+        st = _lib.load().tw_host_numa_node(ctypes.c_void_p(self._host_ptr + offset), ctypes.byref(node))
+        return node.value if st == _lib.TW_OK and node.value >= 0 else None
 
     @property
     def key_device_ptr(self) -> int:
