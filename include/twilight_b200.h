@@ -82,6 +82,16 @@ int tw_host_free(void* host_ptr);
 /* Device address of memory that is already pinned (e.g. torch pin_memory). */
 int tw_host_device_pointer(void* host_ptr, void** device_ptr);
 
+/* ---- slab writes -------------------------------------------------------------
+ * Rows [0, n_rows) of n_entries consecutive entries, entry e at
+ * src + e*src_entry_stride_rows*row_bytes, to dst + e*dst_entry_stride_rows*row_bytes
+ * (device or mapped host memory) with one pitched copy on `stream`: the
+ * prefill write of K / V into the slab (QuestTopKOffloadedCache's D2H,
+ * hi/quest_offload_cache.py:513-537) for a whole layer of entries at once. */
+int tw_slab_write_rows(const void* src, int64_t src_entry_stride_rows, void* dst,
+                       int64_t dst_entry_stride_rows, int n_entries, int64_t n_rows,
+                       int64_t row_bytes, void* stream);
+
 /* ---- Quest metadata ----------------------------------------------------------
  * Page-wise channel min/max of K over complete block_size pages after the sink.
  * Replaces QuestTopKOffloadedCache._build_metadata (hi/quest_offload_cache.py:276-289).

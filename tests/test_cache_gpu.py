@@ -321,3 +321,41 @@ def test_resident_heads_match_offloaded(tw, cuda):
     for c in (plain, mixed):
         c.synchronize()
         c.close()
+
+
+@pytest.mark.parametrize("resident", [(), (1, 2)])
+def test_prefill_layer_equals_per_entry_update(tw, cuda, resident):
+    """prefill_layer (one metadata / INT4 launch per layer, pitched slab copies
+    on a side stream) leaves the slab, the resident K/V, the page metadata and
+    the INT4 codes exactly as per-entry update() does, and decodes identically."""
+    G, R, L = 4, 4, 2000
+    d = layer_data(1, G, R, L, "bfloat16", 88)[0]
+    caches = [make_twilight(tw, cuda, layers=1, G=G, R=R, L=L, dtype=torch.bfloat16, extra=4,
+                            resident_entries=list(resident)) for _ in range(2)]
+    for g in range(G):
+        caches[0].update(d.keys[g].view(1, 1, L, 128).to(cuda), d.values[g].view(1, 1, L, 128).to(cuda), g)
+    caches[1].prefill_layer(key_states=d.keys.view(1, G, L, 128).to(cuda),
+                            value_states=d.values.view(1, G, L, 128).to(cuda), entries=list(range(G)))
+    torch.cuda.synchronize()
+    a, b = caches
+    for g in range(G):
+        for kind in ("key", "value"):
+            assert torch.equal(a.entry_kv(kind, g)[:L].cpu(), b.entry_kv(kind, g)[:L].cpu())
+    # pages with metadata: the complete pages after the sink plus the partial page
+    pages = -(-(L - a.sink_tokens) // a.block_size)
+    for name in ("_page_min", "_page_max"):
+        assert torch.equal(getattr(a, name)[:, :pages], getattr(b, name)[:, :pages]), name
+    for name in ("_packed", "_scale", "_minimum"):
+        assert torch.equal(getattr(a, name)[:, :L], getattr(b, name)[:, :L]), name
+    assert a._meta_pages == b._meta_pages and a.get_seq_length(0) == b.get_seq_length(0) == L
+    q, kn, vn = _step_inputs(cuda, G, R, "bfloat16", 5)
+    q, kn, vn = q.to(cuda), kn.to(cuda), vn.to(cuda)
+    outs = [c.decode_layer(queries=q, key_states=kn, value_states=vn, entries=list(range(G)))
+            for c in caches]
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    with pytest.raises((ValueError, RuntimeError)):
+        b.prefill_layer(key_states=d.keys.view(1, G, L, 128).to(cuda),
+                        value_states=d.values.view(1, G, L, 128).to(cuda), entries=list(range(G)))
+    for c in caches:
+        c.close()

@@ -74,6 +74,7 @@ SIGNATURES = {
                                         ctypes.POINTER(I32T)]),
     "tw_host_numa_node": (I32, [P, ctypes.POINTER(I32T)]),
     "tw_host_free": (I32, [P]),
+    "tw_slab_write_rows": (I32, [P, I64, P, I64, I32, I64, I64, P]),
     "tw_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "tw_quest_page_metadata": (I32, [P, I64, I32, I32, I32, I32, I32, I32, I32, P, P, I64, P]),
     "tw_int4_pack": (I32, [P, I64, I32, I64, I32, I32, I32, P, P, P, I64, I64, P]),

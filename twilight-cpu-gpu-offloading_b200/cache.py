@@ -244,25 +244,93 @@ class QuestTopKOffloadedCache:
     def _build_metadata(self, entry: int, key_states: torch.Tensor) -> None:
         """Quest page min/max of the prompt (hi/quest_offload_cache.py:276-289) plus
         the running min/max of the trailing partial page, continued on append."""
-        keys = key_states[0, 0].contiguous()
-        S = int(keys.shape[0])
+        self._build_metadata_entries(entry, key_states[0, 0].unsqueeze(0))
+
+    def _build_metadata_entries(self, first: int, keys: torch.Tensor) -> None:
+        """_build_metadata for entries first .. first + G - 1 at once; keys [G, S, D]."""
+        keys = keys.contiguous()
+        G, S = int(keys.shape[0]), int(keys.shape[1])
         complete = max(0, S - self.sink_tokens) // self.block_size if S > self.sink_tokens else 0
         if complete:
             _lib.check(_lib.load().tw_quest_page_metadata(
-                keys.data_ptr(), S * HEAD_DIM, 1, self.sink_tokens, self.block_size, HEAD_DIM,
+                keys.data_ptr(), S * HEAD_DIM, G, self.sink_tokens, self.block_size, HEAD_DIM,
                 ops._kv_code(self.dtype), 0, complete,
-                self._page_min[entry].data_ptr(), self._page_max[entry].data_ptr(),
+                self._page_min[first].data_ptr(), self._page_max[first].data_ptr(),
                 self.page_capacity * HEAD_DIM, self._stream()), "quest_page_metadata")
         partial = S - self.sink_tokens - complete * self.block_size if S > self.sink_tokens else 0
         if partial > 0 and complete < self.page_capacity:
             off = complete * HEAD_DIM * keys.element_size()
             _lib.check(_lib.load().tw_quest_page_metadata(
-                keys.data_ptr(), S * HEAD_DIM, 1, self.sink_tokens + complete * self.block_size,
+                keys.data_ptr(), S * HEAD_DIM, G, self.sink_tokens + complete * self.block_size,
                 partial, HEAD_DIM, ops._kv_code(self.dtype), 0, 1,
-                self._page_min[entry].data_ptr() + off, self._page_max[entry].data_ptr() + off,
+                self._page_min[first].data_ptr() + off, self._page_max[first].data_ptr() + off,
                 self.page_capacity * HEAD_DIM, self._stream()), "quest_page_metadata")
-        self._meta_pages[entry] = complete
+        for e in range(first, first + G):
+            self._meta_pages[e] = complete
         self._meta_version += 1
+
+    def prefill_layer(self, *, key_states: torch.Tensor, value_states: torch.Tensor,
+                      entries: list[int]) -> None:
+        """Prefill of one layer's KV heads at once: the per-entry update() of every
+        entry in `entries` (same results), with the Quest metadata (and INT4
+        codes) of all entries in one launch each, and the K / V rows written to
+        the slab by one pitched copy per plane on a side stream, so that the copy
+        engine runs while the metadata kernels do.  key_states / value_states
+        [1, G, S, D] or [G, S, D] on the cache device, in the cache dtype."""
+        keys = key_states.reshape(-1, *key_states.shape[-2:])
+        vals = value_states.reshape(-1, *value_states.shape[-2:])
+        G = len(entries)
+        if keys.shape != vals.shape or keys.shape[0] != G or keys.shape[-1] != HEAD_DIM:
+            raise ValueError("expected [1, G, S, D] K/V for the G entries")
+        if keys.device != self.device or keys.dtype != self.dtype or vals.dtype != self.dtype:
+            raise ValueError("K/V must be on the cache device in the cache dtype")
+        S = int(keys.shape[1])
+        if S <= 1:
+            raise ValueError("prefill needs more than one token")
+        first = _contiguous_entries(entries)
+        self._bookkeeping.preview(first, S)  # strict entry order and capacity
+        if any(self._logical_lengths[e] != 0 for e in entries):
+            raise ValueError("chunked/multiple prefill updates are unsupported")
+        if self._prompt_length is not None and self._prompt_length != S:
+            raise RuntimeError("cache entries received unequal prompt lengths")
+        keys, vals = keys.contiguous(), vals.contiguous()
+        main = torch.cuda.current_stream(self.device)
+        side = getattr(self, "_prefill_stream", None)
+        if side is None:
+            side = self._prefill_stream = torch.cuda.Stream(device=self.device)
+        side.wait_stream(main)
+        lib = _lib.load()
+        item = keys.element_size()
+        row = HEAD_DIM * item
+        L = self.geometry.max_cache_len
+        with torch.cuda.stream(side):
+            g = 0
+            while g < G:
+                e = first + g
+                if e in self._resident_index:
+                    idx = self._resident_index[e]
+                    self._resident_kv[0, idx, :S].copy_(keys[g], non_blocking=True)
+                    self._resident_kv[1, idx, :S].copy_(vals[g], non_blocking=True)
+                    g += 1
+                    continue
+                run = 1
+                while g + run < G and (first + g + run) not in self._resident_index:
+                    run += 1
+                for plane, src in ((0, keys), (1, vals)):
+                    dst = self._slab._host_ptr + plane * (self._slab.nbytes // 2) + e * L * row
+                    _lib.check(lib.tw_slab_write_rows(src[g].data_ptr(), S, dst, L, run, S, row,
+                                                      side.cuda_stream), "slab_write_rows")
+                g += run
+        keys.record_stream(side)
+        vals.record_stream(side)
+        for e in entries:
+            self._bookkeeping.advance(e, S)
+            self._initialized[e] = True
+        self._seen_tokens = self._bookkeeping.seen_tokens
+        if self._prompt_length is None:
+            self._prompt_length = S
+        self._build_metadata_entries(first, keys)
+        main.wait_stream(side)
 
     def _schedule_d2h(self, entry: int, start: int, key_states, value_states) -> None:
         n = int(key_states.shape[-2])
@@ -758,15 +826,16 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         return super().update(key_states, value_states, layer_idx, cache_kwargs)
 
     # --------------------------------------------------------------- metadata --
-    def _build_metadata(self, entry: int, key_states: torch.Tensor) -> None:
-        """Quest metadata + INT4 codes of the prompt (hi/twilight_offload_cache.py:925-936)."""
-        super()._build_metadata(entry, key_states)
-        keys = key_states[0, 0].contiguous()
-        S = int(keys.shape[0])
-        _lib.check(_lib.load().tw_int4_pack(
-            keys.data_ptr(), S * HEAD_DIM, 1, S, HEAD_DIM, self.int4_group_size,
-            ops._kv_code(self.dtype), self._packed[entry].data_ptr(), self._scale[entry].data_ptr(),
-            self._minimum[entry].data_ptr(), self.geometry.max_cache_len, 0, self._stream()),
+    def _build_metadata_entries(self, first: int, keys: torch.Tensor) -> None:
+        """Quest metadata + INT4 codes of the prompt (hi/twilight_offload_cache.py:925-936)
+        for entries first .. first + G - 1; keys [G, S, D]."""
+        keys = keys.contiguous()
+        super()._build_metadata_entries(first, keys)
+        G, S = int(keys.shape[0]), int(keys.shape[1])
+        _lib.check(_lib.load().tw_int4_pack(  # key entry stride in rows
+            keys.data_ptr(), S, G, S, HEAD_DIM, self.int4_group_size,
+            ops._kv_code(self.dtype), self._packed[first].data_ptr(), self._scale[first].data_ptr(),
+            self._minimum[first].data_ptr(), self.geometry.max_cache_len, 0, self._stream()),
             "int4_pack")
 
     # ---------------------------------------------------------------- buffers --

@@ -208,6 +208,25 @@ extern "C" int tw_host_device_pointer(void* host_ptr, void** device_ptr) {
   return TW_OK;
 }
 
+extern "C" int tw_slab_write_rows(const void* src, int64_t src_entry_stride_rows, void* dst,
+                                  int64_t dst_entry_stride_rows, int n_entries, int64_t n_rows,
+                                  int64_t row_bytes, void* stream) {
+  if (n_entries < 0 || n_rows < 0 || row_bytes <= 0 || src_entry_stride_rows < n_rows ||
+      dst_entry_stride_rows < n_rows)
+    return TW_ERR_BAD_ARG;
+  if (n_entries == 0 || n_rows == 0) return TW_OK;
+  if (!src || !dst) return TW_ERR_BAD_ARG;
+  const cudaError_t err = cudaMemcpy2DAsync(
+      dst, (size_t)(dst_entry_stride_rows * row_bytes), src,
+      (size_t)(src_entry_stride_rows * row_bytes), (size_t)(n_rows * row_bytes), (size_t)n_entries,
+      cudaMemcpyDefault, (cudaStream_t)stream);
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return TW_ERR_CUDA;
+  }
+  return TW_OK;
+}
+
 // Workspace: scores [G*R*P] fp32 | logits [G*R*b0*block] fp32.
 extern "C" size_t tw_select_layer_workspace_size(int groups, int heads_per_group, int n_pages,
                                                  int b0_pages, int block_size) {
