@@ -417,6 +417,8 @@ def run_ours(args) -> int:
             cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
     if world > 1:
         torch.distributed.barrier()
+    slab_numa = {"requested": args.numa, "bound_node": step.slab.numa_node,
+                 "page_node": step.slab.page_node(0)}
     step.close()
 
     if rank == 0:
@@ -458,8 +460,7 @@ def run_ours(args) -> int:
                 "mean_union_rows": avg["union_rows"],
                 "queries": (f"AR(1) rho={rho} (step-to-step continuity)" if step.reuse
                             else "independent N(0,1) per step"),
-                "slab_numa": {"requested": args.numa, "bound_node": step.slab.numa_node,
-                              "page_node": step.slab.page_node(0)},
+                "slab_numa": slab_numa,
             },
             "clocks": clocks,
             "gpu_launches": step.launches_per_step * K * world,

@@ -162,6 +162,8 @@ class MappedHostSlab:
 
     def page_node(self, offset: int = 0) -> int | None:
         """Host NUMA node of the page holding byte `offset` of the slab, if known."""
+        if not getattr(self, "_host_ptr", None):
+            raise RuntimeError("the slab has been freed")
         node = ctypes.c_int32(-1)
         st = _lib.load().tw_host_numa_node(ctypes.c_void_p(self._host_ptr + offset), ctypes.byref(node))
         return node.value if st == _lib.TW_OK and node.value >= 0 else None
