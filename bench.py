@@ -20,6 +20,7 @@ is bracketed by barriers and the max over ranks is reported.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import math
@@ -214,6 +215,10 @@ class DeviceStep:
         # fused selection (1 launch) + fused attention or gather + attention + append
         self.launches_per_step = 3 if fused else 4
         self.t = 0
+        # protected-row staging of the one-call path (not with row reuse)
+        self.stage = (torch.empty((2, G, sink + CFG["recent"], 128), dtype=torch.float16,
+                                  device=device) if fused and not reuse else None)
+        self.args = self.decode_args() if fused else None
         if reuse:
             # ping-pong: step t keeps its rows in slot t % 2 under tag t + 1 and
             # reads the other slot's rows (tag t) through the row map
@@ -221,6 +226,37 @@ class DeviceStep:
                                      device=device)
             self.row_map = torch.zeros((G, self.max_len), dtype=torch.int64, device=device)
             self.row_log = torch.zeros((max(n_steps, 1), G, 2), dtype=torch.int32, device=device)
+
+    def decode_args(self):
+        """tw_decode_layer_args of the one-call layer-step (the call
+        TwilightMatchedBudgetOffloadedCache.decode_layer makes)."""
+        a = self.tw._lib.DecodeLayerArgs()
+        G, R = self.G, self.R
+        a.slab_k, a.slab_v = self.slab.key_device_ptr, self.slab.value_device_ptr
+        a.entry_dirs = None
+        a.n_entries, a.max_len, a.first_entry = G, self.max_len, 0
+        a.groups, a.heads_per_group, a.dtype = G, R, 0
+        a.page_min, a.page_max = self.pmin.data_ptr(), self.pmax.data_ptr()
+        a.page_capacity, a.n_pages = self.page_cap, self.cand_pages
+        a.packed, a.scale, a.minimum = (self.packed.data_ptr(), self.scale.data_ptr(),
+                                        self.minimum.data_ptr())
+        a.int4_group_size, a.sink, a.block_size = CFG["int4_group"], CFG["sink"], CFG["block"]
+        a.b0_pages, a.top_p = self.b0, CFG["top_p"]
+        a.old_length, a.sink_end, a.recent_start = self.L, self.sink_end, self.recent_start
+        a.q, a.k_new, a.v_new = self.q16.data_ptr(), self.k_new.data_ptr(), self.v_new.data_ptr()
+        a.out, a.out_dtype, a.append = self.out.data_ptr(), 0, 1
+        a.pages, a.union_pos, a.pos_stride = (self.pages.data_ptr(), self.union_pos.data_ptr(),
+                                              self.max_len)
+        a.union_count, a.head_count = self.union_count.data_ptr(), self.head_count.data_ptr()
+        a.head_pos, a.error_flag = None, self.err.data_ptr()
+        a.select_workspace, a.select_workspace_bytes = self.ws.data_ptr(), self.ws.numel()
+        a.attn_workspace, a.attn_workspace_bytes = self.attn_ws.data_ptr(), self.attn_ws.numel()
+        a.max_rows_per_group = self.per_group_cap
+        a.reuse = None
+        if self.stage is not None:
+            a.stage_k, a.stage_v = self.stage[0].data_ptr(), self.stage[1].data_ptr()
+            a.stage_rows = self.stage.shape[2]
+        return a
 
     def load_query(self, q16: torch.Tensor) -> None:
         self.q16.copy_(q16)
@@ -243,6 +279,14 @@ class DeviceStep:
             reuse = tw.ops.row_reuse(self.row_map, self.t + 1, next_k=self.rows2[cur, 0],
                                      next_v=self.rows2[cur, 1], row_counts=log, **kw)
             self.t += 1
+        self.last_union_count = union_count
+        if self.fused and not ev:
+            # the timed path: one tw_twilight_decode_layer call (3 launches)
+            self._reuse_ref = reuse  # kept alive across the call
+            self.args.reuse = ctypes.addressof(reuse) if reuse is not None else None
+            tw._lib.check(lib.tw_twilight_decode_layer(ctypes.byref(self.args), st),
+                          "twilight_decode_layer")
+            return
         if "select" in ev:
             ev["select"][0].record()
         tw._lib.check(lib.tw_select_layer(

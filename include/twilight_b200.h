@@ -329,7 +329,8 @@ int tw_attend_union(const void* slab_k, const void* slab_v, const uint64_t* entr
 /* ---- whole decode layer-step --------------------------------------------------------------------------
  * One decode layer-step of the Twilight GQA path in one call: Quest score ->
  * top-k pages -> INT4 QK -> top-p + union -> fused union gather + attention ->
- * new-token append (6 launches on `stream`, no host synchronisation).
+ * new-token append (3 launches on `stream` when the fused selection serves
+ * the shape, else 6; no host synchronisation).
  * Replaces prepare_layer_selection + update_layer_gqa_group_ragged + the
  * FlashAttention call of one layer (hi/twilight_offload_cache.py:996-1843,
  * :2610-3602, hi/mp.py:233-279).  Cache pointers (slab, page min/max, INT4
@@ -382,6 +383,19 @@ typedef struct tw_decode_layer_args {
   size_t attn_workspace_bytes;
   int32_t max_rows_per_group;
   const tw_row_reuse* reuse; /* NULL: no row reuse */
+  /* Protected-row staging (stage_k NULL: off; ignored when reuse is set).
+   * Each group's sink rows [0, sink_end) and recent rows [recent_start,
+   * old_length) do not depend on the selection: one more cluster of the
+   * selection launch copies them from the slab into stage_k / stage_v
+   * [G][stage_rows][D] (device memory, 16-byte aligned) while the selection
+   * runs, and the attention reads them from there, so the host link carries
+   * them while it would otherwise idle.  stage_rows >= sink_end +
+   * (old_length - recent_start), else TW_ERR_CAPACITY.  No counterpart in the
+   * reference, which copies these rows with the rest of the union
+   * (hi/twilight_offload_cache.py:2973-3101).  Results are unchanged. */
+  void* stage_k;
+  void* stage_v;
+  int64_t stage_rows;
 } tw_decode_layer_args;
 int tw_twilight_decode_layer(const tw_decode_layer_args* args, void* stream);
 /* sizeof(tw_decode_layer_args), for binding-layout checks. */

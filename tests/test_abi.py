@@ -30,7 +30,7 @@ def test_header_symbols_exported(tw):
 
 def test_status_strings(tw):
     lib = tw.load_library()
-    assert lib.tw_abi_version() == 2
+    assert lib.tw_abi_version() == 3
     for code in range(8):
         assert lib.tw_status_string(code)
     assert tw._lib.status_string(1) == "row index out of bounds"
@@ -67,5 +67,6 @@ def test_decode_layer_args_layout(tw):
         if ctype in (ctypes.c_void_p, ctypes.c_int64, ctypes.c_double, ctypes.c_size_t):
             assert getattr(S, name).offset % 8 == 0, name
     assert lib.tw_twilight_decode_layer(None, None) == tw._lib.TW_ERR_BAD_ARG
-    assert S.reuse.offset == ctypes.sizeof(S) - 8
+    assert S.stage_rows.offset == ctypes.sizeof(S) - 8
+    assert S.stage_k.offset == S.reuse.offset + 8
     assert ctypes.sizeof(tw._lib.RowReuse) == lib.tw_row_reuse_size()

@@ -50,7 +50,8 @@ class DecodeLayerArgs(ctypes.Structure):
         ("pages", P), ("union_pos", P), ("pos_stride", I64), ("union_count", P),
         ("head_count", P), ("head_pos", P), ("error_flag", P), ("select_workspace", P),
         ("select_workspace_bytes", SZ), ("attn_workspace", P), ("attn_workspace_bytes", SZ),
-        ("max_rows_per_group", I32T), ("reuse", P),
+        ("max_rows_per_group", I32T), ("reuse", P), ("stage_k", P), ("stage_v", P),
+        ("stage_rows", I64),
     ]
 
 

@@ -747,15 +747,19 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
 
     hi/twilight_offload_cache.py:133-3743.  budget_mode must be 'dynamic' (the
     deployed profile); 'matched' raises ValueError.  qk_backend values of the
-    reference are accepted and all run the CUDA INT4 estimator.  Extra keyword:
-    ``int4_group_size`` (128 = the reference's per-token scale, or 32/64).
+    reference are accepted and all run the CUDA INT4 estimator.  Extra keywords:
+    ``int4_group_size`` (128 = the reference's per-token scale, or 32/64);
+    ``protected_row_staging`` (default True): decode_layer's selection launch
+    copies each group's sink and recent rows into device memory while it
+    selects, and the attention reads them from there (same results; unused
+    with the previous-token resident cache, whose kept rows serve them).
     """
 
     def __init__(self, *, candidate_token_budget: int = 8192, top_p: float = 0.95,
                  matched_budget_fraction: float = 0.05, budget_mode: str = "dynamic",
                  gqa_groupwise_execution: bool = False, qk_backend: str = "pytorch",
                  int4_group_size: int = 128, previous_token_resident_cache: bool = False,
-                 **kwargs: Any) -> None:
+                 protected_row_staging: bool = True, **kwargs: Any) -> None:
         if candidate_token_budget <= 0:
             raise ValueError("candidate_token_budget must be positive")
         if not 0.0 < top_p <= 1.0:
@@ -809,6 +813,7 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
         self._cached_group_positions: dict[int, torch.Tensor] = {}
         self._cached_per_q_positions: dict[int, tuple[torch.Tensor, ...]] = {}
         self.previous_token_resident_cache = bool(previous_token_resident_cache)
+        self.protected_row_staging = bool(protected_row_staging)
         self._reuse_pools: dict[int, _RowReusePool] = {}
         self._reuse_trace_enabled = self.previous_token_resident_cache
         self._reuse_trace: list[dict[str, Any]] = []
@@ -866,7 +871,13 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             "rows_cap": rows_cap,
             "per_group_cap": per_group,
             "slot": 0,
+            "stage": None,
         }
+        if self.protected_row_staging and not self.previous_token_resident_cache:
+            # sink rows + recent rows of every group (decode_layer's staging)
+            stage_rows = self.sink_tokens + max(1, self.recent_tokens)
+            bufs["stage"] = torch.empty((2, groups, stage_rows, HEAD_DIM), dtype=self.dtype,
+                                        device=dev)
         self._layer_bufs[groups] = bufs
         return bufs
 
@@ -1304,6 +1315,10 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             reuse.prev_rows = G * pool.rows_per_group
             reuse.rows_stride = pool.rows_per_group
             args.reuse = ctypes.addressof(reuse)
+        elif bufs["stage"] is not None:
+            args.stage_k = bufs["stage"][0].data_ptr()
+            args.stage_v = bufs["stage"][1].data_ptr()
+            args.stage_rows = bufs["stage"].shape[2]
         plan = {
             "G": G, "first": first, "args": args, "args_ref": ctypes.byref(args),
             "fn": _lib.load().tw_twilight_decode_layer, "bufs": bufs,

@@ -89,6 +89,8 @@ struct UnionRows {
   uint4* next_v;
   int64_t rows_stride;
   int32_t* row_counts;
+  // protected rows staged by the selection launch (stage.stage_k null: none)
+  ProtectedStage stage;
   // Adds this warp's hit / miss row counts to group s (lane 0 of the warp).
   __device__ __forceinline__ void count(int s, int hits, int misses) const {
     if (!row_counts) return;
@@ -137,6 +139,15 @@ struct UnionRows {
     if (pos < 0 || pos >= old_length) {
       if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
       return false;
+    }
+    if (stage.stage_k) {
+      const int64_t j = stage_index(stage, pos);
+      if (j >= 0) {
+        kp = stage.stage_k + ((int64_t)s * stage.stage_rows + j) * kVecPerRow;
+        vp = stage.stage_v + ((int64_t)s * stage.stage_rows + j) * kVecPerRow;
+        misses += (threadIdx.x & 15) == 0;  // read over the host link by the staging
+        return true;
+      }
     }
     if (row_map) {
       const int64_t j = previous_row(s, pos);
@@ -514,15 +525,19 @@ extern "C" int tw_decode_attention(const void* q, const void* k, const void* v,
   return TW_ERR_UNSUPPORTED;
 }
 
-extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
-                               const uint64_t* entry_dirs, int64_t n_entries, int64_t max_len,
-                               int first_entry, int groups, int64_t old_length,
-                               const int32_t* union_pos, int64_t pos_stride,
-                               const int32_t* union_count, const void* cur_k, const void* cur_v,
-                               const void* q, int heads_per_group, int max_rows_per_group,
-                               int head_dim, int dtype, float softmax_scale, void* out,
-                               int out_dtype, float* lse, int32_t* error_flag, void* workspace,
-                               size_t workspace_bytes, const tw_row_reuse* reuse, void* stream) {
+namespace tw {
+
+// tw_attend_union, with the protected rows read from a stage the selection
+// launch filled (stage null: every row from its source).
+int attend_union_impl(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
+                      int64_t n_entries, int64_t max_len, int first_entry, int groups,
+                      int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
+                      const int32_t* union_count, const void* cur_k, const void* cur_v,
+                      const void* q, int heads_per_group, int max_rows_per_group, int head_dim,
+                      int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
+                      int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                      const tw_row_reuse* reuse, const ProtectedStage* stage,
+                      cudaStream_t stream) {
   if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
   if ((!entry_dirs && (!slab_k || !slab_v)) || !union_pos || !union_count || !cur_k || !cur_v ||
       !q || !out || groups <= 0 || groups > 65535 || heads_per_group <= 0 || first_entry < 0 ||
@@ -581,8 +596,15 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
     rows.rows_stride = reuse->rows_stride;
     rows.row_counts = reuse->row_counts;
   }
+  if (stage && stage->stage_k) {
+    if (!stage->stage_v || stage->old_length != old_length ||
+        stage->stage_rows < stage->n_sink + (old_length - stage->recent_start) ||
+        (((uintptr_t)stage->stage_k | (uintptr_t)stage->stage_v) & 15) != 0)
+      return TW_ERR_BAD_ARG;
+    rows.stage = *stage;
+  }
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  cudaStream_t st = (cudaStream_t)stream;
+  cudaStream_t st = stream;
   if (dtype == TW_F16) {
     if (out_dtype == TW_F32)
       return launch_rows<__half, float>(rows, q, groups, heads_per_group, max_splits, scale_log2,
@@ -595,6 +617,24 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
                                              scale_log2, ws, out, lse, st);
   return launch_rows<__nv_bfloat16, __nv_bfloat16>(rows, q, groups, heads_per_group, max_splits,
                                                    scale_log2, ws, out, lse, st);
+}
+
+}  // namespace tw
+
+extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
+                               const uint64_t* entry_dirs, int64_t n_entries, int64_t max_len,
+                               int first_entry, int groups, int64_t old_length,
+                               const int32_t* union_pos, int64_t pos_stride,
+                               const int32_t* union_count, const void* cur_k, const void* cur_v,
+                               const void* q, int heads_per_group, int max_rows_per_group,
+                               int head_dim, int dtype, float softmax_scale, void* out,
+                               int out_dtype, float* lse, int32_t* error_flag, void* workspace,
+                               size_t workspace_bytes, const tw_row_reuse* reuse, void* stream) {
+  return attend_union_impl(slab_k, slab_v, entry_dirs, n_entries, max_len, first_entry, groups,
+                           old_length, union_pos, pos_stride, union_count, cur_k, cur_v, q,
+                           heads_per_group, max_rows_per_group, head_dim, dtype, softmax_scale,
+                           out, out_dtype, lse, error_flag, workspace, workspace_bytes, reuse,
+                           nullptr, (cudaStream_t)stream);
 }
 
 // ---- allocation-free variant ----------------------------------------------------

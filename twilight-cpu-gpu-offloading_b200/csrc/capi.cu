@@ -38,7 +38,16 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, cudaStream_t stream);
+                       int32_t* error_flag, const ProtectedStage* stage, cudaStream_t stream);
+int attend_union_impl(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
+                      int64_t n_entries, int64_t max_len, int first_entry, int groups,
+                      int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
+                      const int32_t* union_count, const void* cur_k, const void* cur_v,
+                      const void* q, int heads_per_group, int max_rows_per_group, int head_dim,
+                      int dtype, float softmax_scale, void* out, int out_dtype, float* lse,
+                      int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                      const tw_row_reuse* reuse, const ProtectedStage* stage,
+                      cudaStream_t stream);
 int quest_score_dispatch(const void* q, int q_dtype, const void* pmin, const void* pmax, int groups,
                          int R, int n_pages, int64_t stride, int dtype, float* scores,
                          cudaStream_t stream);
@@ -72,7 +81,7 @@ extern "C" const char* tw_status_string(int status) {
 
 extern "C" int tw_last_cuda_error(void) { return g_last_cuda_error; }
 
-extern "C" int tw_abi_version(void) { return 2; }
+extern "C" int tw_abi_version(void) { return 3; }
 
 extern "C" int tw_host_alloc_mapped(size_t bytes, void** host_ptr, void** device_ptr) {
   if (!host_ptr || !device_ptr || bytes == 0) return TW_ERR_BAD_ARG;
@@ -257,7 +266,7 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
                               scale, minimum, entry_stride_tokens, groups, heads_per_group,
                               b0_pages, block_size, sink, group_size, dtype, top_p, old_length,
                               sink_end, recent_start, pages_out, union_pos, pos_stride,
-                              union_count, head_count, head_pos, error_flag,
+                              union_count, head_count, head_pos, error_flag, nullptr,
                               (cudaStream_t)stream);
   if (st != TW_ERR_UNSUPPORTED) return st;
   // per-stage kernels (shapes the fused selection does not serve)
@@ -327,20 +336,44 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
   const uint8_t* packed = a->packed + e0 * a->max_len * (kHeadDim / 2);
   const char* scale = (const char*)a->scale + e0 * a->max_len * ngroups * elem;
   const char* minimum = (const char*)a->minimum + e0 * a->max_len * ngroups * elem;
+  // Protected-row staging (not with row reuse, whose kept rows serve them).
+  ProtectedStage stage{};
+  const bool staged = a->stage_k != nullptr && a->reuse == nullptr;
+  if (staged) {
+    if (!a->stage_v || a->stage_rows < a->sink_end + (a->old_length - a->recent_start))
+      return TW_ERR_CAPACITY;
+    stage.slab_k = (const uint4*)a->slab_k;
+    stage.slab_v = (const uint4*)a->slab_v;
+    stage.dirs = (const unsigned long long*)a->entry_dirs;
+    stage.n_entries = a->n_entries > 0 ? a->n_entries : (int64_t)a->first_entry + G;
+    stage.max_len = a->max_len;
+    stage.first_entry = a->first_entry;
+    stage.stage_k = (uint4*)a->stage_k;
+    stage.stage_v = (uint4*)a->stage_v;
+    stage.stage_rows = a->stage_rows;
+    stage.n_sink = a->sink_end;
+    stage.recent_start = a->recent_start;
+    stage.old_length = a->old_length;
+  }
   int rc = select_layer_fused(a->q, a->dtype, pmin, pmax, a->page_capacity * kHeadDim, a->n_pages,
                               packed, scale, minimum, a->max_len, G, R, a->b0_pages, a->block_size,
                               a->sink, a->int4_group_size, a->dtype, a->top_p, a->old_length,
                               a->sink_end, a->recent_start, a->pages, a->union_pos, a->pos_stride,
-                              a->union_count, a->head_count, a->head_pos, a->error_flag, st);
-  if (rc == TW_ERR_UNSUPPORTED) rc = select_stages(a, pmin, pmax, packed, scale, minimum, st);
+                              a->union_count, a->head_count, a->head_pos, a->error_flag,
+                              staged ? &stage : nullptr, st);
+  bool stage_filled = staged;
+  if (rc == TW_ERR_UNSUPPORTED) {
+    rc = select_stages(a, pmin, pmax, packed, scale, minimum, st);
+    stage_filled = false;  // the per-stage kernels stage nothing
+  }
   if (rc != TW_OK) return rc;
-  rc = tw_attend_union(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
-                       a->first_entry, G, a->old_length,
-                       a->union_pos, a->pos_stride, a->union_count, a->k_new, a->v_new, a->q, R,
-                       a->max_rows_per_group, kHeadDim, a->dtype,
-                       1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
-                       a->error_flag, a->attn_workspace, a->attn_workspace_bytes, a->reuse,
-                       stream);
+  rc = attend_union_impl(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
+                         a->first_entry, G, a->old_length,
+                         a->union_pos, a->pos_stride, a->union_count, a->k_new, a->v_new, a->q, R,
+                         a->max_rows_per_group, kHeadDim, a->dtype,
+                         1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
+                         a->error_flag, a->attn_workspace, a->attn_workspace_bytes, a->reuse,
+                         stage_filled ? &stage : nullptr, st);
   if (rc != TW_OK || !a->append) return rc;
   return tw_append_token(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
                          a->first_entry, G, a->old_length,

@@ -574,6 +574,8 @@ struct SelectArgs {
   int32_t* head_count;
   int32_t* head_pos;
   int32_t* error_flag;
+  int groups;             // selection clusters; a further cluster stages the
+  ProtectedStage stage;   // protected rows when stage.stage_k is set
 };
 
 // Dynamic shared memory: scores f32[P] | pages i32[b0] | logits f32[n] (keys
@@ -600,6 +602,10 @@ select_layer_kernel(SelectArgs a) {
   const int C = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
   const int g = blockIdx.x / C;
+  if (g >= a.groups) {  // the staging cluster: no cluster barrier, no shared memory
+    stage_protected_rows(a.stage, a.groups, (int)blockIdx.x - a.groups * C, C);
+    return;
+  }
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -917,11 +923,12 @@ int select_cluster_size(int groups) {
 template <typename T, typename QT, int R>
 int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t stream) {
   static DynSmemOptIn opt_in;
-  const int cluster = select_cluster_size<T, QT, R>(groups);
+  const int clusters = groups + (a.stage.stage_k ? 1 : 0);
+  const int cluster = select_cluster_size<T, QT, R>(clusters);
   const int st = ensure_dyn_smem((const void*)select_layer_kernel<T, QT, R>, opt_in, (int)smem);
   if (st != TW_OK) return st;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(groups * cluster, 1, 1);
+  cfg.gridDim = dim3(clusters * cluster, 1, 1);
   cfg.blockDim = dim3(kTopPThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -976,7 +983,7 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, cudaStream_t stream) {
+                       int32_t* error_flag, const ProtectedStage* stage, cudaStream_t stream) {
   if (!q || !pmin || !pmax || !packed || !scale || !minimum || !pages_out || !union_pos ||
       !union_count || !head_count || groups <= 0 || groups > (1 << 27) || R <= 0 ||
       n_pages <= 0 || b0 <= 0 || b0 > n_pages || block <= 0 || sink < 0 || old_length < 0 ||
@@ -1015,6 +1022,18 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
   a.head_count = head_count;
   a.head_pos = head_pos;
   a.error_flag = error_flag;
+  a.groups = groups;
+  if (stage && stage->stage_k) {
+    if (!stage->stage_v || (!stage->dirs && (!stage->slab_k || !stage->slab_v)) ||
+        stage->first_entry < 0 || stage->first_entry + (int64_t)groups > stage->n_entries ||
+        old_length > stage->max_len || stage->n_sink != sink_end ||
+        stage->recent_start != recent_start || stage->old_length != old_length ||
+        stage->stage_rows < sink_end + (old_length - recent_start) ||
+        (((uintptr_t)stage->stage_k | (uintptr_t)stage->stage_v | (uintptr_t)stage->slab_k |
+          (uintptr_t)stage->slab_v) & 15) != 0)
+      return TW_ERR_BAD_ARG;
+    a.stage = *stage;
+  }
   return launch_select_fused(a, groups, R, q_dtype, dtype, smem, stream);
 }
 

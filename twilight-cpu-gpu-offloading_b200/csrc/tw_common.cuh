@@ -108,6 +108,86 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   return check_launch();
 }
 
+// Protected rows of a layer-step staged in device memory.  Every group's union
+// holds its sink rows [0, n_sink) and its recent window [recent_start,
+// old_length); neither depends on the selection.  The selection launch copies
+// them from the slab (or the entry directory's rows) into stage_k / stage_v
+// [G][stage_rows][D] while its other clusters select, so the host link carries
+// them while it would otherwise idle, and the attention reads them from device
+// memory.  Staged row j of group g: position j (j < n_sink), else position
+// recent_start + j - n_sink.  stage_k == nullptr: nothing is staged.
+struct ProtectedStage {
+  const uint4* slab_k;              // K plane of the slab (dirs == nullptr)
+  const uint4* slab_v;
+  const unsigned long long* dirs;   // [2][n_entries] row-0 addresses, or null
+  int64_t n_entries;
+  int64_t max_len;
+  int first_entry;
+  uint4* stage_k;
+  uint4* stage_v;
+  int64_t stage_rows;               // >= n_sink + (old_length - recent_start)
+  int64_t n_sink;
+  int64_t recent_start;
+  int64_t old_length;
+};
+
+constexpr int kVecPerRow16 = 16;  // 16-byte vectors per 128-dim fp16 / bf16 row
+
+// The staged index of position pos, or -1 when pos is not a protected row.
+__device__ __forceinline__ int64_t stage_index(const ProtectedStage& s, int64_t pos) {
+  if (pos < s.n_sink) return pos;
+  if (pos >= s.recent_start) return s.n_sink + (pos - s.recent_start);
+  return -1;
+}
+
+// Copies the protected rows of `groups` groups (K and V) into the stage; the
+// calling CTAs are `ctas` CTAs of blockDim.x threads, this one being number
+// `cta`.  Each thread keeps 4 rows' vectors of K and V in flight.
+__device__ __forceinline__ void stage_protected_rows(const ProtectedStage& s, int groups, int cta,
+                                                     int ctas) {
+  const int64_t rows = s.n_sink + (s.old_length - s.recent_start);
+  const int64_t total = (int64_t)groups * rows * kVecPerRow16;
+  const int64_t nthreads = (int64_t)ctas * blockDim.x;
+  constexpr int kInFlight = 4;
+  for (int64_t base = (int64_t)cta * blockDim.x + threadIdx.x; base < total;
+       base += nthreads * kInFlight) {
+    uint4 kv[kInFlight], vv[kInFlight];
+    int64_t dst[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int64_t v = base + u * nthreads;
+      dst[u] = -1;
+      if (v < total) {
+        const int64_t row = v / kVecPerRow16;  // g * rows + j
+        const int l16 = (int)(v % kVecPerRow16);
+        const int64_t g = row / rows;
+        const int64_t j = row - g * rows;
+        const int64_t pos = j < s.n_sink ? j : s.recent_start + (j - s.n_sink);
+        const int64_t e = (int64_t)s.first_entry + g;
+        const uint4* kp;
+        const uint4* vp;
+        if (s.dirs) {
+          kp = reinterpret_cast<const uint4*>(s.dirs[e]) + pos * kVecPerRow16;
+          vp = reinterpret_cast<const uint4*>(s.dirs[s.n_entries + e]) + pos * kVecPerRow16;
+        } else {
+          kp = s.slab_k + (e * s.max_len + pos) * kVecPerRow16;
+          vp = s.slab_v + (e * s.max_len + pos) * kVecPerRow16;
+        }
+        kv[u] = __ldcs(kp + l16);
+        vv[u] = __ldcs(vp + l16);
+        dst[u] = (g * s.stage_rows + j) * kVecPerRow16 + l16;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      if (dst[u] >= 0) {
+        s.stage_k[dst[u]] = kv[u];
+        s.stage_v[dst[u]] = vv[u];
+      }
+    }
+  }
+}
+
 // 8 fp16 / bf16 values of a 16-byte vector as floats.
 template <typename T> __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]);
 template <> __device__ __forceinline__ void unpack8<__half>(const uint4& u, float (&f)[8]) {
