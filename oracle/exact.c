@@ -251,9 +251,12 @@ void orc_topk_pages(const float* scores, int rows, int n, int k, int32_t* out) {
 /* ---- INT4 QK estimate ------------------------------------------------------------------------
  * hi/twilight_fused_qk.py:13-31 (dequant k = code*scale + min in fp32, no FMA)
  * and hi/twilight_offload_cache.py:1197-1263 (QK) + :1261 (/ sqrt(D), applied
- * as torch on CUDA does: x * (1 / (float)sqrt(D))).  Reduction order: lane j
- * (j = 0..3) sums channels 32j..32j+31 in order from 0; then
- * (s0 + s1) + (s2 + s3).  Candidate n of row (g, r) is token
+ * as torch on CUDA does: x * (1 / (float)sqrt(D))).  The dot accumulates with
+ * fused multiply-adds, as the fp32 GEMV of torch.matmul
+ * (hi/twilight_offload_cache.py:1257) does on CUDA.  Reduction order: part j
+ * (j = 0..3) covers channels 32j..32j+31; channel 32j + i goes to
+ * accumulator i % 4 (acc = fma(k, q, acc), i in order from 0), and the part
+ * is (acc0 + acc1) + (acc2 + acc3); then (s0 + s1) + (s2 + s3).  Candidate n of row (g, r) is token
  * sink + pages[g][r][n / block] * block + n % block of entry g. */
 void orc_int4_qk(const float* q, const uint8_t* packed, const uint16_t* scale,
                  const uint16_t* minimum, int64_t entry_stride, const int32_t* pages, int G, int R,
@@ -274,15 +277,15 @@ void orc_int4_qk(const float* q, const uint8_t* packed, const uint16_t* scale,
           const int gi = (32 * j) / group;
           const float s = to_f32(scale[tr * ngroups + gi], dtype);
           const float m = to_f32(minimum[tr * ngroups + gi], dtype);
-          float acc = 0.0f;
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
           for (int i = 0; i < 32; ++i) {
             const int d = 32 * j + i;
             const uint8_t byte = packed[tr * (D / 2) + d / 2];
             const uint32_t code = (d & 1) ? (byte >> 4) : (byte & 15u);
             const float kv = (float)code * s + m;
-            acc = acc + kv * qr[d];
+            acc[i & 3] = fmaf(kv, qr[d], acc[i & 3]);
           }
-          part[j] = acc;
+          part[j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
         }
         const float sum = (part[0] + part[1]) + (part[2] + part[3]);
         logits[(int64_t)row * n_cand + n] = sum * inv;

@@ -69,8 +69,12 @@ __device__ __forceinline__ void quest_page_score2(const float (&qr)[R][4], const
 
 // INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
 // covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
-// k = code * s + m (the values of separately rounded mul and add), acc += k * q
-// (separately rounded) in channel order.  s and m are fp16 / bf16 values.
+// k = code * s + m (the values of separately rounded mul and add, as the
+// reference dequantises), then acc[c % 4] = fma(k, q, acc[c % 4]) over the
+// lane's channels c = 0..31 in order (fused multiply-adds, as torch.matmul's
+// fp32 GEMV of hi/twilight_offload_cache.py:1257 accumulates on CUDA), and the
+// lane's sum is (acc0 + acc1) + (acc2 + acc3).  Four interleaved accumulators
+// keep four independent FMA chains per lane.  s and m are fp16 / bf16 values.
 // A code v in 0..15 as float, exactly: the bits 0x4B0000vv are the float
 // 2^23 + v, from which 2^23 is subtracted (exact).  One byte permute puts
 // byte b of `nibbles` (one code per byte) under the exponent 0x4B.
@@ -82,24 +86,24 @@ __device__ __forceinline__ float nibble_float(uint32_t nibbles, int b) {
 __device__ __forceinline__ float int4_dot32(const uint4& codes, float s, float m,
                                             const float (&qr)[32]) {
   const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
-  float acc = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     const uint32_t lo = words[w] & 0x0f0f0f0fu;         // even channels, one per byte
     const uint32_t hi = (words[w] >> 4) & 0x0f0f0f0fu;  // odd channels
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const int i = 8 * w + 2 * b;
+      const int i = 8 * w + 2 * b;  // channels i (even) and i + 1 (odd)
       // code * s is exact in fp32 (a 4-bit integer times a value of at most
       // 11 significant bits), so the fused multiply-add rounds exactly as the
       // separately rounded code * s + m does.
       const float k0 = __fmaf_rn(nibble_float(lo, b), s, m);
-      acc = __fadd_rn(acc, __fmul_rn(k0, qr[i]));
+      acc[i & 3] = __fmaf_rn(k0, qr[i], acc[i & 3]);
       const float k1 = __fmaf_rn(nibble_float(hi, b), s, m);
-      acc = __fadd_rn(acc, __fmul_rn(k1, qr[i + 1]));
+      acc[(i + 1) & 3] = __fmaf_rn(k1, qr[i + 1], acc[(i + 1) & 3]);
     }
   }
-  return acc;
+  return __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
 }
 
 // Sum of the 4 lanes' partial dot products ((a0 + a1) + (a2 + a3), in lane

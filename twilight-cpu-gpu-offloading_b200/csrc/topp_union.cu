@@ -546,7 +546,6 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
 // kernels (same arithmetic, select_math.cuh).
 constexpr int kSelCluster = 8;      // portable cluster size
 constexpr int kSelClusterWide = 16; // non-portable cluster size
-constexpr int kSelUnroll = 2;  // candidates per 4-lane group in flight (INT4 stage)
 
 struct SelectArgs {
   const void* q;          // [G][R][D], QT
@@ -576,14 +575,17 @@ struct SelectArgs {
   int32_t* error_flag;
   int groups;             // selection clusters; a further cluster stages the
   ProtectedStage stage;   // protected rows when stage.stage_k is set
+  int block_shift;        // block == 1 << block_shift, or -1 (not a power of two)
 };
 
 // Dynamic shared memory: scores f32[P] | pages i32[b0] | logits f32[n] (keys
-// alias them) | mass u64[n] | bitmap u32[words] | sel u8[n].
+// alias them) | mass u64[n] | bitmap u32[words] | sel u8[n] | the group's
+// queries as fp32 [kMaxHeadsPerGroup][D].
 __host__ __device__ __forceinline__ size_t select_smem_bytes(int P, int b0, int n, int64_t L) {
   const size_t words = (size_t)((L + 31) / 32);
   return align16((size_t)P * 4) + align16((size_t)b0 * 4) + align16((size_t)n * 4) +
-         (size_t)n * 8 + align16(words * 4) + (size_t)n;
+         (size_t)n * 8 + align16(words * 4) + align16((size_t)n) +
+         (size_t)kMaxHeadsPerGroup * kHeadDim * 4;
 }
 
 template <typename T, typename QT, int R>
@@ -627,7 +629,13 @@ select_layer_kernel(SelectArgs a) {
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(cur);
   cur += align16((size_t)words * 4);
   unsigned char* sel = cur;
+  cur += align16((size_t)n);
+  float* s_q = reinterpret_cast<float*>(cur);
 
+  {
+    const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)g * R * kHeadDim;
+    for (int i = tid; i < R * kHeadDim; i += blockDim.x) s_q[i] = to_f32(qg[i]);
+  }
   // Leader: clear the bitmap and set the protected sink / recent ranges.
   if (crank == 0) {
     const int64_t sink_hi = min(a.sink_end, L);
@@ -637,14 +645,15 @@ select_layer_kernel(SelectArgs a) {
     }
   }
 
+  __syncthreads();  // s_q
+
   // 1. Quest scores of the group's R heads.
   {
-    const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)g * R * kHeadDim;
     float qr[R][4];
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) qr[r][c] = to_f32(qg[r * kHeadDim + lane + 32 * c]);
+      for (int c = 0; c < 4; ++c) qr[r][c] = s_q[r * kHeadDim + lane + 32 * c];
     const T* gmin = reinterpret_cast<const T*>(a.pmin) + (int64_t)g * a.meta_stride;
     const T* gmax = reinterpret_cast<const T*>(a.pmax) + (int64_t)g * a.meta_stride;
     float* owner_scores[R];
@@ -654,6 +663,11 @@ select_layer_kernel(SelectArgs a) {
     const int per_cta = (P + C - 1) / C;
     const int p_beg = min(P, crank * per_cta);
     const int p_end = min(P, p_beg + per_cta);
+    // The whole min / max range is requested from DRAM into L2 at once, so
+    // the warps' loads below wait on L2 rather than each on a DRAM round trip.
+    if (tid < 2 && p_end > p_beg)
+      prefetch_l2((tid == 0 ? gmin : gmax) + (int64_t)p_beg * kHeadDim,
+                  (size_t)(p_end - p_beg) * kHeadDim * sizeof(T));
     // two pages per warp and pass: both pages' loads are issued together
     const int stride = nwarps;
     for (int p = p_beg + warp; p < p_end; p += 2 * stride) {
@@ -778,42 +792,48 @@ select_layer_kernel(SelectArgs a) {
     const int c_end = min(n, c_beg + chunk);
     const int sub = lane & 3;
     const int tok = lane >> 2;
-    const QT* qrow = reinterpret_cast<const QT*>(a.q) + ((int64_t)g * R + r) * kHeadDim + 32 * sub;
     float qr[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) qr[i] = to_f32(qrow[i]);
+    for (int i = 0; i < 32; ++i) qr[i] = s_q[r * kHeadDim + 32 * sub + i];
     const int ngroups = kHeadDim / a.group_size;
     const int grp = (32 * sub) / a.group_size;
     const int32_t* prow = s_pages;
     float* lout = cluster.map_shared_rank(s_logit, r);
-    const int64_t ebase = (int64_t)g * a.entry_stride;
+    const int64_t tbase = (int64_t)g * a.entry_stride + a.sink;
     const T* scale = reinterpret_cast<const T*>(a.scale);
     const T* minimum = reinterpret_cast<const T*>(a.minimum);
     constexpr int kStep = kTopPThreads / 4;  // candidates per pass of the CTA
-    // base is warp-uniform (all lanes run every pass: int4_logit shuffles)
-    for (int base = c_beg + warp * 8; base < c_end; base += kStep * kSelUnroll) {
-      uint4 codes[kSelUnroll];
-      float sv[kSelUnroll], mv[kSelUnroll];
-#pragma unroll
-      for (int u = 0; u < kSelUnroll; ++u) {
-        const int i = base + tok + u * kStep;
-        codes[u] = make_uint4(0u, 0u, 0u, 0u);
-        sv[u] = 0.0f;
-        mv[u] = 0.0f;
-        if (i < c_end) {
-          const int64_t pos = (int64_t)a.sink + (int64_t)prow[i / a.block] * a.block + (i % a.block);
-          const int64_t tr = ebase + pos;
-          codes[u] = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
-          sv[u] = to_f32(scale[tr * ngroups + grp]);
-          mv[u] = to_f32(minimum[tr * ngroups + grp]);
+    // Each 4-lane group estimates one candidate per pass; the next pass's
+    // candidate is loaded before this pass's arithmetic, so its loads are in
+    // flight while the group computes.  Candidate i is token
+    // sink + prow[i / block] * block + i % block of the group's entry.
+    uint4 codes_n = make_uint4(0u, 0u, 0u, 0u);
+    float sv_n = 0.0f, mv_n = 0.0f;
+    auto load = [&](int i) {
+      if (i < c_end) {
+        int pg, t;
+        if (a.block_shift >= 0) {
+          pg = i >> a.block_shift;
+          t = i & (a.block - 1);
+        } else {
+          pg = i / a.block;
+          t = i - pg * a.block;
         }
+        const int64_t tr = tbase + (int64_t)prow[pg] * a.block + t;
+        codes_n = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
+        sv_n = to_f32(scale[tr * ngroups + grp]);
+        mv_n = to_f32(minimum[tr * ngroups + grp]);
       }
-#pragma unroll
-      for (int u = 0; u < kSelUnroll; ++u) {
-        const int i = base + tok + u * kStep;
-        const float logit = int4_logit(int4_dot32(codes[u], sv[u], mv[u], qr), a.inv_sqrt_d);
-        if (i < c_end && sub == 0) lout[i] = logit;
-      }
+    };
+    // base is warp-uniform (all lanes run every pass: int4_logit shuffles)
+    int base = c_beg + warp * 8;
+    load(base + tok);
+    for (; base < c_end; base += kStep) {
+      const uint4 codes = codes_n;
+      const float sv = sv_n, mv = mv_n;
+      load(base + kStep + tok);
+      const float logit = int4_logit(int4_dot32(codes, sv, mv, qr), a.inv_sqrt_d);
+      if (base + tok < c_end && sub == 0) lout[base + tok] = logit;
     }
   }
   cluster.sync();
@@ -1023,6 +1043,9 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
   a.head_pos = head_pos;
   a.error_flag = error_flag;
   a.groups = groups;
+  a.block_shift = -1;
+  for (int b = 0; b < 31; ++b)
+    if (block == (1 << b)) a.block_shift = b;
   if (stage && stage->stage_k) {
     if (!stage->stage_v || (!stage->dirs && (!stage->slab_k || !stage->slab_v)) ||
         stage->first_entry < 0 || stage->first_entry + (int64_t)groups > stage->n_entries ||

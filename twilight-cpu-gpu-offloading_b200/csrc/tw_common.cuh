@@ -188,6 +188,23 @@ __device__ __forceinline__ void stage_protected_rows(const ProtectedStage& s, in
   }
 }
 
+// Bulk prefetch of the 16-byte granules covering [p, p + bytes) into L2, in
+// pieces of at most 64 KB (one instruction each; no data is returned).
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+  if (bytes == 0) return;
+  uintptr_t a = (uintptr_t)p & ~(uintptr_t)15;
+  const uintptr_t e = ((uintptr_t)p + bytes + 15) & ~(uintptr_t)15;
+  while (a < e) {
+    const uint32_t n = (uint32_t)((e - a) < 65536 ? (e - a) : 65536);
+    asm volatile(
+        "{\n\t.reg .u64 ga;\n\tcvta.to.global.u64 ga, %0;\n\t"
+        "cp.async.bulk.prefetch.L2.global [ga], %1;\n\t}" ::"l"(a),
+        "r"(n)
+        : "memory");
+    a += n;
+  }
+}
+
 // 8 fp16 / bf16 values of a 16-byte vector as floats.
 template <typename T> __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]);
 template <> __device__ __forceinline__ void unpack8<__half>(const uint4& u, float (&f)[8]) {
