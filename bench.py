@@ -212,8 +212,10 @@ class DeviceStep:
         self.q16 = torch.empty((G, R, 128), dtype=torch.float16, device=device)
         self.k_new = layer.key_new.to(device)
         self.v_new = layer.value_new.to(device)
-        # fused selection (1 launch) + fused attention or gather + attention + append
-        self.launches_per_step = 3 if fused else 4
+        # timed fused step: one tw_twilight_decode_layer call = the selection launch
+        # (whose extra cluster stages the protected rows and appends the token) +
+        # the fused attention; staged twin: selection, gather, attention, append
+        self.launches_per_step = 2 if fused else 4
         self.t = 0
         # protected-row staging of the one-call path (not with row reuse)
         self.stage = (torch.empty((2, G, sink + CFG["recent"], 128), dtype=torch.float16,
@@ -281,7 +283,7 @@ class DeviceStep:
             self.t += 1
         self.last_union_count = union_count
         if self.fused and not ev:
-            # the timed path: one tw_twilight_decode_layer call (3 launches)
+            # the timed path: one tw_twilight_decode_layer call (2 launches)
             self._reuse_ref = reuse  # kept alive across the call
             self.args.reuse = ctypes.addressof(reuse) if reuse is not None else None
             tw._lib.check(lib.tw_twilight_decode_layer(ctypes.byref(self.args), st),
@@ -850,7 +852,7 @@ def run_cfg5(args) -> int:
                                    "INT4 g32, B0 4096, top-p 0.95, KV heads 0-1 resident, "
                                    f"{layers} layers cycled",
                        "parallelism": f"KV-head sharded over {world} GPU(s) + NCCL all-gather"},
-            "gpu_launches": 3 * K * world}), flush=True)
+            "gpu_launches": 2 * K * world}), flush=True)
     cache.synchronize()
     cache.close()
     dist.destroy_process_group()
@@ -951,7 +953,7 @@ def run_cfg4(args) -> int:
                                    "top-p 0.9, one layer-step per request per step",
                        "contexts_rank0": [ctxs[r] for r in mine],
                        "parallelism": f"request-sharded over {world} GPU(s), no collective"},
-            "gpu_launches": 3 * n_steps}), flush=True)
+            "gpu_launches": 2 * n_steps}), flush=True)
     for c in caches:
         c.close()
     if world > 1:
@@ -1128,7 +1130,7 @@ def run_cfg3(args) -> int:
                    "model_gemms": "torch / cuBLAS (o_proj, MLP, LM head); q/k/v projection + RoPE is "
                                   "tw_qkv_rope"},
         "clocks": clocks,
-        "gpu_launches_per_token": CFG3["layers"] * 4,  # qkv_rope + decode_layer's 3
+        "gpu_launches_per_token": CFG3["layers"] * 3,  # qkv_rope + decode_layer's 2
         "prefill_ms": round(model.prefill_ms, 2),
         "prefill_note": "prefill_layer for 32 layers x 8 KV heads x 32768 tokens (metadata, INT4 codes, "
                         "4 GiB of K/V written to the slab / resident heads)",

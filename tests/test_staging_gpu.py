@@ -159,6 +159,13 @@ def test_staging_through_the_c_abi_on_a_direct_slab(tw, cuda):
     for plane, src in ((0, s.data.keys), (1, s.data.values)):
         want = torch.cat((src[:, :n_sink], src[:, s.recent_start:L]), dim=1)
         assert torch.equal(stage[plane, :, :n_sink + n_recent].cpu(), want)
+    # with the append (run by the same extra cluster) the token lands at
+    # position L of every entry's slab rows, and the output is unchanged
+    assert s.call(s.args(q, kn, vn, stage, append=1)) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(s.out, plain)
+    assert torch.equal(s.slab.rows[0, :, L], kn.cpu())
+    assert torch.equal(s.slab.rows[1, :, L], vn.cpu())
     s.slab.close()
 
 
@@ -173,3 +180,54 @@ def test_staging_capacity_is_checked(tw, cuda):
     assert s.call(s.args(q, kn, vn, stage, stage_rows=need)) == 0
     torch.cuda.synchronize()
     s.slab.close()
+
+
+@pytest.mark.parametrize("dtype,group,resident", [("float16", 32, ()), ("bfloat16", 128, (0, 3))])
+def test_fused_append_equals_append_kernel(tw, cuda, dtype, group, resident):
+    """decode_layer appends the new token in the selection launch's extra
+    cluster; prepare_layer_selection + attend_layer appends it with the
+    separate append kernel.  Over 20 steps (a new Quest page starts at the first
+    one) the slab rows, the running page min / max and the INT4 codes, scales
+    and minima are identical, and so are the outputs."""
+    G, R, L, steps = 4, 4, 2000, 20
+    tdt = synth.TORCH_DTYPES[dtype]
+    d = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=dtype, seed=23,
+                         workload="outliers")
+    kw = {"resident_entries": list(resident)} if resident else {}
+    caches = []
+    for _ in range(2):
+        c = tw.TwilightMatchedBudgetOffloadedCache(
+            num_cache_entries=G, max_cache_len=L + steps + 8, head_dim=128,
+            num_query_heads_per_kv=R, dtype=tdt, device=cuda, sink_tokens=SINK,
+            recent_tokens=RECENT, block_size=BLOCK, candidate_token_budget=512, top_p=0.95,
+            budget_mode="dynamic", layer_batched_selection=True, gqa_groupwise_execution=True,
+            qk_backend="cuda", int4_group_size=group, incremental_page_metadata=True, **kw)
+        c.prefill_layer(key_states=d.keys.to(cuda), value_states=d.values.to(cuda),
+                        entries=list(range(G)))
+        caches.append(c)
+    assert (L - SINK) % BLOCK == 0  # the first appended token opens a page
+    for step in range(steps):
+        q, kn, vn = _inputs(G, R, tdt, 700 + step, cuda)
+        one = caches[0].decode_layer(queries=q, key_states=kn, value_states=vn,
+                                     entries=list(range(G)))
+        qs = [q[g].view(1, R, 1, 128) for g in range(G)]
+        caches[1].prepare_layer_selection(entries=list(range(G)), queries=qs)
+        two = caches[1].attend_layer(key_states=[kn[g].view(1, 1, 1, 128) for g in range(G)],
+                                     value_states=[vn[g].view(1, 1, 1, 128) for g in range(G)],
+                                     queries=qs, entries=list(range(G)))
+        torch.cuda.synchronize()
+        assert torch.equal(one, two), step
+    a, b = caches
+    pages = (L + steps - SINK + BLOCK - 1) // BLOCK  # pages holding written tokens
+    for name in ("_page_min", "_page_max"):
+        assert torch.equal(getattr(a, name)[:, :pages], getattr(b, name)[:, :pages]), name
+    for name in ("_packed", "_scale", "_minimum"):  # positions written so far
+        assert torch.equal(getattr(a, name)[:, :L + steps], getattr(b, name)[:, :L + steps]), name
+    for g in range(G):
+        for kind in ("key", "value"):
+            ra = a.entry_kv(kind, g)[L:L + steps].cpu()
+            rb = b.entry_kv(kind, g)[L:L + steps].cpu()
+            assert torch.equal(ra, rb), (kind, g)
+    for c in caches:
+        c.synchronize()
+        c.close()

@@ -6,6 +6,7 @@
 
 #include <unordered_map>
 
+#include "append.cuh"
 #include "tw_common.cuh"
 
 namespace tw {
@@ -38,7 +39,8 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, const ProtectedStage* stage, cudaStream_t stream);
+                       int32_t* error_flag, const ProtectedStage* stage,
+                       const AppendArgs* append, cudaStream_t stream);
 int attend_union_impl(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
                       int64_t n_entries, int64_t max_len, int first_entry, int groups,
                       int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
@@ -266,7 +268,7 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
                               scale, minimum, entry_stride_tokens, groups, heads_per_group,
                               b0_pages, block_size, sink, group_size, dtype, top_p, old_length,
                               sink_end, recent_start, pages_out, union_pos, pos_stride,
-                              union_count, head_count, head_pos, error_flag, nullptr,
+                              union_count, head_count, head_pos, error_flag, nullptr, nullptr,
                               (cudaStream_t)stream);
   if (st != TW_ERR_UNSUPPORTED) return st;
   // per-stage kernels (shapes the fused selection does not serve)
@@ -355,16 +357,34 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
     stage.recent_start = a->recent_start;
     stage.old_length = a->old_length;
   }
+  // The new token's append runs in the selection launch's extra cluster: it
+  // writes position old_length, which neither this step's selection nor its
+  // attention reads.
+  AppendArgs app{};
+  bool fuse_append = false;
+  if (a->append) {
+    const int st_app = check_append_args(
+        a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len, a->first_entry, G,
+        a->old_length, a->k_new, a->v_new, a->sink, a->block_size, a->page_min, a->page_max,
+        a->packed, a->scale, a->minimum, a->int4_group_size);
+    if (st_app != TW_OK) return st_app;
+    app = make_append_args(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
+                           a->first_entry, a->old_length, a->k_new, a->v_new, a->sink,
+                           a->block_size, a->page_min, a->page_max, a->page_capacity * kHeadDim,
+                           a->packed, a->scale, a->minimum, a->int4_group_size);
+    fuse_append = (int64_t)G * kHeadDim <= 8 * 1024;  // one extra cluster covers it
+  }
   int rc = select_layer_fused(a->q, a->dtype, pmin, pmax, a->page_capacity * kHeadDim, a->n_pages,
                               packed, scale, minimum, a->max_len, G, R, a->b0_pages, a->block_size,
                               a->sink, a->int4_group_size, a->dtype, a->top_p, a->old_length,
                               a->sink_end, a->recent_start, a->pages, a->union_pos, a->pos_stride,
                               a->union_count, a->head_count, a->head_pos, a->error_flag,
-                              staged ? &stage : nullptr, st);
+                              staged ? &stage : nullptr, fuse_append ? &app : nullptr, st);
   bool stage_filled = staged;
   if (rc == TW_ERR_UNSUPPORTED) {
     rc = select_stages(a, pmin, pmax, packed, scale, minimum, st);
     stage_filled = false;  // the per-stage kernels stage nothing
+    fuse_append = false;   // nor append
   }
   if (rc != TW_OK) return rc;
   rc = attend_union_impl(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
@@ -374,7 +394,7 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
                          1.0f / sqrtf((float)kHeadDim), a->out, a->out_dtype, nullptr,
                          a->error_flag, a->attn_workspace, a->attn_workspace_bytes, a->reuse,
                          stage_filled ? &stage : nullptr, st);
-  if (rc != TW_OK || !a->append) return rc;
+  if (rc != TW_OK || !a->append || fuse_append) return rc;
   return tw_append_token(a->slab_k, a->slab_v, a->entry_dirs, a->n_entries, a->max_len,
                          a->first_entry, G, a->old_length,
                          a->k_new, a->v_new, kHeadDim, a->dtype, a->sink, a->block_size,

@@ -3,52 +3,10 @@
 // Reference: affine_int4_pack / affine_int4_dequantize
 // (hi/twilight_offload_cache.py:25-47), fused_affine_int4_qk
 // (hi/twilight_fused_qk.py:13-55), logits /= sqrt(D) (hi/twilight_offload_cache.py:1261).
+#include "append.cuh"
 #include "select_math.cuh"
 
 namespace tw {
-
-// Rounding of the `/ 15.0` in affine_int4_pack.  torch on CUDA multiplies by
-// the fp32 reciprocal of a CPU-scalar divisor; torch on CPU divides.
-enum ScaleDiv : int { kScaleReciprocal = 0, kScaleDivide = 1 };
-
-// Quantise the 4 channels 4*lane .. 4*lane+3 of one row held by a warp.
-// group_size in {32, 64, 128}: lanes 0..31 split into groups of group_size/4.
-// Returns the two packed bytes for this lane (low byte = channels 0,1).
-template <typename T>
-__device__ __forceinline__ uint16_t quantize_lane(const T (&raw)[4], int group_size, int scale_div,
-                                                  T* scale_out, T* min_out) {
-  const int lanes_per_group = group_size >> 2;
-  float x[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = to_f32(raw[i]);
-  float mn = fminf(fminf(x[0], x[1]), fminf(x[2], x[3]));
-  float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-  for (int off = 1; off < lanes_per_group; off <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  }
-  // (maximum - minimum) is computed in the K dtype, then widened.
-  const float diff = to_f32(from_f32<T>(__fsub_rn(mx, mn)));
-  const float clamped = fmaxf(diff, 1e-9f);
-  const float sc32 = scale_div == kScaleDivide ? __fdiv_rn(clamped, 15.0f)
-                                               : __fmul_rn(clamped, __fdiv_rn(1.0f, 15.0f));
-  const T sc_t = from_f32<T>(sc32);
-  const float sc = to_f32(sc_t);
-  const T mn_t = from_f32<T>(mn);  // exact: mn is a K-dtype value
-  uint32_t codes[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float c = rintf(__fdiv_rn(__fsub_rn(x[i], mn), sc));
-    if (!(c >= 0.0f)) c = 0.0f;  // negatives and NaN (0/0) -> 0, as clamp + uint8 cast
-    if (c > 15.0f) c = 15.0f;
-    codes[i] = (uint32_t)c;
-  }
-  if ((threadIdx.x & (lanes_per_group - 1)) == 0) {
-    *scale_out = sc_t;
-    *min_out = mn_t;
-  }
-  return (uint16_t)((codes[0] | (codes[1] << 4)) | ((codes[2] | (codes[3] << 4)) << 8));
-}
 
 // Warp per row.  keys rows: entry e, row t at keys + (e*key_entry_stride + t)*D.
 template <typename T>
@@ -75,8 +33,8 @@ __global__ void int4_pack_kernel(const T* __restrict__ keys, int64_t key_entry_s
 }
 
 // INT4 QK estimate.  4 lanes per candidate token, lane j covers channels
-// 32j .. 32j+31 (16 code bytes, one uint4 load).  Per channel k = code*s + m
-// (separately rounded), acc += k*q in channel order, then (a0+a1)+(a2+a3).
+// 32j .. 32j+31 (16 code bytes, one uint4 load); the arithmetic is
+// int4_dot32 (select_math.cuh), then (a0+a1)+(a2+a3) over the lanes.
 template <typename T, typename QT>
 __global__ void __launch_bounds__(256)
 int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
@@ -121,67 +79,12 @@ int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
   }
 }
 
-// New-token append: one CTA (128 threads) per group.  Copies the row to the
-// slab (mapped host or device memory), folds it into the running page min/max
-// and INT4-packs it.
+// New-token append: one CTA (128 threads) per group (append_token_row).
 template <typename T>
-__global__ void append_token_kernel(uint4* __restrict__ slab_k, uint4* __restrict__ slab_v,
-                                    const unsigned long long* __restrict__ dirs,
-                                    int64_t n_entries, int64_t max_len, int first_entry,
-                                    int64_t position,
-                                    const T* __restrict__ cur_k, const T* __restrict__ cur_v,
-                                    int sink, int block, T* __restrict__ pmin, T* __restrict__ pmax,
-                                    int64_t meta_entry_stride, uint8_t* __restrict__ packed,
-                                    T* __restrict__ scale, T* __restrict__ minimum, int group_size,
-                                    int scale_div) {
+__global__ void append_token_kernel(AppendArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  const int g = blockIdx.x;
-  const int entry = first_entry + g;
-  const int d = threadIdx.x;
-  const T* krow = cur_k + (int64_t)g * kHeadDim;
-  const T* vrow = cur_v + (int64_t)g * kHeadDim;
-  constexpr int kVecPerRow = kHeadDim * sizeof(T) / 16;
-  if (slab_k != nullptr || dirs != nullptr) {
-    uint4* kb = dirs ? reinterpret_cast<uint4*>(dirs[entry])
-                     : slab_k + (int64_t)entry * max_len * kVecPerRow;
-    uint4* vb = dirs ? reinterpret_cast<uint4*>(dirs[n_entries + entry])
-                     : slab_v + (int64_t)entry * max_len * kVecPerRow;
-    if (d < kVecPerRow) {
-      kb[position * kVecPerRow + d] = reinterpret_cast<const uint4*>(krow)[d];
-    } else if (d < 2 * kVecPerRow) {
-      const int j = d - kVecPerRow;
-      vb[position * kVecPerRow + j] = reinterpret_cast<const uint4*>(vrow)[j];
-    }
-  }
-  if (pmin != nullptr && position >= sink) {
-    const int64_t rel = position - sink;
-    const int64_t page = rel / block;
-    const int64_t off = rel % block;
-    const int64_t idx = (int64_t)entry * meta_entry_stride + page * kHeadDim + d;
-    const T x = krow[d];
-    if (off == 0) {
-      pmin[idx] = x;
-      pmax[idx] = x;
-    } else {
-      const float fx = to_f32(x);
-      if (fx < to_f32(pmin[idx])) pmin[idx] = x;
-      if (fx > to_f32(pmax[idx])) pmax[idx] = x;
-    }
-  }
-  if (packed != nullptr && threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    T raw[4];
-    const uint2 v = *reinterpret_cast<const uint2*>(krow + 4 * lane);
-    memcpy(raw, &v, sizeof(v));
-    const int ngroups = kHeadDim / group_size;
-    const int64_t orow = (int64_t)entry * max_len + position;
-    const int grp = (4 * lane) / group_size;
-    const uint16_t bytes = quantize_lane<T>(raw, group_size, scale_div,
-                                            scale + orow * ngroups + grp,
-                                            minimum + orow * ngroups + grp);
-    reinterpret_cast<uint16_t*>(packed + orow * (kHeadDim / 2))[lane] = bytes;
-  }
+  append_token_row<T>(a, blockIdx.x, threadIdx.x);
 }
 
 bool valid_group_size(int gs) { return gs == 32 || gs == 64 || gs == 128; }
@@ -278,22 +181,16 @@ extern "C" int tw_append_token(void* slab_k, void* slab_v, const uint64_t* entry
                                void* page_max, int64_t meta_entry_stride, uint8_t* packed,
                                void* scale, void* minimum, int group_size, void* stream) {
   if (head_dim != kHeadDim) return TW_ERR_UNSUPPORTED;
-  if (!cur_k || !cur_v || groups <= 0 || first_entry < 0 || position < 0 ||
-      position >= max_len || block_size <= 0 || sink < 0)
-    return TW_ERR_BAD_ARG;
-  if ((slab_k == nullptr) != (slab_v == nullptr)) return TW_ERR_BAD_ARG;
-  if (entry_dirs && first_entry + groups > n_entries) return TW_ERR_BAD_ARG;
-  if ((page_min == nullptr) != (page_max == nullptr)) return TW_ERR_BAD_ARG;
-  if (packed != nullptr && (!scale || !minimum || !valid_group_size(group_size)))
-    return TW_ERR_BAD_ARG;
-  if ((slab_k && ((uintptr_t)slab_k & 15)) || ((uintptr_t)cur_k & 15) || ((uintptr_t)cur_v & 15))
-    return TW_ERR_BAD_ARG;
+  const int st = check_append_args(slab_k, slab_v, entry_dirs, n_entries, max_len, first_entry,
+                                   groups, position, cur_k, cur_v, sink, block_size, page_min,
+                                   page_max, packed, scale, minimum, group_size);
+  if (st != TW_OK) return st;
+  const AppendArgs a = make_append_args(slab_k, slab_v, entry_dirs, n_entries, max_len,
+                                        first_entry, position, cur_k, cur_v, sink, block_size,
+                                        page_min, page_max, meta_entry_stride, packed, scale,
+                                        minimum, group_size);
   TW_DISPATCH_KV_DTYPE(dtype, T, {
     return launch_pdl(append_token_kernel<T>, dim3(groups), dim3(kHeadDim), 0,
-                      (cudaStream_t)stream, (uint4*)slab_k, (uint4*)slab_v,
-                      (const unsigned long long*)entry_dirs, n_entries, max_len, first_entry,
-                      position, (const T*)cur_k, (const T*)cur_v, sink, block_size, (T*)page_min,
-                      (T*)page_max, meta_entry_stride, packed, (T*)scale, (T*)minimum,
-                      packed ? group_size : 128, (int)kScaleReciprocal);
+                      (cudaStream_t)stream, a);
   });
 }

@@ -24,6 +24,7 @@
 // the leader writes the sorted union by a popcount scan.
 #include <cooperative_groups.h>
 
+#include "append.cuh"
 #include "select_math.cuh"
 
 namespace cg = cooperative_groups;
@@ -574,7 +575,9 @@ struct SelectArgs {
   int32_t* head_pos;
   int32_t* error_flag;
   int groups;             // selection clusters; a further cluster stages the
-  ProtectedStage stage;   // protected rows when stage.stage_k is set
+  ProtectedStage stage;   // protected rows when stage.stage_k is set, and
+  AppendArgs append;      // appends the new token when do_append is set
+  int do_append;
   int block_shift;        // block == 1 << block_shift, or -1 (not a power of two)
 };
 
@@ -604,8 +607,15 @@ select_layer_kernel(SelectArgs a) {
   const int C = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
   const int g = blockIdx.x / C;
-  if (g >= a.groups) {  // the staging cluster: no cluster barrier, no shared memory
-    stage_protected_rows(a.stage, a.groups, (int)blockIdx.x - a.groups * C, C);
+  if (g >= a.groups) {  // the extra cluster: no cluster barrier, no shared memory
+    const int cta = (int)blockIdx.x - a.groups * C;
+    // The new token (independent of this step's selection and attention: it
+    // goes to position old_length, beyond every row they read): group j by
+    // the cluster's threads 128 j .. 128 j + 127.
+    const int flat = cta * (int)blockDim.x + (int)threadIdx.x;
+    if (a.do_append && flat < a.groups * kHeadDim)
+      append_token_row<T>(a.append, flat / kHeadDim, flat % kHeadDim);
+    if (a.stage.stage_k) stage_protected_rows(a.stage, a.groups, cta, C);
     return;
   }
   const int tid = threadIdx.x;
@@ -943,7 +953,7 @@ int select_cluster_size(int groups) {
 template <typename T, typename QT, int R>
 int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t stream) {
   static DynSmemOptIn opt_in;
-  const int clusters = groups + (a.stage.stage_k ? 1 : 0);
+  const int clusters = groups + ((a.stage.stage_k || a.do_append) ? 1 : 0);
   const int cluster = select_cluster_size<T, QT, R>(clusters);
   const int st = ensure_dyn_smem((const void*)select_layer_kernel<T, QT, R>, opt_in, (int)smem);
   if (st != TW_OK) return st;
@@ -1003,7 +1013,8 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, const ProtectedStage* stage, cudaStream_t stream) {
+                       int32_t* error_flag, const ProtectedStage* stage,
+                       const AppendArgs* append, cudaStream_t stream) {
   if (!q || !pmin || !pmax || !packed || !scale || !minimum || !pages_out || !union_pos ||
       !union_count || !head_count || groups <= 0 || groups > (1 << 27) || R <= 0 ||
       n_pages <= 0 || b0 <= 0 || b0 > n_pages || block <= 0 || sink < 0 || old_length < 0 ||
@@ -1056,6 +1067,12 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
           (uintptr_t)stage->slab_v) & 15) != 0)
       return TW_ERR_BAD_ARG;
     a.stage = *stage;
+  }
+  if (append) {
+    // the extra cluster (kSelCluster CTAs of kTopPThreads) covers 128 threads per group
+    if ((int64_t)groups * kHeadDim > (int64_t)kSelCluster * kTopPThreads) return TW_ERR_UNSUPPORTED;
+    a.append = *append;
+    a.do_append = 1;
   }
   return launch_select_fused(a, groups, R, q_dtype, dtype, smem, stream);
 }
