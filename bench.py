@@ -839,6 +839,22 @@ def run_cfg5(args) -> int:
     e.record()
     torch.cuda.synchronize()
     total_ms = sh.max_over_ranks(s.elapsed_time(e), device=device if world > 1 else None)
+    # Union sizes of further steps (outside the timed region): the rows this
+    # rank read over the host link (its offloaded heads) and from HBM.
+    host_rows = dev_rows = 0
+    B = 3
+    for i in range(B):
+        li = (W + K + i) % layers
+        stepper.step(li, *steps[(W + K + i) % (K + W)], out_local=out_local)
+        counts = cache._layer_bufs[hl]["union_count"].cpu().tolist()
+        for j, c in enumerate(counts):
+            if li * hl + j in resident:
+                dev_rows += c + 1
+            else:
+                host_rows += c
+    host_bytes = 512.0 * host_rows / B
+    host_max = sh.max_over_ranks(host_bytes, device=device if world > 1 else None)
+    pinned = pinned_h2d_peak_gbs(device) if rank == 0 else None
     dist.barrier()
     if rank == 0:
         ms = total_ms / K
@@ -852,6 +868,17 @@ def run_cfg5(args) -> int:
                                    "INT4 g32, B0 4096, top-p 0.95, KV heads 0-1 resident, "
                                    f"{layers} layers cycled",
                        "parallelism": f"KV-head sharded over {world} GPU(s) + NCCL all-gather"},
+            "host_link": {
+                "bytes_per_step_rank0": round(host_bytes),
+                "bytes_per_step_max_rank": round(host_max),
+                "union_rows_per_step_rank0": {"offloaded_heads": round(host_rows / B),
+                                              "resident_heads": round(dev_rows / B)},
+                "achieved_gbs_max_rank": round(host_max / (ms * 1e-3) / 1e9, 2),
+                "pinned_h2d_peak_gbs": round(pinned, 2),
+                "frac": round(host_max / (ms * 1e-3) / 1e9 / pinned, 4),
+                "note": "union sizes from 3 further steps; bytes = 512 B per union row of an "
+                        "offloaded head; achieved = the busiest rank's bytes / the max-over-ranks "
+                        "step time"},
             "gpu_launches": 2 * K * world}), flush=True)
     cache.synchronize()
     cache.close()
@@ -1093,22 +1120,28 @@ def run_cfg3(args) -> int:
     dev_ms = s.elapsed_time(e)
     model.cache.synchronize()
     steps = n_tok - 1
-    # front-end kernel alone (layer 0 weights, L2 flushed before each call)
+    # Front-end kernel alone: one call per layer's weights (1.6 GB in all, so
+    # no call finds its weights in L2), queued behind a GPU-side sleep so that
+    # the events time the kernels and not the host's submission of each call.
     p0 = model.layers[0]
     x = torch.randn(model.H, device=device).to(torch.bfloat16)
     cs = torch.ones(128, dtype=torch.bfloat16, device=device)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     fe_ms = []
-    for i in range(12):
+    n_fe = CFG3["layers"]
+    for i in range(4):
         l2_flush(flush)
+        torch.cuda._sleep(4_000_000)  # ~2 ms of GPU time while the calls are queued
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        tw.ops.qkv_rope(x, p0["wq"], p0["wk"], p0["wv"], cs, cs, q_out=model.q, k_out=model.k,
-                        v_out=model.v)
+        for li in range(n_fe):
+            p = model.layers[li]
+            tw.ops.qkv_rope(x, p["wq"], p["wk"], p["wv"], cs, cs, q_out=model.q, k_out=model.k,
+                            v_out=model.v)
         b.record()
         b.synchronize()
-        if i >= 2:
-            fe_ms.append(a.elapsed_time(b))
+        if i >= 1:
+            fe_ms.append(a.elapsed_time(b) / n_fe)
     fe_bytes = sum(p0[k].numel() * 2 for k in ("wq", "wk", "wv"))
     fe_us = float(np.median(fe_ms)) * 1e3
     peaks = measured_peaks()
@@ -1135,6 +1168,8 @@ def run_cfg3(args) -> int:
         "prefill_note": "prefill_layer for 32 layers x 8 KV heads x 32768 tokens (metadata, INT4 codes, "
                         "4 GiB of K/V written to the slab / resident heads)",
         "front_end": {"kernel": "qkv_rope_kernel (q/k/v GEMV + RoPE, one launch per layer)",
+                      "timing": "32 back-to-back calls over the 32 layers' weights, queued "
+                                "behind a GPU sleep; per-call mean",
                       "us": round(fe_us, 2), "bytes": fe_bytes,
                       "achieved_gbs": round(fe_bytes / (fe_us * 1e-6) / 1e9, 1),
                       "peak_gbs": hbm_peak,

@@ -11,43 +11,41 @@
 // rotate_half(x) = cat(-x[D/2:], x[:D/2]), each product and the sum rounded to
 // the model dtype, as elementwise ops in that dtype compute them.
 //
-// Layout: a warp per rotary channel pair (c, c + 64) of one head, so the
-// rotation needs no exchange: the warp computes both dot products (16-byte
-// weight loads, 8 vectors of each row in flight per lane, fp32 accumulation,
-// rounded to the model dtype like the projection's output) and lane 0 writes
-// both rotated channels.  8 warps per CTA share the hidden vector in shared
-// memory; (n_q + 2 n_kv) * 64 pairs make 384 CTAs for Llama-3-8B, all resident
-// at once.  The kernel is bound by the weight bytes read from HBM
-// ((n_q + 2 n_kv) * D * hidden * 2 bytes per token).
+// Layout: one CTA per rotary channel pair (c, c + 64) of one head, so the
+// rotation needs no exchange between CTAs.  The CTA's 8 warps split the
+// hidden dimension: thread t reads 16-byte vectors t, t + 256, ... of both
+// weight rows and of the hidden vector (all its loads issued before its
+// arithmetic), accumulates in fp32, and the 8 warp sums are added in warp
+// order through shared memory (a fixed order: the result does not depend on
+// scheduling).  Thread 0 rounds both dot products to the model dtype, like the
+// projection's output, and writes the rotated channels.  (n_q + 2 n_kv) * 64
+// pairs make 3072 small CTAs for Llama-3-8B, several resident per SM, so the
+// hardware balances them over the 148 SMs.  The kernel is bound by the weight
+// bytes read from HBM ((n_q + 2 n_kv) * D * hidden * 2 bytes per token).
 #include "tw_common.cuh"
 
 namespace tw {
 
-constexpr int kFrontThreads = 256;   // 8 warps, one channel pair each
+constexpr int kFrontThreads = 256;   // 8 warps per channel pair
 constexpr int kFrontHalf = kHeadDim / 2;
 constexpr int kFrontMaxHidden = 16384;
-constexpr int kFrontBatch = 8;       // weight vectors of each row in flight per lane
+constexpr int kFrontBatch = 2;       // 16-byte vectors of each row in flight per thread
 
 template <typename T>
-__global__ void __launch_bounds__(kFrontThreads, 3)
+__global__ void __launch_bounds__(kFrontThreads, 6)
 qkv_rope_kernel(const T* __restrict__ hidden, const T* __restrict__ w_q,
                 const T* __restrict__ w_k, const T* __restrict__ w_v, int hidden_size,
                 int n_q, int n_kv, const T* __restrict__ cos, const T* __restrict__ sin,
                 T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out) {
   pdl_wait();
   pdl_launch_dependents();
-  extern __shared__ __align__(16) unsigned char front_smem[];
-  uint4* s_hidden = reinterpret_cast<uint4*>(front_smem);  // hidden_size / 8 vectors
-  const int vecs = hidden_size / 8;                        // 16-byte vectors per weight row
-  const uint4* hv = reinterpret_cast<const uint4*>(hidden);
-  for (int i = threadIdx.x; i < vecs; i += blockDim.x) s_hidden[i] = hv[i];
-  __syncthreads();
-
-  const int lane = threadIdx.x & 31;
-  const int pair = blockIdx.x * (kFrontThreads / 32) + (threadIdx.x >> 5);
+  __shared__ float s_part[kFrontThreads / 32][2];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int pair = blockIdx.x;
   const int head = pair / kFrontHalf;  // q heads, then k heads, then v heads
   const int c = pair % kFrontHalf;     // channels c and c + 64
-  if (head >= n_q + 2 * n_kv) return;
   const T* w;
   T* dst;
   bool rotate;
@@ -64,31 +62,31 @@ qkv_rope_kernel(const T* __restrict__ hidden, const T* __restrict__ w_q,
     dst = v_out + (int64_t)(head - n_q - n_kv) * kHeadDim;
     rotate = false;
   }
+  const int vecs = hidden_size / 8;  // 16-byte vectors per weight row
   const uint4* wa = reinterpret_cast<const uint4*>(w + (int64_t)c * hidden_size);
   const uint4* wb = reinterpret_cast<const uint4*>(w + (int64_t)(c + kFrontHalf) * hidden_size);
+  const uint4* hv = reinterpret_cast<const uint4*>(hidden);
   float acc_a = 0.0f, acc_b = 0.0f;
-  for (int base = lane; base < vecs; base += 32 * kFrontBatch) {
-    uint4 ra[kFrontBatch], rb[kFrontBatch];
+  for (int base = tid; base < vecs; base += kFrontThreads * kFrontBatch) {
+    uint4 ra[kFrontBatch], rb[kFrontBatch], rh[kFrontBatch];
 #pragma unroll
     for (int u = 0; u < kFrontBatch; ++u) {
-      const int i = base + 32 * u;
+      const int i = base + kFrontThreads * u;
       const bool in = i < vecs;
       ra[u] = in ? __ldcs(wa + i) : make_uint4(0u, 0u, 0u, 0u);
       rb[u] = in ? __ldcs(wb + i) : make_uint4(0u, 0u, 0u, 0u);
+      rh[u] = in ? __ldg(hv + i) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < kFrontBatch; ++u) {
-      const int i = base + 32 * u;
-      if (i < vecs) {
-        float fa[8], fb[8], fh[8];
-        unpack8<T>(ra[u], fa);
-        unpack8<T>(rb[u], fb);
-        unpack8<T>(s_hidden[i], fh);
+      float fa[8], fb[8], fh[8];
+      unpack8<T>(ra[u], fa);
+      unpack8<T>(rb[u], fb);
+      unpack8<T>(rh[u], fh);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          acc_a = fmaf(fa[j], fh[j], acc_a);
-          acc_b = fmaf(fb[j], fh[j], acc_b);
-        }
+      for (int j = 0; j < 8; ++j) {
+        acc_a = fmaf(fa[j], fh[j], acc_a);
+        acc_b = fmaf(fb[j], fh[j], acc_b);
       }
     }
   }
@@ -97,9 +95,20 @@ qkv_rope_kernel(const T* __restrict__ hidden, const T* __restrict__ w_q,
     acc_a += __shfl_xor_sync(0xffffffffu, acc_a, off);
     acc_b += __shfl_xor_sync(0xffffffffu, acc_b, off);
   }
-  if (lane != 0) return;
-  const T xa = from_f32<T>(acc_a);  // channel c
-  const T xb = from_f32<T>(acc_b);  // channel c + 64
+  if (lane == 0) {
+    s_part[warp][0] = acc_a;
+    s_part[warp][1] = acc_b;
+  }
+  __syncthreads();
+  if (tid != 0) return;
+  float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kFrontThreads / 32; ++k) {
+    sa += s_part[k][0];
+    sb += s_part[k][1];
+  }
+  const T xa = from_f32<T>(sa);  // channel c
+  const T xb = from_f32<T>(sb);  // channel c + 64
   if (!rotate) {
     dst[c] = xa;
     dst[c + kFrontHalf] = xb;
@@ -132,23 +141,15 @@ extern "C" int tw_qkv_rope(const void* hidden, const void* w_q, const void* w_k,
     return TW_ERR_BAD_ARG;
   if ((((uintptr_t)hidden | (uintptr_t)w_q | (uintptr_t)w_k | (uintptr_t)w_v) & 15) != 0)
     return TW_ERR_BAD_ARG;
-  const size_t smem = (size_t)hidden_size * 2;
-  static DynSmemOptIn opt_in_h, opt_in_b;
   const int pairs = (n_q_heads + 2 * n_kv_heads) * kFrontHalf;
-  const dim3 grid((pairs + kFrontThreads / 32 - 1) / (kFrontThreads / 32));
   cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == TW_F16) {
-    const int s = ensure_dyn_smem((const void*)qkv_rope_kernel<__half>, opt_in_h, (int)smem);
-    if (s != TW_OK) return s;
-    return launch_pdl(qkv_rope_kernel<__half>, grid, dim3(kFrontThreads), smem, st,
+  if (dtype == TW_F16)
+    return launch_pdl(qkv_rope_kernel<__half>, dim3(pairs), dim3(kFrontThreads), 0, st,
                       (const __half*)hidden, (const __half*)w_q, (const __half*)w_k,
                       (const __half*)w_v, hidden_size, n_q_heads, n_kv_heads,
                       (const __half*)cos, (const __half*)sin, (__half*)q_out, (__half*)k_out,
                       (__half*)v_out);
-  }
-  const int s = ensure_dyn_smem((const void*)qkv_rope_kernel<__nv_bfloat16>, opt_in_b, (int)smem);
-  if (s != TW_OK) return s;
-  return launch_pdl(qkv_rope_kernel<__nv_bfloat16>, grid, dim3(kFrontThreads), smem, st,
+  return launch_pdl(qkv_rope_kernel<__nv_bfloat16>, dim3(pairs), dim3(kFrontThreads), 0, st,
                     (const __nv_bfloat16*)hidden, (const __nv_bfloat16*)w_q,
                     (const __nv_bfloat16*)w_k, (const __nv_bfloat16*)w_v, hidden_size, n_q_heads,
                     n_kv_heads, (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin,
