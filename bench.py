@@ -525,8 +525,8 @@ def run_ours(args) -> int:
                 # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one
                 # ncu --set full capture of a launch of this workload; the host-link
                 # bytes are the sysmem read sectors (x 32 B) of the same capture
-                "traffic": (29492224 if step.reuse else 369408) if step.fused else None,
-                "traffic_host_link": (4210176 if step.reuse else 35748352) if step.fused else None,
+                "traffic": (29492224 if step.reuse else 361216) if step.fused else None,
+                "traffic_host_link": (4210176 if step.reuse else 33984000) if step.fused else None,
                 "traffic_source": ("ncu --set full, one launch of attention_kernel<UnionRows> on "
                                    "this workload (profiles/)") if step.fused else None,
                 "mapped_read_peak_gbs": round(mapped, 2),
