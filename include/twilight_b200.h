@@ -329,8 +329,12 @@ int tw_attend_union(const void* slab_k, const void* slab_v, const uint64_t* entr
 /* ---- whole decode layer-step --------------------------------------------------------------------------
  * One decode layer-step of the Twilight GQA path in one call: Quest score ->
  * top-k pages -> INT4 QK -> top-p + union -> fused union gather + attention ->
- * new-token append (3 launches on `stream` when the fused selection serves
- * the shape, else 6; no host synchronisation).
+ * new-token append, with no host synchronisation.  When the fused selection
+ * serves the shape this is 2 launches on `stream`: the selection, whose extra
+ * cluster also appends the new token (position old_length, which neither the
+ * selection nor the attention of this step reads) and stages the protected
+ * rows, then the fused attention.  Otherwise the per-stage kernels, the
+ * attention and the append kernel run (6 launches).
  * Replaces prepare_layer_selection + update_layer_gqa_group_ragged + the
  * FlashAttention call of one layer (hi/twilight_offload_cache.py:996-1843,
  * :2610-3602, hi/mp.py:233-279).  Cache pointers (slab, page min/max, INT4
