@@ -593,20 +593,25 @@ def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False, numa=None) ->
                      layer.values[e].view(1, 1, L, 128).to(device), e)
     torch.cuda.synchronize()
     host_q = queries.pin_memory()
-    host_k = layer.key_new.view(G, 1, 1, 1, 128).pin_memory()
-    host_v = layer.value_new.view(G, 1, 1, 1, 128).pin_memory()
     out_host = torch.empty((G, R, 128), dtype=torch.float16, pin_memory=True)
     entries = list(range(G))
 
-    q_dev = torch.empty((G, R, 128), dtype=torch.float16, device=device)
-    kv_dev = torch.empty((2, G, 128), dtype=torch.float16, device=device)
-    host_kv = torch.stack((layer.key_new, layer.value_new)).pin_memory()
+    # Each step's inputs (query, new K, new V) packed in one pinned row, so a
+    # step is one H2D copy, one decode_layer call and one D2H copy.
+    nq, nkv = G * R * 128, G * 128
+    host_in = torch.empty((host_q.shape[0], nq + 2 * nkv), dtype=torch.float16).pin_memory()
+    host_in[:, :nq] = host_q.reshape(host_q.shape[0], nq)
+    host_in[:, nq:nq + nkv] = layer.key_new.reshape(1, nkv)
+    host_in[:, nq + nkv:] = layer.value_new.reshape(1, nkv)
+    in_dev = torch.empty(nq + 2 * nkv, dtype=torch.float16, device=device)
+    q_dev = in_dev[:nq].view(G, R, 128)
+    k_dev = in_dev[nq:nq + nkv].view(G, 128)
+    v_dev = in_dev[nq + nkv:].view(G, 128)
     out_dev = torch.empty((G, R, 128), dtype=torch.float16, device=device)
 
     def one(i):
-        q_dev.copy_(host_q[i], non_blocking=True)
-        kv_dev.copy_(host_kv, non_blocking=True)
-        cache.decode_layer(queries=q_dev, key_states=kv_dev[0], value_states=kv_dev[1],
+        in_dev.copy_(host_in[i], non_blocking=True)
+        cache.decode_layer(queries=q_dev, key_states=k_dev, value_states=v_dev,
                            entries=entries, out=out_dev)
         out_host.copy_(out_dev, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
