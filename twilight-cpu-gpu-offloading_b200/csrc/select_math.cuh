@@ -67,6 +67,55 @@ __device__ __forceinline__ void quest_page_score2(const float (&qr)[R][4], const
   }
 }
 
+// quest_page_score with 8 threads per page.  Thread j (0..7) of the page's
+// 8-thread group holds the partial sums of lanes l = 4j .. 4j+3 of the warp
+// layout above (the same products added in the same order: channels l, l+32,
+// l+64, l+96), then combines them in the same tree: the lane offsets 1 and 2
+// inside the thread, the lane offsets 4, 8, 16 as group offsets 1, 2, 4.
+// Bit-identical to quest_page_score, with 8-byte loads (4 channels) and a
+// quarter of its shuffles.  q: the R query rows as fp32 [R][D] in shared
+// memory.  valid = false: no loads, the result is unused.  The result is
+// valid in thread j = 0; all 32 lanes of the warp must call this together.
+template <typename T, int R>
+__device__ __forceinline__ void quest_page_score8(const float* __restrict__ q,
+                                                  const T* __restrict__ gmin,
+                                                  const T* __restrict__ gmax, int64_t p, int j,
+                                                  bool valid, float (&out)[R]) {
+  float lo[4][4], hi[4][4];  // [c][i]: channel 32 c + 4 j + i
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint2 a = make_uint2(0u, 0u), b = make_uint2(0u, 0u);
+    if (valid) {
+      a = *reinterpret_cast<const uint2*>(gmin + p * kHeadDim + 32 * c + 4 * j);
+      b = *reinterpret_cast<const uint2*>(gmax + p * kHeadDim + 32 * c + 4 * j);
+    }
+    const T* ta = reinterpret_cast<const T*>(&a);
+    const T* tb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      lo[c][i] = to_f32(ta[i]);
+      hi[c][i] = to_f32(tb[i]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float4 qv = *reinterpret_cast<const float4*>(q + r * kHeadDim + 32 * c + 4 * j);
+      const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        part[i] = __fadd_rn(part[i], __fmul_rn(qq[i] > 0.0f ? hi[c][i] : lo[c][i], qq[i]));
+    }
+    float v = __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3]));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 8));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 8));
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 8));
+    out[r] = v;
+  }
+}
+
 // INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
 // covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
 // k = code * s + m (the values of separately rounded mul and add, as the

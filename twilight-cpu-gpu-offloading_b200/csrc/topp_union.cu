@@ -587,7 +587,7 @@ struct SelectArgs {
 __host__ __device__ __forceinline__ size_t select_smem_bytes(int P, int b0, int n, int64_t L) {
   const size_t words = (size_t)((L + 31) / 32);
   return align16((size_t)P * 4) + align16((size_t)b0 * 4) + align16((size_t)n * 4) +
-         (size_t)n * 8 + align16(words * 4) + align16((size_t)n) +
+         align16((size_t)n * 8) + align16(words * 4) + align16((size_t)n) +
          (size_t)kMaxHeadsPerGroup * kHeadDim * 4;
 }
 
@@ -635,7 +635,7 @@ select_layer_kernel(SelectArgs a) {
   float* s_logit = reinterpret_cast<float*>(cur);
   cur += align16((size_t)n * 4);
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(cur);
-  cur += (size_t)n * 8;
+  cur += align16((size_t)n * 8);
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(cur);
   cur += align16((size_t)words * 4);
   unsigned char* sel = cur;
@@ -659,11 +659,6 @@ select_layer_kernel(SelectArgs a) {
 
   // 1. Quest scores of the group's R heads.
   {
-    float qr[R][4];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) qr[r][c] = s_q[r * kHeadDim + lane + 32 * c];
     const T* gmin = reinterpret_cast<const T*>(a.pmin) + (int64_t)g * a.meta_stride;
     const T* gmax = reinterpret_cast<const T*>(a.pmax) + (int64_t)g * a.meta_stride;
     float* owner_scores[R];
@@ -678,22 +673,18 @@ select_layer_kernel(SelectArgs a) {
     if (tid < 2 && p_end > p_beg)
       prefetch_l2((tid == 0 ? gmin : gmax) + (int64_t)p_beg * kHeadDim,
                   (size_t)(p_end - p_beg) * kHeadDim * sizeof(T));
-    // two pages per warp and pass: both pages' loads are issued together
-    const int stride = nwarps;
-    for (int p = p_beg + warp; p < p_end; p += 2 * stride) {
-      const int p2 = p + stride < p_end ? p + stride : P;
-      float sc[R], sc2[R];
-      if (p2 < P) {
-        quest_page_score2<T, R>(qr, gmin, gmax, p, p2, lane, sc, sc2);
-      } else {
-        quest_page_score<T, R>(qr, gmin, gmax, p, lane, sc);
-      }
-      if (lane == 0) {
+    // 8 threads per page, 4 pages per warp and pass (the pass index is
+    // warp-uniform: the 8-thread shuffles need the whole warp).
+    const int j8 = lane & 7;
+    const int groups_per_cta = (int)(blockDim.x >> 3);
+    for (int base = p_beg + warp * 4; base < p_end; base += groups_per_cta) {
+      const int p = base + (lane >> 3);
+      const bool valid = p < p_end;
+      float sc[R];
+      quest_page_score8<T, R>(s_q, gmin, gmax, valid ? p : p_beg, j8, valid, sc);
+      if (valid && j8 == 0) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          owner_scores[r][p] = sc[r];
-          if (p2 < P) owner_scores[r][p2] = sc2[r];
-        }
+        for (int r = 0; r < R; ++r) owner_scores[r][p] = sc[r];
       }
     }
   }
@@ -1027,6 +1018,9 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
   if (q_dtype != TW_F32 && q_dtype != dtype) return TW_ERR_BAD_ARG;
   size_t smem = 0;
   if (!select_fused_supported(R, n_pages, b0, block, old_length, &smem)) return TW_ERR_UNSUPPORTED;
+  // 8-byte page-row loads (4 channels) in the Quest phase
+  if ((((uintptr_t)pmin | (uintptr_t)pmax) & 7) != 0 || meta_stride % 4 != 0)
+    return TW_ERR_UNSUPPORTED;
   SelectArgs a{};
   a.q = q;
   a.pmin = pmin;
