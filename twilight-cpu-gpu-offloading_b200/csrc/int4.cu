@@ -71,7 +71,7 @@ int4_qk_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ packed,
       const int64_t pos = (int64_t)sink + (int64_t)page * block + (n % block);
       const int64_t tr = ebase + pos;
       const uint4 c = __ldg(reinterpret_cast<const uint4*>(packed + tr * (kHeadDim / 2)) + sub);
-      acc = int4_dot32(c, to_f32(scale[tr * ngroups + grp]), to_f32(minimum[tr * ngroups + grp]),
+      acc = int4_dot32<T>(c, scale[tr * ngroups + grp], to_f32(minimum[tr * ngroups + grp]),
                        qr);
     }
     const float logit = int4_logit(acc, inv_sqrt_d);

@@ -118,39 +118,73 @@ __device__ __forceinline__ void quest_page_score8(const float* __restrict__ q,
 
 // INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
 // covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
-// k = code * s + m (the values of separately rounded mul and add, as the
-// reference dequantises), then acc[c % 4] = fma(k, q, acc[c % 4]) over the
-// lane's channels c = 0..31 in order (fused multiply-adds, as torch.matmul's
-// fp32 GEMV of hi/twilight_offload_cache.py:1257 accumulates on CUDA), and the
-// lane's sum is (acc0 + acc1) + (acc2 + acc3).  Four interleaved accumulators
-// keep four independent FMA chains per lane.  s and m are fp16 / bf16 values.
-// A code v in 0..15 as float, exactly: the bits 0x4B0000vv are the float
-// 2^23 + v, from which 2^23 is subtracted (exact).  One byte permute puts
-// byte b of `nibbles` (one code per byte) under the exponent 0x4B.
-__device__ __forceinline__ float nibble_float(uint32_t nibbles, int b) {
-  return __fsub_rn(__int_as_float(__byte_perm(nibbles, 0x4B000000u, 0x7440u | (uint32_t)b)),
-                   8388608.0f);
+// k = code * s + m, the value of the reference's separately rounded mul and
+// add (code * s is exact in fp32: a 4-bit integer times a value of at most 11
+// significant bits, so one rounding of code * s + m equals the two), then
+// acc[c % 4] = fma(k, q, acc[c % 4]) over the lane's channels c = 0..31 in
+// order (fused multiply-adds, as torch.matmul's fp32 GEMV of
+// hi/twilight_offload_cache.py:1257 accumulates on CUDA), and the lane's sum is
+// (acc0 + acc1) + (acc2 + acc3).  Four interleaved accumulators keep four
+// independent FMA chains per lane.
+//
+// The dequantisation is one mixed-precision fused multiply-add per channel
+// (sm_100: fma.rn.f32.f16 / .bf16, the 16-bit operands exact in fp32, one
+// rounding).  Two codes become a pair of 16-bit values exactly: a byte permute
+// writes 0x64 (fp16) or 0x43 (bf16) above each code, the value 1024 + v or
+// 128 + v, and one packed subtraction of 1024 or 128 leaves v.  s is the scale
+// in the K dtype, m the minimum widened to fp32.
+template <typename T> __device__ __forceinline__ uint32_t code_pair(uint32_t bytes, uint32_t sel);
+template <> __device__ __forceinline__ uint32_t code_pair<__half>(uint32_t bytes, uint32_t sel) {
+  const uint32_t x = __byte_perm(bytes, 0x64646464u, sel);  // fp16 1024 + v
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  h = __hsub2(h, __half2(__ushort_as_half(0x6400u), __ushort_as_half(0x6400u)));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t code_pair<__nv_bfloat16>(uint32_t bytes, uint32_t sel) {
+  const uint32_t x = __byte_perm(bytes, 0x43434343u, sel);  // bf16 128 + v
+  __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&x);
+  h = __hsub2(h, __nv_bfloat162(__ushort_as_bfloat16(0x4300u), __ushort_as_bfloat16(0x4300u)));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <typename T> __device__ __forceinline__ float fma_mixed(uint16_t a, uint16_t b, float c);
+template <> __device__ __forceinline__ float fma_mixed<__half>(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+template <> __device__ __forceinline__ float fma_mixed<__nv_bfloat16>(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+template <typename T> __device__ __forceinline__ uint16_t bits16(T x);
+template <> __device__ __forceinline__ uint16_t bits16<__half>(__half x) { return __half_as_ushort(x); }
+template <> __device__ __forceinline__ uint16_t bits16<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat16_as_ushort(x);
 }
 
-__device__ __forceinline__ float int4_dot32(const uint4& codes, float s, float m,
-                                            const float (&qr)[32]) {
+template <typename T>
+__device__ __forceinline__ float int4_dot32(const uint4& codes, T s, float m,
+                                                  const float (&qr)[32]) {
   const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+  const uint16_t sb = bits16<T>(s);
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
-    const uint32_t lo = words[w] & 0x0f0f0f0fu;         // even channels, one per byte
-    const uint32_t hi = (words[w] >> 4) & 0x0f0f0f0fu;  // odd channels
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int i = 8 * w + 2 * b;  // channels i (even) and i + 1 (odd)
-      // code * s is exact in fp32 (a 4-bit integer times a value of at most
-      // 11 significant bits), so the fused multiply-add rounds exactly as the
-      // separately rounded code * s + m does.
-      const float k0 = __fmaf_rn(nibble_float(lo, b), s, m);
-      acc[i & 3] = __fmaf_rn(k0, qr[i], acc[i & 3]);
-      const float k1 = __fmaf_rn(nibble_float(hi, b), s, m);
-      acc[(i + 1) & 3] = __fmaf_rn(k1, qr[i + 1], acc[(i + 1) & 3]);
-    }
+    const uint32_t lo = words[w] & 0x0f0f0f0fu;         // byte b: channel 8w + 2b
+    const uint32_t hi = (words[w] >> 4) & 0x0f0f0f0fu;  // byte b: channel 8w + 2b + 1
+    // pairs: (8w, 8w+2), (8w+4, 8w+6), (8w+1, 8w+3), (8w+5, 8w+7)
+    const uint32_t p0 = code_pair<T>(lo, 0x5140u), p1 = code_pair<T>(lo, 0x5342u);
+    const uint32_t p2 = code_pair<T>(hi, 0x5140u), p3 = code_pair<T>(hi, 0x5342u);
+    const int i = 8 * w;
+    acc[0] = __fmaf_rn(fma_mixed<T>((uint16_t)p0, sb, m), qr[i + 0], acc[0]);
+    acc[1] = __fmaf_rn(fma_mixed<T>((uint16_t)p2, sb, m), qr[i + 1], acc[1]);
+    acc[2] = __fmaf_rn(fma_mixed<T>((uint16_t)(p0 >> 16), sb, m), qr[i + 2], acc[2]);
+    acc[3] = __fmaf_rn(fma_mixed<T>((uint16_t)(p2 >> 16), sb, m), qr[i + 3], acc[3]);
+    acc[0] = __fmaf_rn(fma_mixed<T>((uint16_t)p1, sb, m), qr[i + 4], acc[0]);
+    acc[1] = __fmaf_rn(fma_mixed<T>((uint16_t)p3, sb, m), qr[i + 5], acc[1]);
+    acc[2] = __fmaf_rn(fma_mixed<T>((uint16_t)(p1 >> 16), sb, m), qr[i + 6], acc[2]);
+    acc[3] = __fmaf_rn(fma_mixed<T>((uint16_t)(p3 >> 16), sb, m), qr[i + 7], acc[3]);
   }
   return __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
 }

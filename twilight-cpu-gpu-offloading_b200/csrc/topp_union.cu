@@ -809,7 +809,8 @@ select_layer_kernel(SelectArgs a) {
     // flight while the group computes.  Candidate i is token
     // sink + prow[i / block] * block + i % block of the group's entry.
     uint4 codes_n = make_uint4(0u, 0u, 0u, 0u);
-    float sv_n = 0.0f, mv_n = 0.0f;
+    T sv_n = from_f32<T>(0.0f);
+    float mv_n = 0.0f;
     auto load = [&](int i) {
       if (i < c_end) {
         int pg, t;
@@ -822,7 +823,7 @@ select_layer_kernel(SelectArgs a) {
         }
         const int64_t tr = tbase + (int64_t)prow[pg] * a.block + t;
         codes_n = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
-        sv_n = to_f32(scale[tr * ngroups + grp]);
+        sv_n = scale[tr * ngroups + grp];
         mv_n = to_f32(minimum[tr * ngroups + grp]);
       }
     };
@@ -831,9 +832,10 @@ select_layer_kernel(SelectArgs a) {
     load(base + tok);
     for (; base < c_end; base += kStep) {
       const uint4 codes = codes_n;
-      const float sv = sv_n, mv = mv_n;
+      const T sv = sv_n;
+      const float mv = mv_n;
       load(base + kStep + tok);
-      const float logit = int4_logit(int4_dot32(codes, sv, mv, qr), a.inv_sqrt_d);
+      const float logit = int4_logit(int4_dot32<T>(codes, sv, mv, qr), a.inv_sqrt_d);
       if (base + tok < c_end && sub == 0) lout[base + tok] = logit;
     }
   }
