@@ -530,11 +530,11 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
 // ---- whole-layer selection in one launch --------------------------------------------------
 // One thread-block cluster of C CTAs per KV group (C = 16, the largest
 // cluster B200 schedules, when every group's cluster fits at once, else 8)
-// runs the four
-// selection stages with every intermediate in shared memory:
-//  1. Quest scores: all CTAs of the cluster split the candidate pages; each
-//     page's R scores go to the shared memory of the R row owners (CTA r owns
-//     query head r) over distributed shared memory;
+// runs the four selection stages with every intermediate in shared memory:
+//  1. Quest scores: all CTAs of the cluster split the candidate pages, 8
+//     threads per page (quest_page_score8); each page's R scores go to the
+//     shared memory of the R row owners (CTA r owns query head r) over
+//     distributed shared memory;
 //  2. top-k pages: each owner radix-selects its row in its own shared memory
 //     (as topk_pages_kernel);
 //  3. INT4 estimate: the row's candidates are split over the C / R
@@ -545,6 +545,9 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
 //     bitmap words.
 // Scores, pages, logits and selections are bit-identical to the per-stage
 // kernels (same arithmetic, select_math.cuh).
+// One further cluster, when the caller asks for it, does work independent of
+// this step's selection while it runs: it appends the new token (position
+// old_length) and stages the protected rows (ProtectedStage).
 constexpr int kSelCluster = 8;      // portable cluster size
 constexpr int kSelClusterWide = 16; // non-portable cluster size
 
