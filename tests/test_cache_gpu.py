@@ -241,7 +241,7 @@ def test_error_paths(tw, cuda):
     small.close()
 
 
-@pytest.mark.parametrize("R,dtype", [(4, "float16"), (8, "bfloat16")])
+@pytest.mark.parametrize("R,dtype", [(4, "float16"), (8, "bfloat16"), (3, "bfloat16")])
 def test_decode_layer_equals_prepare_plus_attend(tw, cuda, R, dtype):
     """The one-call layer-step (tw_twilight_decode_layer) gives the same unions
     and attention output, bit for bit, as prepare_layer_selection + attend_layer,

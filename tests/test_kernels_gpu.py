@@ -430,13 +430,15 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
 
 
 @pytest.mark.parametrize("R,L,budget", [(1, 3007, 768), (2, 3014, 768), (3, 3021, 768),
-                                         (4, 3028, 768), (8, 3056, 768), (8, 131072, 4096)])
+                                         (4, 3028, 768), (5, 3035, 768), (6, 3042, 768),
+                                         (8, 3056, 768), (8, 131072, 4096)])
 @pytest.mark.parametrize("dtype,group", [("float16", 32), ("bfloat16", 128), ("bfloat16", 64)])
 def test_select_layer_fused_equals_stages(tw, cuda, R, L, budget, dtype, group):
-    """tw_select_layer (one cluster launch per layer when R divides the cluster)
-    gives the per-stage kernels' pages, per-head counts and positions and the
-    union, bit for bit; R = 3 exercises the per-stage fallback, 131072 tokens
-    with B0 4096 the config-5 shape."""
+    """tw_select_layer (one cluster launch per layer for R in 1, 2, 3, 4, 6, 8,
+    clusters of 8 CTAs, or 6 for R = 3 and 6) gives the per-stage kernels'
+    pages, per-head counts and positions and the union, bit for bit; R = 5
+    exercises the per-stage fallback, 131072 tokens with B0 4096 the config-5
+    shape."""
     G, sink, recent, block = 3 if L < 100000 else 2, 64, 256, 16
     layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=dtype, seed=70 + R,
                              workload="needles" if R % 2 else "outliers", sink=sink,

@@ -372,7 +372,7 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
                            a->first_entry, a->old_length, a->k_new, a->v_new, a->sink,
                            a->block_size, a->page_min, a->page_max, a->page_capacity * kHeadDim,
                            a->packed, a->scale, a->minimum, a->int4_group_size);
-    fuse_append = (int64_t)G * kHeadDim <= 8 * 1024;  // one extra cluster covers it
+    fuse_append = (int64_t)G * kHeadDim <= 6 * 1024;  // one extra cluster (>= 6 CTAs) covers it
   }
   int rc = select_layer_fused(a->q, a->dtype, pmin, pmax, a->page_capacity * kHeadDim, a->n_pages,
                               packed, scale, minimum, a->max_len, G, R, a->b0_pages, a->block_size,

@@ -551,6 +551,15 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
 constexpr int kSelCluster = 8;      // portable cluster size
 constexpr int kSelClusterWide = 16; // non-portable cluster size
 
+// Query heads per group the fused selection serves, and its cluster sizes for
+// them: the largest multiple of R within 8 (portable) or 16 (non-portable),
+// so that every query head's row is shared by the same number of CTAs.
+__host__ __device__ constexpr bool select_fused_r(int R) {
+  return R == 1 || R == 2 || R == 3 || R == 4 || R == 6 || R == 8;
+}
+__host__ __device__ constexpr int select_cluster_narrow(int R) { return R * (kSelCluster / R); }
+__host__ __device__ constexpr int select_cluster_wide(int R) { return R * (kSelClusterWide / R); }
+
 struct SelectArgs {
   const void* q;          // [G][R][D], QT
   const void* pmin;       // first group's page min / max, K dtype
@@ -900,25 +909,27 @@ select_layer_kernel(SelectArgs a) {
   cluster.sync();  // the leader's bitmap is read until here
 }
 
-// Whether the fused selection serves this shape (R dividing the cluster, and
+// Whether the fused selection serves this shape (select_fused_r(R), and
 // the shared memory fitting one CTA).
 bool select_fused_supported(int R, int P, int b0, int block, int64_t L, size_t* smem) {
-  if (R <= 0 || kSelCluster % R != 0 || b0 <= 0 || P <= 0) return false;  // R | 8 | 16
+  if (!select_fused_r(R) || b0 <= 0 || P <= 0) return false;
   const int64_t n = (int64_t)b0 * block;
   if (n > 65536 || L > ((int64_t)1 << 30)) return false;
   *smem = select_smem_bytes(P, b0, (int)n, L);
   return *smem <= 160 * 1024;
 }
 
-// Clusters of 16 CTAs when the device can run at least `groups` of them at
-// once (queried once per device and kernel; the kernel needs one SM per CTA
-// at the shared memory the fused selection may use), else clusters of 8.
+// Wide clusters (16 CTAs; 15 or 12 for R = 3 or 6) when the device can run
+// at least `groups` of them at once (queried once per device and kernel; the
+// kernel needs one SM per CTA at the shared memory the fused selection may
+// use), else narrow ones (8; 6 for R = 3 or 6).
 template <typename T, typename QT, int R>
 int select_cluster_size(int groups) {
   static int wide_clusters[kMaxDevices];  // 0: not queried, -1: none
   static std::mutex mu;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kSelCluster;
+  constexpr int narrow = select_cluster_narrow(R), wide = select_cluster_wide(R);
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return narrow;
   std::lock_guard<std::mutex> lk(mu);
   if (wide_clusters[dev] == 0) {
     int n = -1;
@@ -927,12 +938,12 @@ int select_cluster_size(int groups) {
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
             cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(kSelClusterWide, 1, 1);
+      cfg.gridDim = dim3(wide, 1, 1);
       cfg.blockDim = dim3(kTopPThreads, 1, 1);
       cfg.dynamicSmemBytes = 160 * 1024;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = kSelClusterWide;
+      attr[0].val.clusterDim.x = wide;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
@@ -943,7 +954,7 @@ int select_cluster_size(int groups) {
     cudaGetLastError();  // a refused query leaves no error behind
     wide_clusters[dev] = n;
   }
-  return wide_clusters[dev] >= groups ? kSelClusterWide : kSelCluster;
+  return wide_clusters[dev] >= groups ? wide : narrow;
 }
 
 template <typename T, typename QT, int R>
@@ -980,7 +991,9 @@ int launch_select_t(const SelectArgs& a, int groups, int R, size_t smem, cudaStr
   switch (R) {
     case 1: return launch_select_r<T, QT, 1>(a, groups, smem, stream);
     case 2: return launch_select_r<T, QT, 2>(a, groups, smem, stream);
+    case 3: return launch_select_r<T, QT, 3>(a, groups, smem, stream);
     case 4: return launch_select_r<T, QT, 4>(a, groups, smem, stream);
+    case 6: return launch_select_r<T, QT, 6>(a, groups, smem, stream);
     case 8: return launch_select_r<T, QT, 8>(a, groups, smem, stream);
     default: return TW_ERR_UNSUPPORTED;
   }
@@ -999,7 +1012,7 @@ int launch_select_fused(const SelectArgs& a, int groups, int R, int q_dtype, int
 }
 
 // The whole Twilight selection of one layer in one launch when the shape
-// allows it (R dividing kSelCluster, shared memory fitting a CTA); returns
+// allows it (select_fused_r(R), shared memory fitting a CTA); returns
 // TW_ERR_UNSUPPORTED otherwise, and the caller runs the per-stage kernels.
 // Same arguments and checks as tw_select_layer's stages; q in fp32 or the K dtype.
 int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void* pmax,
@@ -1068,8 +1081,10 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
     a.stage = *stage;
   }
   if (append) {
-    // the extra cluster (kSelCluster CTAs of kTopPThreads) covers 128 threads per group
-    if ((int64_t)groups * kHeadDim > (int64_t)kSelCluster * kTopPThreads) return TW_ERR_UNSUPPORTED;
+    // the extra cluster (at least select_cluster_narrow(R) CTAs of kTopPThreads)
+    // covers 128 threads per group
+    if ((int64_t)groups * kHeadDim > (int64_t)select_cluster_narrow(R) * kTopPThreads)
+      return TW_ERR_UNSUPPORTED;
     a.append = *append;
     a.do_append = 1;
   }
