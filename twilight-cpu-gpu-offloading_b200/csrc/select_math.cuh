@@ -36,37 +36,6 @@ __device__ __forceinline__ void quest_page_score(const float (&qr)[R][4], const 
   }
 }
 
-// quest_page_score for two pages at once (both pages' loads issued first).
-template <typename T, int R>
-__device__ __forceinline__ void quest_page_score2(const float (&qr)[R][4], const T* __restrict__ gmin,
-                                                  const T* __restrict__ gmax, int64_t p, int64_t p2,
-                                                  int lane, float (&out)[R], float (&out2)[R]) {
-  float lo[4], hi[4], lo2[4], hi2[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    lo[c] = to_f32(gmin[p * kHeadDim + lane + 32 * c]);
-    hi[c] = to_f32(gmax[p * kHeadDim + lane + 32 * c]);
-    lo2[c] = to_f32(gmin[p2 * kHeadDim + lane + 32 * c]);
-    hi2[c] = to_f32(gmax[p2 * kHeadDim + lane + 32 * c]);
-  }
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float acc = 0.0f, acc2 = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      acc = __fadd_rn(acc, __fmul_rn(qr[r][c] > 0.0f ? hi[c] : lo[c], qr[r][c]));
-      acc2 = __fadd_rn(acc2, __fmul_rn(qr[r][c] > 0.0f ? hi2[c] : lo2[c], qr[r][c]));
-    }
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, off));
-      acc2 = __fadd_rn(acc2, __shfl_down_sync(0xffffffffu, acc2, off));
-    }
-    out[r] = acc;
-    out2[r] = acc2;
-  }
-}
-
 // quest_page_score with 8 threads per page.  Thread j (0..7) of the page's
 // 8-thread group holds the partial sums of lanes l = 4j .. 4j+3 of the warp
 // layout above (the same products added in the same order: channels l, l+32,
