@@ -4,7 +4,7 @@ new-token append) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the metric's configuration): one decoder layer
+Workload (cfg2, the configuration the metric is quoted on): one decoder layer
 with 8 KV heads x 4 query heads, head_dim 128, 32768 tokens of fp16 K/V in a
 pinned, device-mapped host slab, K ~ N(0,1) with 4 outlier channels per KV
 head scaled by exp(N(0,1)), INT4 group 32, Quest B0 4096 tokens (256 pages of
@@ -14,7 +14,12 @@ is one layer-step; each timed step uses a fresh query, and L2 is flushed
 
 With N > 1 (torchrun) every rank runs its own request (its own slab on its
 own GPU): request sharding, no collective on the data path; the timed region
-is bracketed by barriers and the max over ranks is reported.
+is bracketed by barriers and the max over ranks is reported.  The host-link
+peaks and the public-API (e2e) leg run on every rank at once.  The same line
+carries two sharded sub-runs: "cfg5" (one 70B-shaped request at 131072
+tokens, KV heads sharded over the ranks, an NCCL all-gather of the per-head
+outputs per layer) and "cfg4" (16 requests of 8192..131072 tokens, 2 per
+rank, no collective).
 """
 
 from __future__ import annotations
@@ -118,19 +123,69 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def pinned_h2d_peak_gbs(device: torch.device, nbytes: int = 256 << 20) -> float:
+def max_over_ranks(x: float, device, world: int) -> float:
+    if world == 1:
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed_ms(fn) -> float:
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e)
+
+
+def link_peaks(tw, slab, device, world: int, reps: int = 6) -> dict:
+    """Host-link peaks with every rank probing at the same time (a barrier
+    before each repetition, the slowest rank's time per repetition):
+
+    * copy: a 256 MiB pinned host -> device cudaMemcpyAsync (copy engine);
+    * mapped: a sequential zero-copy read of this rank's mapped slab (all its
+      K and V rows, tw_gather_kv: SM 16-byte loads, the attention kernel's
+      access path).
+
+    Per mechanism: the best single-rank GB/s and the best aggregate GB/s
+    (world x bytes / the slowest rank's time).  With world = 1 both are the
+    one GPU's peak."""
+    nbytes = 256 << 20
     host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
-    best = 0.0
-    for _ in range(6):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        dev.copy_(host, non_blocking=True)
-        e.record()
-        e.synchronize()
-        best = max(best, nbytes / (s.elapsed_time(e) * 1e-3) / 1e9)
-    del host, dev
-    return best
+    D = slab.geometry.head_dim
+    n_rows = slab.geometry.num_entries * slab.geometry.max_cache_len
+    src_k = (slab.rows[0].reshape(n_rows, D), slab.key_device_ptr)
+    src_v = (slab.rows[1].reshape(n_rows, D), slab.value_device_ptr)
+    rows = torch.arange(n_rows, dtype=torch.int64, device=device)
+    out_k = torch.empty((n_rows, D), dtype=slab.dtype, device=device)
+    out_v = torch.empty_like(out_k)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    probes = {
+        "copy": (nbytes, lambda: dev.copy_(host, non_blocking=True)),
+        "mapped": (2 * n_rows * D * out_k.element_size(),
+                   lambda: tw.ops.gather_kv(src_k, src_v, rows, out_k, out_v, err)),
+    }
+    res = {}
+    for name, (nb, fn) in probes.items():
+        fn()  # warm-up
+        torch.cuda.synchronize()
+        single = agg = 0.0
+        for _ in range(reps):
+            if world > 1:
+                torch.distributed.barrier()
+            ms = _timed_ms(fn)
+            slowest = max_over_ranks(ms, device, world)
+            single = max(single, nb / (ms * 1e-3) / 1e9)
+            agg = max(agg, world * nb / (slowest * 1e-3) / 1e9)
+        res[name] = {"single_gbs": round(single, 2), "aggregate_gbs": round(agg, 2),
+                     "per_rank_gbs": round(agg / world, 2)}
+    if int(err.item()) != 0:
+        raise RuntimeError("mapped-read probe reported an invalid row")
+    del host, dev, out_k, out_v, rows
+    return res
 
 
 # --------------------------------------------------------------- workload ---
@@ -453,21 +508,32 @@ def run_ours(args) -> int:
     avg = {k: float(np.mean([b[k] for b in byts])) for k in byts[0]}
     brk_bytes = bytes_of(brk_log, W + K + 1)  # after the untimed per-stage step
 
-    t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    max_total_ms = float(t.item())
+    # Parity of one timed step: the first timed step's query again (same inputs,
+    # so the same outputs), its unions, per-head counts and attention output
+    # read back for the CPU leg's check.
+    step.load_query(q_dev[0])
+    step.run()
+    torch.cuda.synchronize()
+    gpu_check = {"q": queries[W].clone(), "out": step.out.cpu().clone(),
+                 "union_count": step.union_count.cpu().clone(),
+                 "union_pos": step.union_pos.cpu().clone(),
+                 "head_count": step.head_count.cpu().clone()}
+    if int(step.err.item()) != 0:
+        raise RuntimeError(f"device-side check failed: status {int(step.err.item())}")
 
-    e2e = None
+    max_total_ms = max_over_ranks(total_ms, device, world)
+    # host-link peaks with every rank probing at once, then the public-API leg
+    # on every rank at once; both between barriers, max over ranks
+    peaks_link = link_peaks(tw, step.slab, device, world)
+    e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W, world,
+                                           reuse=args.reuse, numa=args.numa)
+    sharded = ({} if args.no_sharded else
+               run_sharded(args, tw, device, world, rank, peaks_link["copy"]["per_rank_gbs"]))
     cpu = None
-    pinned = None
-    if rank == 0:
-        pinned = pinned_h2d_peak_gbs(device)
-        mapped = mapped_read_peak_gbs(tw, step, device)
-        e2e = None if args.no_e2e else run_e2e(tw, layer, queries, device, K, W, reuse=args.reuse,
-                                               numa=args.numa)
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        parity = parity_check(layer, gpu_check)
+        cpu = cpu_baseline(layer, queries[W:], budget_s=args.cpu_seconds)
     if world > 1:
         torch.distributed.barrier()
     slab_numa = {"requested": args.numa, "bound_node": step.slab.numa_node,
@@ -481,10 +547,13 @@ def run_ours(args) -> int:
         ms_per_step = max_total_ms / K
         value = world * K / (max_total_ms * 1e-3)
         dom = "attention" if step.fused else "gather"
-        gather_ms = float(np.mean(kern_ms[dom]))
         gather_gbs = float(np.mean([b["gather_bytes"] / (ms * 1e-3) / 1e9
                                     for b, ms in zip(brk_bytes, kern_ms[dom])]))
-        t_roof_ms = max(avg["hbm_bytes"] / (hbm_peak * 1e9), avg["host_bytes"] / (pinned * 1e9)) * 1e3
+        copy_pk, mapped_pk = peaks_link["copy"], peaks_link["mapped"]
+        # the denominator: this rank's share of the host-link copy peak with
+        # every rank copying at once (= the one-GPU copy peak at world 1)
+        link_peak = copy_pk["per_rank_gbs"]
+        t_roof_ms = max(avg["hbm_bytes"] / (hbm_peak * 1e9), avg["host_bytes"] / (link_peak * 1e9)) * 1e3
         line = {
             "metric": METRIC,
             "value": round(value, 3),
@@ -499,22 +568,10 @@ def run_ours(args) -> int:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "fp16 K/V, fp32 math",
-            "data": "synthetic (seeded splitmix64 normals; BASELINE config 2 shapes)",
-            "config": {
-                "workload": "cfg2: one layer, 8 KV x 4 Q heads, D 128, ctx 32768, fp16 K/V "
-                            "in a pinned mapped host slab, 4 lognormal outlier channels, INT4 g32, "
-                            "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
-                "l2": "flushed before every timed step (512 MiB device write, then read back so "
-                      "the remaining lines are clean; outside the events)",
-                "parallelism": f"request-sharded replicas x{world}",
-                "path": ("fused gather+attention" if step.fused else "staged gather then attention")
-                        + (" + previous-token row reuse" if step.reuse else ""),
-                "mean_union_rows": avg["union_rows"],
-                "queries": (f"AR(1) rho={rho} (step-to-step continuity)" if step.reuse
-                            else "independent N(0,1) per step"),
-                "slab_numa": slab_numa,
-            },
+            "dtype": DTYPE_NOTE,
+            "data": DATA_NOTE,
+            "config": cfg2_config(world, fused=step.fused, reuse=step.reuse, rho=rho),
+            "workload_stats": {"mean_union_rows": avg["union_rows"], "slab_numa": slab_numa},
             "clocks": clocks,
             "gpu_launches": step.launches_per_step * K * world,
             "kernel_ms": {n: round(float(np.mean(v)), 5) for n, v in kern_ms.items()},
@@ -525,10 +582,13 @@ def run_ours(args) -> int:
                 "kernel": ("attention_kernel<UnionRows> (fused zero-copy gather + split-K attention)"
                            if step.fused else "gather_union_kernel (zero-copy mapped-host reads)"),
                 "achieved": round(gather_gbs, 2),
-                "peak": round(pinned, 2),
-                "peak_source": "pinned H2D cudaMemcpyAsync measured in this run (256 MiB, best of 6)",
+                "peak": round(link_peak, 2),
+                "peak_source": ("pinned H2D cudaMemcpyAsync (256 MiB, best of 6) measured in this "
+                                "run" + ("" if world == 1 else
+                                         f" with all {world} ranks copying at once: this rank's "
+                                         "share of the aggregate")),
                 "unit": "GB/s",
-                "frac": round(gather_gbs / pinned, 4),
+                "frac": round(gather_gbs / link_peak, 4),
                 # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one
                 # ncu --set full capture of a launch of this workload; the host-link
                 # bytes are the sysmem read sectors (x 32 B) of the same capture
@@ -536,7 +596,12 @@ def run_ours(args) -> int:
                 "traffic_host_link": (4210176 if step.reuse else 33984000) if step.fused else None,
                 "traffic_source": ("ncu --set full, one launch of attention_kernel<UnionRows> on "
                                    "this workload (profiles/)") if step.fused else None,
-                "mapped_read_peak_gbs": round(mapped, 2),
+                "frac_of_mapped_read_peak": round(gather_gbs / mapped_pk["per_rank_gbs"], 4),
+                "link_peaks": peaks_link,
+                "link_peaks_note": ("copy = pinned H2D cudaMemcpyAsync (copy engine); mapped = "
+                                    "sequential zero-copy SM reads of the mapped slab (the "
+                                    "attention kernel's access path); aggregate = all ranks at "
+                                    "once, world x bytes / the slowest rank's time"),
             },
             "roofline_step": {
                 "t_roof_us": round(t_roof_ms * 1e3, 2),
@@ -546,7 +611,8 @@ def run_ours(args) -> int:
                 "hbm_bytes": avg["hbm_bytes"],
                 "hbm_peak_gbs": hbm_peak,
                 "hbm_peak_source": hbm_src,
-                "pinned_h2d_peak_gbs": round(pinned, 2),
+                "host_link_peak_gbs": round(link_peak, 2),
+                "host_link_peak_source": "copy peak per rank with all ranks at once (roofline.link_peaks)",
             },
             "e2e": e2e,
         }
@@ -556,37 +622,46 @@ def run_ours(args) -> int:
                 "mean_hit_rows": avg["hit_rows"],
                 "hbm_bytes_kept_rows": avg["reuse_hbm_bytes"],
             }
+        if parity is not None:
+            line["parity"] = parity
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        line.update(sharded)
         print(json.dumps(line), flush=True)
+        if parity is not None and not parity["ok"]:
+            raise RuntimeError(f"parity check failed: {parity}")
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
 
 
-def mapped_read_peak_gbs(tw, step: DeviceStep, device) -> float:
-    """Sequential zero-copy read bandwidth of the mapped slab (tw_gather_kv over contiguous rows)."""
-    n = 32768
-    rows = torch.arange(n, dtype=torch.int64, device=device)
-    out_k = torch.empty((n, 128), dtype=torch.float16, device=device)
-    out_v = torch.empty_like(out_k)
-    src_k = (step.slab.rows[0, 0], step.slab.key_device_ptr)
-    src_v = (step.slab.rows[1, 0], step.slab.value_device_ptr)
-    best = 0.0
-    for _ in range(5):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        tw.ops.gather_kv(src_k, src_v, rows, out_k, out_v, step.err)
-        e.record()
-        e.synchronize()
-        best = max(best, 2 * n * 256 / (s.elapsed_time(e) * 1e-3) / 1e9)
-    return best
+DTYPE_NOTE = "fp16 K/V, fp32 math"
+DATA_NOTE = "synthetic (seeded splitmix64 normals; cfg2 shapes)"
 
 
-def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False, numa=None) -> dict:
+def cfg2_config(world: int, fused: bool = True, reuse: bool = False, rho: float = 0.0) -> dict:
+    """The workload's config object, identical in both arms."""
+    return {
+        "workload": "cfg2: one layer, 8 KV x 4 Q heads, D 128, ctx 32768, fp16 K/V "
+                    "in a pinned mapped host slab, 4 lognormal outlier channels, INT4 g32, "
+                    "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
+        "l2": "flushed before every timed step (512 MiB device write, then read back so "
+              "the remaining lines are clean; outside the events)",
+        "parallelism": f"request-sharded replicas x{world}",
+        "path": ("fused gather+attention" if fused else "staged gather then attention")
+                + (" + previous-token row reuse" if reuse else ""),
+        "queries": (f"AR(1) rho={rho} (step-to-step continuity)" if reuse
+                    else "independent N(0,1) per step"),
+    }
+
+
+def run_e2e(tw, layer, queries, device, K, W, world: int = 1, reuse: bool = False,
+            numa=None) -> dict:
     """Same step through the public cache API with host buffers: per step H2D of
-    the query and the new token's K/V from pinned memory, prepare_layer_selection
-    + attend_layer, D2H of the attention output."""
+    the query and the new token's K/V from pinned memory, decode_layer, D2H of
+    the attention output, stream synchronisation.  Every rank runs it at the
+    same time (a barrier before the timed loop); the slowest rank's wall time
+    gives the whole job's rate."""
     G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
     cache = tw.TwilightMatchedBudgetOffloadedCache(
         num_cache_entries=G, max_cache_len=L + K + W + 8, head_dim=128, num_query_heads_per_kv=R,
@@ -625,10 +700,14 @@ def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False, numa=None) ->
 
     for i in range(W):
         one(i)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(K):
         one(W + i)
     dt = time.perf_counter() - t0
+    dt_max = max_over_ranks(dt, device, world)
     cache.synchronize()
     extra = {}
     if reuse:
@@ -637,17 +716,22 @@ def run_e2e(tw, layer, queries, device, K, W, reuse: bool = False, numa=None) ->
             sum(r["hit_rows"] for r in rows) / max(1, sum(r["history_rows"] for r in rows)), 4)
     cache.close()
     h2d = (G * R * 128 + 2 * G * 128) * 2
-    return {**extra,"value": round(K / dt, 3), "unit": "layer-steps/s", "us_per_layer_step": round(dt / K * 1e6, 2),
+    return {**extra, "value": round(world * K / dt_max, 3), "unit": "layer-steps/s",
+            "us_per_layer_step": round(dt_max / K * 1e6, 2),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": G * R * 128 * 2,
+            "ranks": world,
             "api": "TwilightMatchedBudgetOffloadedCache.decode_layer (one library call per layer-step)",
+            "timing": "host wall clock over K steps, every rank at once after a barrier; the "
+                      "slowest rank's time; value = ranks x K / that time",
             "note": "K/V history stays in the pinned host slab and is read over the host link inside the step"}
 
 
 # ------------------------------------------------------- CPU baseline arm ---
 
-def cpu_layer_step(layer, q16, prep, gather_fn) -> torch.Tensor:
-    """The reference's CPU path for one layer-step (oracle/torch_ref.py = the
-    reference's torch operator sequence): selection, flat-row gather, attention."""
+def cpu_layer_step(layer, q16, prep, gather_fn):
+    """The port of the reference's CPU path for one layer-step (oracle/torch_ref.py
+    = the reference's torch operator sequence, with group-wise INT4 as the GPU
+    arm): selection, flat-row gather, attention.  -> (out [G,R,D] fp32, selection)."""
     from oracle import torch_ref
 
     G, R = CFG["groups"], CFG["heads"]
@@ -665,7 +749,7 @@ def cpu_layer_step(layer, q16, prep, gather_fn) -> torch.Tensor:
         vv = torch.cat((v[off:off + n], layer.value_new[g:g + 1]))
         outs.append(torch_ref.sdpa_decode_attention(q16[g], kk, vv))
         off += n
-    return torch.stack(outs)
+    return torch.stack(outs), sel
 
 
 def cpu_prepare(layer):
@@ -720,41 +804,127 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
+class CpuPath:
+    """The CPU path the baseline times: the reference's own code when its
+    package is present (oracle/ref_harness.py: prepare_layer_selection with the
+    reference's per-token INT4 codes, its only mode; the flat-row gather; its
+    SDPA-math attention per KV group), else the port (oracle/torch_ref.py with
+    the GPU arm's group-32 codes)."""
+
+    def __init__(self, layer) -> None:
+        from oracle import ref_harness
+
+        torch.set_num_threads(host_threads())
+        self.layer = layer
+        self.gather_fn, self.gather_name = make_gather(layer)
+        self.kind = "port"
+        self.ref = None
+        if ref_harness.reference_package_dir() is not None:
+            try:
+                self.ref = ref_harness.ReferenceLayerStep(
+                    layer.keys, layer.values, heads=CFG["heads"], sink=CFG["sink"],
+                    recent=CFG["recent"], block=CFG["block"], b0_tokens=CFG["b0_tokens"],
+                    top_p=CFG["top_p"])
+                self.kind = "reference"
+            except Exception as exc:  # the package is there but does not run here
+                self.ref_error = f"{type(exc).__name__}: {exc}"
+        if self.ref is None:
+            self.prep = cpu_prepare(layer)
+
+    def step(self, q16):
+        if self.ref is not None:
+            return self.ref.step(q16, self.layer.key_new, self.layer.value_new, self.gather_fn)
+        return cpu_layer_step(self.layer, q16, self.prep, self.gather_fn)
+
+    def describe(self) -> str:
+        if self.ref is not None:
+            return ("the reference's own TwilightMatchedBudgetOffloadedCache.prepare_layer_selection "
+                    "(hi/twilight_offload_cache.py:996; device cpu, pytorch QK backend, per-token "
+                    "INT4 scale: the reference has no group-wise mode) + " + self.gather_name
+                    + " + its sdpa_math_decode_attention per KV group")
+        return ("oracle/torch_ref.py (the reference's torch ops, INT4 g32) + " + self.gather_name
+                + " + SDPA decode attention per KV group")
+
+
 def cpu_baseline(layer, queries, budget_s: float = 15.0, max_steps: int = 40) -> dict:
-    torch.set_num_threads(host_threads())
-    prep = cpu_prepare(layer)
-    gather_fn, gname = make_gather(layer)
-    cpu_layer_step(layer, queries[0], prep, gather_fn)  # warm-up
+    path = CpuPath(layer)
+    path.step(queries[0])  # warm-up
     times = []
     t_end = time.perf_counter() + budget_s
     i = 0
     while (time.perf_counter() < t_end and i < max_steps) or i < 3:
         t0 = time.perf_counter()
-        cpu_layer_step(layer, queries[i % len(queries)], prep, gather_fn)
+        path.step(queries[i % len(queries)])
         times.append(time.perf_counter() - t0)
         i += 1
     med = statistics.median(times)
     return {"value": round(1.0 / med, 4), "unit": "layer-steps/s", "cores": torch.get_num_threads(),
-            "kind": "port", "us_per_layer_step": round(med * 1e6, 1),
-            "sample": f"{len(times)} cfg2 layer-steps (median), oracle/torch_ref.py selection + "
-                      f"{gname} + SDPA decode attention per KV group"}
+            "kind": path.kind, "us_per_layer_step": round(med * 1e6, 1),
+            "sample": f"{len(times)} cfg2 layer-steps (median): {path.describe()}"}
+
+
+def parity_check(layer, gpu: dict) -> dict:
+    """The GPU arm's first timed step against the port of the reference's CPU
+    sequence on the same layer and query (group-32 INT4 as the GPU arm;
+    oracle/torch_ref.py is pinned bit for bit to the reference's own
+    prepare_layer_selection on the golden cases):
+
+    * unions_equal / head_counts_equal: the GPU's sorted unions and per-head
+      top-p counts against the port's;
+    * counts_within_tie_rule: every GPU count inside the window of counts whose
+      cumulative softmax mass crosses p within the fp32 cumsum error n 2^-24;
+    * max_abs_err: the GPU's fp16 output against float64 attention over the
+      GPU's own union + current token (tolerance 2e-2, 16-bit output), and
+      max_abs_err_vs_port against the port's own output."""
+    from oracle import torch_ref
+
+    sys.path.insert(0, str(REPO / "tests"))
+    from tolerance import ATTN_TOL_16BIT, count_window
+
+    G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
+    q = gpu["q"]
+    prep = cpu_prepare(layer)
+    gather_fn, _ = make_gather(layer)
+    out_port, sel = cpu_layer_step(layer, q, prep, gather_fn)
+    unions_equal = True
+    err = 0.0
+    for g in range(G):
+        n = int(gpu["union_count"][g])
+        u = gpu["union_pos"][g, :n].long()
+        unions_equal &= bool(torch.equal(u, sel.unions[g].long()))
+        kk = torch.cat((layer.keys[g].index_select(0, u), layer.key_new[g:g + 1]))
+        vv = torch.cat((layer.values[g].index_select(0, u), layer.value_new[g:g + 1]))
+        ref = torch_ref.decode_attention(q[g], kk, vv)
+        err = max(err, (gpu["out"][g].double() - ref).abs().max().item())
+    counts_equal = bool(torch.equal(gpu["head_count"].long(), sel.desired.long()))
+    in_window = True
+    for g in range(G):
+        for r in range(R):
+            lo, hi = count_window(sel.logits[g, r].numpy(), CFG["top_p"])
+            in_window &= lo <= int(gpu["head_count"][g, r]) <= hi
+    err_port = (gpu["out"].double() - out_port.double()).abs().max().item() if unions_equal else None
+    ok = (unions_equal or in_window) and err < ATTN_TOL_16BIT
+    return {"ok": bool(ok), "unions_equal": unions_equal, "head_counts_equal": counts_equal,
+            "counts_within_tie_rule": bool(in_window), "max_abs_err": round(err, 6),
+            "max_abs_err_vs_port": None if err_port is None else round(err_port, 6),
+            "tol": ATTN_TOL_16BIT, "checked": "the first timed step (query index warmup+0)",
+            "against": "oracle/torch_ref.py (the reference's fp32 selection sequence, INT4 g32) "
+                       "and float64 attention"}
 
 
 def run_reference(args) -> int:
     world, rank, local = dist_env()
     if rank != 0:
         return 0
-    from oracle import synth  # noqa: F401  (the reference arm executes the oracle port)
+    from oracle import synth  # noqa: F401  (the reference arm runs the reference's CPU code)
 
-    torch.set_num_threads(host_threads())
     layer, queries = build_workload(None, torch.device("cpu"), seed=0, n_queries=args.steps + args.warmup)
-    prep = cpu_prepare(layer)
-    gather_fn, gname = make_gather(layer)
+    path = CpuPath(layer)
     for i in range(args.warmup):
-        cpu_layer_step(layer, queries[i], prep, gather_fn)
+        path.step(queries[i])
     t0 = time.perf_counter()
     for i in range(args.steps):
-        cpu_layer_step(layer, queries[args.warmup + i], prep, gather_fn)
+        path.step(queries[args.warmup + i])
     dt = time.perf_counter() - t0
     value = args.steps / dt
     line = {
@@ -771,17 +941,18 @@ def run_reference(args) -> int:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "fp16 K/V, fp32 math",
-        "data": "synthetic (seeded splitmix64 normals; BASELINE config 2 shapes)",
-        "config": {"workload": "cfg2 (as the GPU arm), all host cores",
-                   "parallelism": "rank 0 only (CPU)"},
+        "dtype": DTYPE_NOTE,
+        "data": DATA_NOTE,
+        "config": cfg2_config(world),
+        "reference_execution": "rank 0 only, on all its host cores (CPU); the other ranks exit",
         "cpu_baseline": {"value": round(value, 4), "unit": "layer-steps/s",
-                         "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{args.steps} cfg2 layer-steps: oracle/torch_ref.py (the "
-                                   f"reference's torch ops on CPU) + {gname} + SDPA attention"},
+                         "cores": torch.get_num_threads(), "kind": path.kind,
+                         "sample": f"{args.steps} cfg2 layer-steps: {path.describe()}"},
         "e2e": {"value": round(value, 4), "unit": "layer-steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if getattr(path, "ref_error", None):
+        line["reference_error"] = path.ref_error
     print(json.dumps(line), flush=True)
     return 0
 
@@ -790,30 +961,31 @@ CFG5 = dict(kv_heads=8, heads=8, length=131072, dtype="bfloat16", b0_tokens=4096
             int4_group=32, layers=2, resident_heads=(0, 1))
 
 
-def run_cfg5(args) -> int:
-    """one 70B-shaped request (8 KV x 8 Q heads per layer, 131072
-    tokens, bf16) sharded by KV head over the ranks; each layer-step = the local
-    sparse layer-step + an NCCL all-gather of the [heads_local, 8, 128] outputs.
-    KV heads 0 and 1 of every layer are GPU-resident (the static choice of "the
-    2 highest-score heads"), the rest are read from pinned host memory.  Inputs
-    are seeded torch.randn on the GPU (K with 4 outlier channels per head)."""
+def init_dist(device, world: int) -> None:
+    """NCCL process group for world > 1 (short timeout: ranks that wait for
+    one another end with an error)."""
     import torch.distributed as dist
     from datetime import timedelta
 
-    world, rank, local = dist_env()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
-    else:
-        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29599", rank=0, world_size=1)
-    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+
+
+def measure_cfg5(tw, device, world: int, rank: int, K: int, W: int, link_peak: float | None) -> dict | None:
+    """Head-sharded long-context decode: one 70B-shaped request (8 KV x 8 Q heads
+    per layer, 131072 tokens, bf16) with its KV heads sharded over the ranks;
+    each layer-step = the local sparse layer-step (decode_layer) + an NCCL
+    all-gather of the [heads_local, 8, 128] outputs (hi/mp.py:276-278 feeds
+    the gathered output to o_proj).  KV heads 0 and 1 of every layer are
+    GPU-resident (the static choice of "the 2 highest-score heads"), the rest
+    are read from pinned host memory.  Inputs are seeded torch.randn on the
+    GPU (K with 4 lognormal outlier channels per head).  Returns rank 0's
+    summary (None on other ranks)."""
     sh = importlib.import_module("twilight-cpu-gpu-offloading_b200.sharding")
     G, R, L = CFG5["kv_heads"], CFG5["heads"], CFG5["length"]
     heads = sh.shard_kv_heads(G, world, rank)
     hl = len(heads)
     layers = CFG5["layers"]
-    K, W = args.steps, args.warmup
     resident = [li * hl + i for li in range(layers) for i, h in enumerate(heads)
                 if h in CFG5["resident_heads"]]
     cache = tw.TwilightMatchedBudgetOffloadedCache(
@@ -843,14 +1015,16 @@ def run_cfg5(args) -> int:
     for i in range(W):
         stepper.step(i % layers, *steps[i], out_local=out_local)
     torch.cuda.synchronize()
-    dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for i in range(K):
-        stepper.step((W + i) % layers, *steps[W + i], out_local=out_local)
-    e.record()
-    torch.cuda.synchronize()
-    total_ms = sh.max_over_ranks(s.elapsed_time(e), device=device if world > 1 else None)
+    if world > 1:
+        torch.distributed.barrier()
+    total_ms = _timed_ms(lambda: [stepper.step((W + i) % layers, *steps[W + i], out_local=out_local)
+                                  for i in range(K)])
+    total_ms = max_over_ranks(total_ms, device, world)
+    # the all-gather alone (same tensors, back to back)
+    if world > 1:
+        torch.distributed.barrier()
+    ag_ms = max_over_ranks(_timed_ms(lambda: [sh.gather_head_outputs(out_local) for _ in range(K)]),
+                           device, world)
     # Union sizes of further steps (outside the timed region): the rows this
     # rank read over the host link (its offloaded heads) and from HBM.
     host_rows = dev_rows = 0
@@ -865,36 +1039,51 @@ def run_cfg5(args) -> int:
             else:
                 host_rows += c
     host_bytes = 512.0 * host_rows / B
-    host_max = sh.max_over_ranks(host_bytes, device=device if world > 1 else None)
-    pinned = pinned_h2d_peak_gbs(device) if rank == 0 else None
-    dist.barrier()
-    if rank == 0:
-        ms = total_ms / K
-        print(json.dumps({
-            "metric": METRIC, "workload": "cfg5", "value": round(K / (total_ms * 1e-3), 3),
-            "unit": "layer-steps/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(ms, 5), "us_per_layer_step": round(ms * 1e3, 2),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16 K/V, fp32 math", "data": "synthetic (seeded torch.randn on the GPU)",
-            "config": {"workload": "cfg5: one request, 8 KV x 8 Q heads, D 128, ctx 131072, bf16, "
-                                   "INT4 g32, B0 4096, top-p 0.95, KV heads 0-1 resident, "
-                                   f"{layers} layers cycled",
-                       "parallelism": f"KV-head sharded over {world} GPU(s) + NCCL all-gather"},
-            "host_link": {
-                "bytes_per_step_rank0": round(host_bytes),
-                "bytes_per_step_max_rank": round(host_max),
-                "union_rows_per_step_rank0": {"offloaded_heads": round(host_rows / B),
-                                              "resident_heads": round(dev_rows / B)},
-                "achieved_gbs_max_rank": round(host_max / (ms * 1e-3) / 1e9, 2),
-                "pinned_h2d_peak_gbs": round(pinned, 2),
-                "frac": round(host_max / (ms * 1e-3) / 1e9 / pinned, 4),
-                "note": "union sizes from 3 further steps; bytes = 512 B per union row of an "
-                        "offloaded head; achieved = the busiest rank's bytes / the max-over-ranks "
-                        "step time"},
-            "gpu_launches": 2 * K * world}), flush=True)
+    host_max = max_over_ranks(host_bytes, device, world)
     cache.synchronize()
     cache.close()
-    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    ms = total_ms / K
+    achieved = host_max / (ms * 1e-3) / 1e9
+    return {
+        "workload": "cfg5: one request, 8 KV x 8 Q heads, D 128, ctx 131072, bf16, INT4 g32, "
+                    f"B0 4096, top-p 0.95, KV heads 0-1 resident, {layers} layers cycled",
+        "parallelism": f"KV-head sharded over {world} GPU(s) ({hl} KV heads each) + NCCL all-gather",
+        "scaling": "strong", "steps": K, "warmup": W,
+        "value": round(K / (total_ms * 1e-3), 3), "unit": "layer-steps/s",
+        "us_per_layer_step": round(ms * 1e3, 2),
+        "all_gather_us": round(ag_ms / K * 1e3, 2) if world > 1 else 0.0,
+        "all_gather_note": "NCCL all_gather_into_tensor of the [heads_local, 8, 128] bf16 outputs "
+                           "alone, back to back, max over ranks",
+        "host_link": {
+            "bytes_per_step_rank0": round(host_bytes),
+            "bytes_per_step_max_rank": round(host_max),
+            "union_rows_per_step_rank0": {"offloaded_heads": round(host_rows / B),
+                                          "resident_heads": round(dev_rows / B)},
+            "achieved_gbs_max_rank": round(achieved, 2),
+            "peak_gbs": None if link_peak is None else round(link_peak, 2),
+            "frac": None if not link_peak else round(achieved / link_peak, 4),
+            "note": "union sizes from 3 further steps; bytes = 512 B per union row of an "
+                    "offloaded head; achieved = the busiest rank's bytes / the max-over-ranks "
+                    "step time; peak = the per-rank host-link copy peak with all ranks at once"},
+        "gpu_launches": 2 * K * world,
+    }
+
+
+def run_cfg5(args) -> int:
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    init_dist(device, world)
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    res = measure_cfg5(tw, device, world, rank, args.steps, args.warmup, None)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "n_gpus": world, "higher_is_better": True,
+                          "vs_baseline": None, "dtype": "bf16 K/V, fp32 math",
+                          "data": "synthetic (seeded torch.randn on the GPU)", **res}), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
     return 0
 
 
@@ -903,29 +1092,20 @@ CFG4 = dict(requests=16, per_gpu=2, kv_heads=8, heads=4, ctx_lo=8192, ctx_hi=131
 
 
 def cfg4_contexts() -> list[int]:
-    """The 16 request contexts of config 4: seeded U[8192, 131072], rounded down
-    to a multiple of 16."""
+    """The 16 request contexts of the batched workload: seeded U[8192, 131072],
+    rounded down to a multiple of 16."""
     g = torch.Generator().manual_seed(4)
     raw = torch.randint(CFG4["ctx_lo"], CFG4["ctx_hi"] + 1, (CFG4["requests"],), generator=g)
     return [int(x) // 16 * 16 for x in raw]
 
 
-def run_cfg4(args) -> int:
-    """batched multi-request decode sharded by request.  Rank
-    r serves requests 2r and 2r+1 of the 16 (weak scaling: N = 8 covers all 16),
-    each request one layer of 8 KV x 4 Q heads over its own pinned slab; a step
-    runs one sparse layer-step (decode_layer) per request.  bf16 K/V ~ N(0,1)
-    with 8 needle rows (x4) per head at seeded random positions."""
-    import torch.distributed as dist
-    from datetime import timedelta
-
-    world, rank, local = dist_env()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
-    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
-    K, W = args.steps, args.warmup
+def measure_cfg4(tw, device, world: int, rank: int, K: int, W: int, numa=None) -> dict | None:
+    """Batched multi-request decode sharded by request: rank r serves requests
+    2r and 2r+1 of the 16 (weak scaling: 8 ranks cover all 16), each request
+    one layer of 8 KV x 4 Q heads over its own pinned slab; a step runs one
+    sparse layer-step (decode_layer) per request.  bf16 K/V ~ N(0,1) with 8
+    needle rows (x4) per head at seeded random positions.  Returns rank 0's
+    summary (None on other ranks)."""
     G, R = CFG4["kv_heads"], CFG4["heads"]
     ctxs = cfg4_contexts()
     mine = [(2 * rank + i) % CFG4["requests"] for i in range(CFG4["per_gpu"])]
@@ -938,7 +1118,7 @@ def run_cfg4(args) -> int:
             num_query_heads_per_kv=R, dtype=torch.bfloat16, device=device,
             candidate_token_budget=CFG4["b0_tokens"], top_p=CFG4["top_p"], budget_mode="dynamic",
             layer_batched_selection=True, gqa_groupwise_execution=True, qk_backend="cuda",
-            int4_group_size=CFG4["int4_group"], host_numa_node=args.numa)
+            int4_group_size=CFG4["int4_group"], host_numa_node=numa)
         for h in range(G):
             gh = torch.Generator(device=device).manual_seed(1_000 * req + h)
             k = torch.randn(L, 128, generator=gh, device=device)
@@ -954,50 +1134,67 @@ def run_cfg4(args) -> int:
                       for _ in range(K + W)])
     outs = [torch.empty((G, R, 128), dtype=torch.bfloat16, device=device) for _ in caches]
     entries = list(range(G))
-    torch.cuda.synchronize()
-    for i in range(W):
+
+    def one(i):
         for c, st, o in zip(caches, steps, outs):
             c.decode_layer(queries=st[i][0], key_states=st[i][1], value_states=st[i][2],
                            entries=entries, out=o)
+
+    torch.cuda.synchronize()
+    for i in range(W):
+        one(i)
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for i in range(K):
-        for c, st, o in zip(caches, steps, outs):
-            c.decode_layer(queries=st[W + i][0], key_states=st[W + i][1], value_states=st[W + i][2],
-                           entries=entries, out=o)
-    e.record()
-    torch.cuda.synchronize()
-    total_ms = s.elapsed_time(e)
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-        dist.barrier()
+        torch.distributed.barrier()
+    total_ms = max_over_ranks(_timed_ms(lambda: [one(W + i) for i in range(K)]), device, world)
     for c in caches:
         c.synchronize()
-    if rank == 0:
-        n_steps = K * len(mine) * world
-        print(json.dumps({
-            "metric": METRIC, "workload": "cfg4", "value": round(n_steps / (total_ms * 1e-3), 3),
-            "unit": "layer-steps/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(total_ms / K, 5),
-            "us_per_layer_step": round(total_ms / K / len(mine) * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16 K/V, fp32 math", "data": "synthetic (seeded torch.randn on the GPU, needles)",
-            "config": {"workload": "cfg4: 2 requests per GPU of 16, ctx U[8192,131072] (seeded) "
-                                   "rounded to 16, 8 KV x 4 Q heads, bf16, INT4 g32, B0 2048, "
-                                   "top-p 0.9, one layer-step per request per step",
-                       "contexts_rank0": [ctxs[r] for r in mine],
-                       "parallelism": f"request-sharded over {world} GPU(s), no collective"},
-            "gpu_launches": 2 * n_steps}), flush=True)
-    for c in caches:
         c.close()
+    if rank != 0:
+        return None
+    n_steps = K * len(mine) * world
+    return {
+        "workload": "cfg4: 2 requests per GPU of 16, ctx U[8192,131072] (seeded) rounded to 16, "
+                    "8 KV x 4 Q heads, bf16, INT4 g32, B0 2048, top-p 0.9, one layer-step per "
+                    "request per step",
+        "parallelism": f"request-sharded over {world} GPU(s), no collective",
+        "scaling": "weak", "steps": K, "warmup": W,
+        "contexts_rank0": [ctxs[r] for r in mine],
+        "value": round(n_steps / (total_ms * 1e-3), 3), "unit": "layer-steps/s",
+        "ms_per_step": round(total_ms / K, 5),
+        "us_per_layer_step": round(total_ms / K / len(mine) * 1e3, 2),
+        "gpu_launches": 2 * n_steps,
+    }
+
+
+def run_cfg4(args) -> int:
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    init_dist(device, world)
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    res = measure_cfg4(tw, device, world, rank, args.steps, args.warmup, args.numa)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "n_gpus": world, "higher_is_better": True,
+                          "vs_baseline": None, "dtype": "bf16 K/V, fp32 math",
+                          "data": "synthetic (seeded torch.randn on the GPU, needles)", **res}),
+              flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        torch.distributed.destroy_process_group()
     return 0
+
+
+def run_sharded(args, tw, device, world: int, rank: int, link_peak: float | None = None) -> dict:
+    """The two sharded workloads beside the headline line: cfg5 (one request,
+    KV heads sharded over the ranks, NCCL all-gather per layer) and cfg4
+    (16 requests, 2 per rank, no collective).  Rank 0 gets their summaries."""
+    K, W = min(args.steps, 20), args.warmup
+    out = {}
+    c5 = measure_cfg5(tw, device, world, rank, K, W, link_peak)
+    c4 = measure_cfg4(tw, device, world, rank, K, W, args.numa)
+    if rank == 0:
+        out = {"cfg5": c5, "cfg4": c4}
+    return out
 
 
 CFG3 = dict(layers=32, hidden=4096, heads=32, kv_heads=8, intermediate=14336, vocab=128256,
@@ -1014,7 +1211,7 @@ CFG_REF3B = dict(layers=28, hidden=3072, heads=24, kv_heads=8, intermediate=8192
 
 
 class Llama8BDecoder:
-    """a Llama-3-8B-shaped decoder (32 layers, 32 / 8 heads, D 128,
+    """cfg3, head-wise offloaded full-model decode: a Llama-3-8B-shaped decoder (32 layers, 32 / 8 heads, D 128,
     hidden 4096, MLP 14336, vocab 128256) with random-init bf16 weights, decoding
     one token per step through the sparse path: RMSNorm, tw_qkv_rope (q / k / v
     projection + RoPE), TwilightMatchedBudgetOffloadedCache.decode_layer (Quest +
@@ -1110,7 +1307,7 @@ class Llama8BDecoder:
 
 
 def run_cfg3(args) -> int:
-    """Full-model decode TPOT on one GPU, timed as the
+    """Full-model decode TPOT (cfg3: Llama-3-8B shape, 25 % of KV heads resident) on one GPU, timed as the
     reference times it (scripts/run_ruler_partial_h2d_tpot_case_v1.py:1303-1323):
     decode step D1 is the warm-up, then a synchronized wall over D2..D32."""
     _, rank, local = dist_env()
@@ -1228,6 +1425,9 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the cfg5 (head-sharded) and cfg4 (request-sharded batch) sub-runs "
+                         "of the default workload")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5", "ref3b"], default="cfg2",
                     help="cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
                          "decode, TPOT), cfg4 (request-sharded batch of 16 requests), cfg5 "

@@ -439,7 +439,10 @@ int tw_qkv_rope(const void* hidden, const void* w_q, const void* w_k, const void
  *     A call with max_seqlen_k <= 128 uses no scratch.
  *   - Set-up: the first call on each device looks up the array's device
  *     address (cudaGetSymbolAddress) with that device current; make that
- *     first call before any stream capture.
+ *     first call before any stream capture.  Only a successful lookup is
+ *     kept: if it fails the call returns TW_ERR_CUDA and the next call on
+ *     that device tries again.  Device ordinals 0..63 are served; a higher
+ *     ordinal returns TW_ERR_UNSUPPORTED.
  *   - Sharing: every call on a device uses the same array, which keeps the
  *     last call's contents (the call clears the counters it needs).  Calls
  *     whose executions overlap on the GPU (e.g. on two streams at once) race

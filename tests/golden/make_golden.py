@@ -1,7 +1,9 @@
 """Generate golden vectors from the reference itself (run in a container that
 holds the reference tree; the GPU box does not need it).
 
-    python tests/golden/make_golden.py [--reference /path/to/reference]
+    python tests/golden/make_golden.py --reference /path/to/reference-checkout
+
+(or with $TW_REFERENCE_ROOT set to the checkout).
 
 It imports the reference's own modules (source/headinfer/headinfer/), builds a
 TwilightMatchedBudgetOffloadedCache / QuestTopKOffloadedCache on device='cpu'
@@ -16,8 +18,8 @@ from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import sys
-from collections import defaultdict
 from pathlib import Path
 
 import numpy as np
@@ -28,6 +30,7 @@ REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
 
 from oracle import synth  # noqa: E402
+from oracle.ref_harness import make_ref_cache, make_twilight_cache  # noqa: E402
 
 CASES = {
     # Twilight (Quest B0 -> INT4 per-token QK -> top-p -> GQA union), outliers.
@@ -53,60 +56,15 @@ def sha(t: torch.Tensor) -> str:
     return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
 
 
-def make_ref_cache(mod, cls_name: str, *, entries: int, max_len: int, heads: int, dtype, sink: int,
-                   recent: int, block: int, **extra):
-    from headinfer.slab_cache import SequentialCacheState, SlabGeometry
-
-    cls = getattr(mod, cls_name)
-    c = cls.__new__(cls)
-    c.geometry = SlabGeometry(num_entries=entries, batch_size=1, max_cache_len=max_len, head_dim=128)
-    c.dtype = dtype
-    c.device = torch.device("cpu")
-    c.allocated_capacity = max_len
-    c.num_query_heads_per_kv = heads
-    c.sink_tokens = sink
-    c.recent_tokens = recent
-    c.block_size = block
-    c.selection_interval = 1
-    c.layer_batched_selection = True
-    c._bookkeeping = SequentialCacheState(entries, max_len)
-    c._logical_lengths = c._bookkeeping.logical_lengths
-    c._page_min = [None] * entries
-    c._page_max = [None] * entries
-    c._prompt_length = None
-    c._cached_selected_pages = [None] * entries
-    c._layer_prepared_entries = set()
-    c._capture_selection_trace = False
-    c._selection_trace = []
-    c.metrics_enabled = False
-    c.metrics = defaultdict(float)
-    c._timing_events = []
-    for k, v in extra.items():
-        setattr(c, k, v)
-    return c
-
-
 def twilight_case(ref_twilight, ref_root, name, cfg):
     G, R, L = cfg["groups"], cfg["heads"], cfg["length"]
     tdt = synth.TORCH_DTYPES[cfg["dtype"]]
     layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=cfg["dtype"],
                              seed=cfg["seed"], workload=cfg["workload"], sink=cfg["sink"],
                              recent=cfg["recent"], block=cfg["block"], n_needles=cfg["n_needles"])
-    c = make_ref_cache(
-        ref_twilight, "TwilightMatchedBudgetOffloadedCache", entries=G, max_len=L + 8, heads=R,
-        dtype=tdt, sink=cfg["sink"], recent=cfg["recent"], block=cfg["block"],
-        candidate_token_budget=cfg["b0_tokens"], top_p=cfg["top_p"], matched_budget_fraction=0.05,
-        budget_mode="dynamic", gqa_groupwise_execution=True, detailed_selection_profile=False,
-        qk_backend="pytorch", exact_scan_graph=False, exact_top_p_graph=False,
-        fused_quest_score=False, reuse_quant_metadata=False, _layer_quant_metadata={},
-        fused_final_indices=False, gpu_compact_gqa_union=True, gpu_union_validate_cpu=False,
-        cpu_bitmap_union=False, post_selection_pipeline=False, resident_zero_copy=False,
-        resident_precompute_gpu_mapping=False, _resident_zero_copy_placeholder_active=False,
-        _capture_budget_trace=True, _budget_trace=[],
-        _quant_key_packed=[None] * G, _quant_key_scale=[None] * G, _quant_key_minimum=[None] * G,
-        _cached_twilight_positions=[None] * G, _cached_twilight_group_positions=[None] * G,
-        _cached_twilight_per_q_lengths=[None] * G, _gpu_group_membership=None,
-        _post_selection_pending={}, _post_selection_host_starts={})
+    c = make_twilight_cache(ref_twilight, groups=G, heads=R, max_len=L + 8, dtype=tdt,
+                            sink=cfg["sink"], recent=cfg["recent"], block=cfg["block"],
+                            b0_tokens=cfg["b0_tokens"], top_p=cfg["top_p"], budget_trace=True)
     c._capture_selection_trace = True
     c._prompt_length = L
     for e in range(G):
@@ -234,8 +192,11 @@ def int4_group32_case(ref_twilight):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TW_REFERENCE_ROOT"),
+                    help="the reference checkout (holds source/headinfer/headinfer/)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or $TW_REFERENCE_ROOT) is required")
     sys.path.insert(0, str(Path(args.reference) / "source" / "headinfer"))
     torch.set_num_threads(1)
     from headinfer import quest_offload_cache, twilight_offload_cache

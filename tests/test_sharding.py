@@ -66,3 +66,16 @@ def test_shard_ranges(tw):
             assert max(map(len, parts)) - min(map(len, parts)) <= 1
     with pytest.raises(ValueError):
         sh.shard_kv_heads(8, 3, 0)
+
+
+def test_gather_head_outputs_without_process_group():
+    """A single process with no process group owns every KV head: the
+    all-gather is the identity (HeadShardedLayerStep then runs unsharded)."""
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised")
+    sys.path.insert(0, str(REPO))
+    sh = importlib.import_module("twilight-cpu-gpu-offloading_b200.sharding")
+    local = torch.arange(24, dtype=torch.float32).view(2, 3, 4)
+    assert sh.gather_head_outputs(local) is local

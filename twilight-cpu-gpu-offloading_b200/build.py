@@ -12,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -48,13 +49,31 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles every source to an object in parallel (one nvcc per file),
+    then links the shared library."""
     if not force and not needs_build():
         return LIB
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, *map(str, sources()), "-o", str(tmp)]
+    obj_dir = PKG / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    jobs = []
+    for src in sources():
+        obj = obj_dir / (src.stem + ".o")
+        jobs.append((obj, [nvcc(), *compile_flags, "-c", str(src), "-o", str(obj)]))
     if verbose:
-        print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
+        for _, cmd in jobs:
+            print(" ".join(cmd))
+    workers = max(1, min(len(jobs), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        results = list(pool.map(lambda j: subprocess.run(j[1]).returncode, jobs))
+    if any(results):
+        raise RuntimeError(f"nvcc failed for {[str(j[0].name) for j, r in zip(jobs, results) if r]}")
+    tmp = LIB.with_suffix(".so.tmp")
+    link = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
+            *[str(o) for o, _ in jobs], "-o", str(tmp)]
+    if verbose:
+        print(" ".join(link))
+    subprocess.run(link, check=True)
     tmp.replace(LIB)
     return LIB
 

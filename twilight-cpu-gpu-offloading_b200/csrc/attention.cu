@@ -650,12 +650,13 @@ extern "C" int tw_attend_union(const void* slab_k, const void* slab_v,
 static __device__ __align__(256) unsigned char g_noalloc_scratch[TW_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kNoAllocMaxDevices = 64;
-std::once_flag g_noalloc_once[kNoAllocMaxDevices];
-void* g_noalloc_ptr[kNoAllocMaxDevices];
-cudaError_t g_noalloc_err[kNoAllocMaxDevices];
+constexpr int kNoAllocMaxDevices = 64;  // device ordinals 0..63 (TW_ERR_UNSUPPORTED beyond)
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices];  // null until a lookup on that device succeeds
 
-// Device address of this device's scratch array (set up on first use).
+// Device address of this device's scratch array.  Only a successful lookup
+// is kept: a failed one (e.g. a first call made during stream capture)
+// returns TW_ERR_CUDA and the next call tries again.
 int noalloc_scratch(void** ptr) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -664,14 +665,15 @@ int noalloc_scratch(void** ptr) {
     return TW_ERR_CUDA;
   }
   if (dev < 0 || dev >= kNoAllocMaxDevices) return TW_ERR_UNSUPPORTED;
-  std::call_once(g_noalloc_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
-    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || !p) {
+      set_last_cuda_error(err != cudaSuccess ? err : cudaErrorInvalidSymbol);
+      return TW_ERR_CUDA;
+    }
     g_noalloc_ptr[dev] = p;
-  });
-  if (g_noalloc_err[dev] != cudaSuccess) {
-    set_last_cuda_error(g_noalloc_err[dev]);
-    return TW_ERR_CUDA;
   }
   *ptr = g_noalloc_ptr[dev];
   return TW_OK;

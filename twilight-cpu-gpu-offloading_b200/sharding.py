@@ -44,7 +44,7 @@ def shard_kv_heads(kv_heads: int, world: int, rank: int) -> range:
 def gather_head_outputs(local: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather [G_local, R, D] attention outputs into [G, R, D] (rank order =
     KV-head order).  Runs on the tensors' device: NCCL on CUDA, gloo on CPU."""
-    world = dist.get_world_size(group)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
         return local
     out = torch.empty((world * local.shape[0], *local.shape[1:]), dtype=local.dtype,
@@ -63,7 +63,8 @@ def max_over_ranks(value: float, device: torch.device | None = None, group=None)
 
 class HeadShardedLayerStep:
     """Decode layer-steps of one request whose KV heads are sharded over the
-    ranks of a process group (one KV-head group per GPU).
+    ranks of a process group (e.g. a 70B layer at 131072 tokens with one KV-head
+    group per GPU).
 
     Each rank owns `cache`, a TwilightMatchedBudgetOffloadedCache holding only
     its KV heads (entries = layer * heads_local + i).  `step` runs the local
@@ -76,8 +77,9 @@ class HeadShardedLayerStep:
     def __init__(self, cache, kv_heads: int, group=None) -> None:
         self.cache = cache
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        # without a process group the one process owns every KV head
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.heads = shard_kv_heads(kv_heads, self.world, self.rank)
         self.heads_local = len(self.heads)
         if cache.geometry.num_entries % self.heads_local:
