@@ -12,8 +12,9 @@ head scaled by exp(N(0,1)), INT4 group 32, Quest B0 4096 tokens (256 pages of
 is one layer-step; each timed step uses a fresh query, and L2 is flushed
 (512 MiB write) before every timed step, outside its CUDA events.
 
-With N > 1 (torchrun) every rank runs its own request (its own slab on its
-own GPU): request sharding, no collective on the data path; the timed region
+With N > 1 (torchrun) every rank runs its own copy of the request (its own
+slab on its own GPU, the same seeded data): request sharding, no collective
+on the data path; the timed region
 is bracketed by barriers and the max over ranks is reported.  The host-link
 peaks and the public-API (e2e) leg run on every rank at once.  The same line
 carries two sharded sub-runs: "cfg5" (one 70B-shaped request at 131072
@@ -256,7 +257,7 @@ class DeviceStep:
         self.head_count = torch.zeros((G, R), dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         ws = tw.ops.select_layer_workspace_bytes(G, R, self.cand_pages, self.b0, block)
-        self.ws = torch.empty(ws, dtype=torch.uint8, device=device)
+        self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)  # zero before the first call
         self.flat_k = torch.empty((self.rows_cap, 128), dtype=torch.float16, device=device)
         self.flat_v = torch.empty_like(self.flat_k)
         self.cu = torch.zeros(G + 1, dtype=torch.int32, device=device)
@@ -433,7 +434,10 @@ def run_ours(args) -> int:
     K, W = args.steps, args.warmup
     rho = args.reuse_rho if args.reuse else 0.0
     B = min(K, 10)  # extra steps with per-stage events (kept out of the timed steps)
-    layer, queries = build_workload(tw, device, seed=rank, n_queries=K + W + B, rho=rho)
+    # Every rank serves a replica of the same seeded request (seed 0, the 1-GPU
+    # workload), so per-rank work is constant as N grows (weak scaling); the
+    # cfg4 sub-run covers requests of different sizes.
+    layer, queries = build_workload(tw, device, seed=0, n_queries=K + W + B, rho=rho)
     step = DeviceStep(tw, layer, device, fused=not args.staged, reuse=args.reuse,
                       n_steps=K + W + B + 1, numa=args.numa)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)

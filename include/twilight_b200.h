@@ -172,7 +172,11 @@ int tw_top_p_union(const float* logits, const int32_t* pages,
  * Quest score -> top-k pages -> INT4 QK -> top-p + union in one call (4 launches).
  * Replaces TwilightMatchedBudgetOffloadedCache.prepare_layer_selection
  * (hi/twilight_offload_cache.py:996-1843, gpu_compact_gqa_union path).
- * workspace: >= tw_select_layer_workspace_size(...) bytes of device memory.
+ * workspace: >= tw_select_layer_workspace_size(...) bytes of device memory,
+ * zero-filled once before its first use: its last bytes hold the fused
+ * selection's union merge state (a per-group count and candidate bitmap),
+ * which every call leaves zero again.  Calls sharing one workspace must not
+ * overlap on the GPU.
  * pages_out: [G][R][b0] int32 (the Quest B0 pages, ascending). */
 size_t tw_select_layer_workspace_size(int groups, int heads_per_group, int n_pages, int b0_pages,
                                       int block_size);
@@ -330,11 +334,14 @@ int tw_attend_union(const void* slab_k, const void* slab_v, const uint64_t* entr
  * One decode layer-step of the Twilight GQA path in one call: Quest score ->
  * top-k pages -> INT4 QK -> top-p + union -> fused union gather + attention ->
  * new-token append, with no host synchronisation.  When the fused selection
- * serves the shape this is 2 launches on `stream`: the selection, whose extra
- * cluster also appends the new token (position old_length, which neither the
- * selection nor the attention of this step reads) and stages the protected
- * rows, then the fused attention.  Otherwise the per-stage kernels, the
- * attention and the append kernel run (6 launches).
+ * serves the shape this is 2 launches on `stream`: the selection (one
+ * thread-block cluster per query-head row), whose CTAs also append the new
+ * token (position old_length, which neither the selection nor the attention
+ * of this step reads) and stage the protected rows, then the fused
+ * attention.  Otherwise the per-stage kernels, the attention and the append
+ * kernel run (6 launches).  select_workspace: >=
+ * tw_select_layer_workspace_size(...) bytes, zero-filled once before its
+ * first use (see tw_select_layer).
  * Replaces prepare_layer_selection + update_layer_gqa_group_ragged + the
  * FlashAttention call of one layer (hi/twilight_offload_cache.py:996-1843,
  * :2610-3602, hi/mp.py:233-279).  Cache pointers (slab, page min/max, INT4
@@ -389,8 +396,8 @@ typedef struct tw_decode_layer_args {
   const tw_row_reuse* reuse; /* NULL: no row reuse */
   /* Protected-row staging (stage_k NULL: off; ignored when reuse is set).
    * Each group's sink rows [0, sink_end) and recent rows [recent_start,
-   * old_length) do not depend on the selection: one more cluster of the
-   * selection launch copies them from the slab into stage_k / stage_v
+   * old_length) do not depend on the selection: the selection launch's CTAs
+   * copy them (TMA bulk copies started at launch) from the slab into stage_k / stage_v
    * [G][stage_rows][D] (device memory, 16-byte aligned) while the selection
    * runs, and the attention reads them from there, so the host link carries
    * them while it would otherwise idle.  stage_rows >= sink_end +

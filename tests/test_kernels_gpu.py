@@ -431,14 +431,14 @@ def test_attend_union_matches_gather_then_attention(tw, cuda, dtype, R):
 
 @pytest.mark.parametrize("R,L,budget", [(1, 3007, 768), (2, 3014, 768), (3, 3021, 768),
                                          (4, 3028, 768), (5, 3035, 768), (6, 3042, 768),
-                                         (8, 3056, 768), (8, 131072, 4096)])
+                                         (7, 3049, 768), (8, 3056, 768), (8, 131072, 4096)])
 @pytest.mark.parametrize("dtype,group", [("float16", 32), ("bfloat16", 128), ("bfloat16", 64)])
 def test_select_layer_fused_equals_stages(tw, cuda, R, L, budget, dtype, group):
-    """tw_select_layer (one cluster launch per layer for R in 1, 2, 3, 4, 6, 8,
-    clusters of 8 CTAs, or 6 for R = 3 and 6) gives the per-stage kernels'
-    pages, per-head counts and positions and the union, bit for bit; R = 5
-    exercises the per-stage fallback, 131072 tokens with B0 4096 the config-5
-    shape."""
+    """tw_select_layer (one launch: a thread-block cluster per query-head row,
+    the GQA union merged by the group's last row cluster) gives the per-stage
+    kernels' pages, per-head counts and positions and the union, bit for bit,
+    for every R <= 8; 131072 tokens with B0 4096 is the long-context
+    head-sharded shape."""
     G, sink, recent, block = 3 if L < 100000 else 2, 64, 256, 16
     layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype=dtype, seed=70 + R,
                              workload="needles" if R % 2 else "outliers", sink=sink,
@@ -484,3 +484,60 @@ def test_select_layer_fused_equals_stages(tw, cuda, R, L, budget, dtype, group):
     assert torch.equal(hc0, hc1)
     assert torch.equal(up0, up1)
     assert torch.equal(hp0, hp1)
+
+
+def test_select_layer_reuses_its_workspace(tw, cuda):
+    """Consecutive tw_select_layer calls on one zero-filled workspace give the
+    same result (the fused selection's union merge state at the workspace's
+    end is left zero by every call), also after a call of another layer shape
+    (fewer candidate pages) on the same buffer."""
+    import ctypes
+
+    G, R, L, sink, recent, block = 4, 4, 8192, 64, 256, 16
+    layer = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype="float16", seed=91,
+                             workload="outliers")
+    keys = layer.keys.to(cuda)
+    cap = (L - sink) // block + 1
+    pmin = torch.zeros((G, cap, 128), dtype=keys.dtype, device=cuda)
+    pmax = torch.zeros_like(pmin)
+    P_built = tw.ops.quest_page_metadata(keys, sink=sink, block_size=block, page_min=pmin,
+                                         page_max=pmax)
+    packed = torch.zeros((G, L, 64), dtype=torch.uint8, device=cuda)
+    scale = torch.zeros((G, L, 4), dtype=keys.dtype, device=cuda)
+    minimum = torch.zeros_like(scale)
+    tw.ops.int4_pack(keys, group_size=32, packed=packed, scale=scale, minimum=minimum)
+    q = layer.queries.float().to(cuda)
+    lib = tw.load_library()
+    w_full = torch_ref.window(L, sink=sink, recent=recent, block=block, candidate_token_budget=1024,
+                              metadata_pages=P_built)
+    ws_bytes = tw.ops.select_layer_workspace_bytes(G, R, w_full.candidate_pages, w_full.b0_pages, block)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=cuda)
+
+    def run(old_length, budget):
+        w = torch_ref.window(old_length, sink=sink, recent=recent, block=block,
+                             candidate_token_budget=budget, metadata_pages=P_built)
+        pages = torch.zeros((G, R, w.b0_pages), dtype=torch.int32, device=cuda)
+        upos = torch.full((G, L), -1, dtype=torch.int32, device=cuda)
+        ucnt = torch.zeros(G, dtype=torch.int32, device=cuda)
+        hc = torch.zeros((G, R), dtype=torch.int32, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        rc = lib.tw_select_layer(
+            q.data_ptr(), pmin.data_ptr(), pmax.data_ptr(), cap * 128, w.candidate_pages,
+            packed.data_ptr(), scale.data_ptr(), minimum.data_ptr(), L, G, R, w.b0_pages, block,
+            sink, 128, 32, 0, ctypes.c_double(0.95), old_length, w.sink_end, w.recent_start,
+            pages.data_ptr(), upos.data_ptr(), L, ucnt.data_ptr(), hc.data_ptr(), None,
+            err.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        return pages.cpu(), upos.cpu(), ucnt.cpu(), hc.cpu()
+
+    first = run(L, 1024)
+    for _ in range(2):
+        again = run(L, 1024)
+        assert all(torch.equal(a, b) for a, b in zip(first, again))
+    run(L - 3000, 512)  # another shape on the same buffer
+    again = run(L, 1024)
+    assert all(torch.equal(a, b) for a, b in zip(first, again))
+    tail = ws[-4096:].cpu()
+    assert int(tail.count_nonzero()) == 0

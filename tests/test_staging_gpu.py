@@ -105,7 +105,7 @@ class _SlabStep:
         self.head_count = torch.zeros((G, R), dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         ws = tw.ops.select_layer_workspace_bytes(G, R, self.n_pages, self.b0, BLOCK)
-        self.ws = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
         aws = tw.ops.decode_attention_workspace_bytes(G, R, self.per_group)
         self.attn_ws = torch.zeros(aws, dtype=torch.uint8, device=dev)
         self.out = torch.empty((G, R, 128), dtype=torch.float16, device=dev)

@@ -864,7 +864,8 @@ class TwilightMatchedBudgetOffloadedCache(QuestTopKOffloadedCache):
             "union_count": torch.zeros(groups, dtype=torch.int32, device=dev),
             "head_count": torch.zeros((groups, R), dtype=torch.int32, device=dev),
             "head_pos": torch.empty((groups, R, n_cap), dtype=torch.int32, device=dev),
-            "workspace": torch.empty(max(ws, 256), dtype=torch.uint8, device=dev),
+            # zero: the fused selection keeps its union merge state here, left zero
+            "workspace": torch.zeros(max(ws, 256), dtype=torch.uint8, device=dev),
             "attn_workspace": torch.zeros(max(attn_ws, 256), dtype=torch.uint8, device=dev),
             "flat": torch.empty((2, 2, rows_cap, HEAD_DIM), dtype=self.dtype, device=dev),
             "cu": torch.zeros((2, groups + 1), dtype=torch.int32, device=dev),

@@ -39,8 +39,10 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, const ProtectedStage* stage,
-                       const AppendArgs* append, cudaStream_t stream);
+                       int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                       const ProtectedStage* stage, const AppendArgs* append,
+                       cudaStream_t stream);
+size_t merge_region_bytes(int groups, int n_pages, int block);
 int attend_union_impl(const void* slab_k, const void* slab_v, const uint64_t* entry_dirs,
                       int64_t n_entries, int64_t max_len, int first_entry, int groups,
                       int64_t old_length, const int32_t* union_pos, int64_t pos_stride,
@@ -238,14 +240,18 @@ extern "C" int tw_slab_write_rows(const void* src, int64_t src_entry_stride_rows
   return TW_OK;
 }
 
-// Workspace: scores [G*R*P] fp32 | logits [G*R*b0*block] fp32.
+// Workspace: scores [G*R*P] fp32 | logits [G*R*b0*block] fp32 (the per-stage
+// kernels), then the fused selection's union merge region (count u32[G] and
+// candidate bitmap u32[G][ceil(P*block/32)], at the end of the caller's
+// buffer; zero before the first call, left zero by every call).
 extern "C" size_t tw_select_layer_workspace_size(int groups, int heads_per_group, int n_pages,
                                                  int b0_pages, int block_size) {
   if (groups <= 0 || heads_per_group <= 0 || n_pages < 0 || b0_pages < 0 || block_size <= 0)
     return 0;
   const size_t rows = (size_t)groups * heads_per_group;
   return align256(rows * (size_t)n_pages * sizeof(float)) +
-         align256(rows * (size_t)b0_pages * block_size * sizeof(float));
+         align256(rows * (size_t)b0_pages * block_size * sizeof(float)) +
+         merge_region_bytes(groups, n_pages, block_size);
 }
 
 extern "C" int tw_select_layer(const float* q, const void* page_min, const void* page_max,
@@ -268,8 +274,8 @@ extern "C" int tw_select_layer(const float* q, const void* page_min, const void*
                               scale, minimum, entry_stride_tokens, groups, heads_per_group,
                               b0_pages, block_size, sink, group_size, dtype, top_p, old_length,
                               sink_end, recent_start, pages_out, union_pos, pos_stride,
-                              union_count, head_count, head_pos, error_flag, nullptr, nullptr,
-                              (cudaStream_t)stream);
+                              union_count, head_count, head_pos, error_flag, workspace,
+                              workspace_bytes, nullptr, nullptr, (cudaStream_t)stream);
   if (st != TW_ERR_UNSUPPORTED) return st;
   // per-stage kernels (shapes the fused selection does not serve)
   const size_t rows = (size_t)groups * heads_per_group;
@@ -357,9 +363,9 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
     stage.recent_start = a->recent_start;
     stage.old_length = a->old_length;
   }
-  // The new token's append runs in the selection launch's extra cluster: it
-  // writes position old_length, which neither this step's selection nor its
-  // attention reads.
+  // The new token's append runs in the selection launch (one CTA per group):
+  // it writes position old_length, which neither this step's selection nor
+  // its attention reads.
   AppendArgs app{};
   bool fuse_append = false;
   if (a->append) {
@@ -372,13 +378,14 @@ extern "C" int tw_twilight_decode_layer(const tw_decode_layer_args* a, void* str
                            a->first_entry, a->old_length, a->k_new, a->v_new, a->sink,
                            a->block_size, a->page_min, a->page_max, a->page_capacity * kHeadDim,
                            a->packed, a->scale, a->minimum, a->int4_group_size);
-    fuse_append = (int64_t)G * kHeadDim <= 6 * 1024;  // one extra cluster (>= 6 CTAs) covers it
+    fuse_append = true;  // one CTA per group of the selection launch appends
   }
   int rc = select_layer_fused(a->q, a->dtype, pmin, pmax, a->page_capacity * kHeadDim, a->n_pages,
                               packed, scale, minimum, a->max_len, G, R, a->b0_pages, a->block_size,
                               a->sink, a->int4_group_size, a->dtype, a->top_p, a->old_length,
                               a->sink_end, a->recent_start, a->pages, a->union_pos, a->pos_stride,
                               a->union_count, a->head_count, a->head_pos, a->error_flag,
+                              a->select_workspace, a->select_workspace_bytes,
                               staged ? &stage : nullptr, fuse_append ? &app : nullptr, st);
   bool stage_filled = staged;
   if (rc == TW_ERR_UNSUPPORTED) {

@@ -85,6 +85,51 @@ __device__ __forceinline__ void quest_page_score8(const float* __restrict__ q,
   }
 }
 
+// quest_page_score for one head with 4 threads per page.  Thread j (0..3) of
+// the page's 4-thread group holds the partial sums of lanes l = 8j .. 8j+7 of
+// the warp layout above (the same products added in the same order: channels
+// l, l+32, l+64, l+96), combines them as the tree's lane offsets 1, 2 and 4
+// inside the thread, then the lane offsets 8 and 16 as group offsets 1 and 2.
+// Bit-identical to quest_page_score, with 16-byte loads (8 channels).  q: the
+// query row as fp32 [D] in shared memory.  valid = false: no loads, the
+// result is unused.  The result is valid in thread j = 0; all 32 lanes of the
+// warp must call this together (the groups are 4 consecutive lanes).
+template <typename T>
+__device__ __forceinline__ float quest_page_score4(const float* __restrict__ q,
+                                                   const T* __restrict__ gmin,
+                                                   const T* __restrict__ gmax, int64_t p, int j,
+                                                   bool valid) {
+  uint4 lo[4], hi[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    lo[c] = make_uint4(0u, 0u, 0u, 0u);
+    hi[c] = lo[c];
+    if (valid) {
+      lo[c] = *reinterpret_cast<const uint4*>(gmin + p * kHeadDim + 32 * c + 8 * j);
+      hi[c] = *reinterpret_cast<const uint4*>(gmax + p * kHeadDim + 32 * c + 8 * j);
+    }
+  }
+  float part[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[i] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const T* tl = reinterpret_cast<const T*>(&lo[c]);
+    const T* th = reinterpret_cast<const T*>(&hi[c]);
+    const float4 q0 = *reinterpret_cast<const float4*>(q + 32 * c + 8 * j);
+    const float4 q1 = *reinterpret_cast<const float4*>(q + 32 * c + 8 * j + 4);
+    const float qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      part[i] = __fadd_rn(part[i], __fmul_rn(qq[i] > 0.0f ? to_f32(th[i]) : to_f32(tl[i]), qq[i]));
+  }
+  float v = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
+                      __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 4));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 4));
+  return v;
+}
+
 // INT4 estimate of 32 channels of one candidate (lane j of a 4-lane group
 // covers channels 32j .. 32j+31, one uint4 of 16 code bytes): per channel
 // k = code * s + m, the value of the reference's separately rounded mul and
@@ -154,6 +199,35 @@ __device__ __forceinline__ float int4_dot32(const uint4& codes, T s, float m,
     acc[1] = __fmaf_rn(fma_mixed<T>((uint16_t)p3, sb, m), qr[i + 5], acc[1]);
     acc[2] = __fmaf_rn(fma_mixed<T>((uint16_t)(p1 >> 16), sb, m), qr[i + 6], acc[2]);
     acc[3] = __fmaf_rn(fma_mixed<T>((uint16_t)(p3 >> 16), sb, m), qr[i + 7], acc[3]);
+  }
+  return __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+}
+
+// int4_dot32 with the lane's 32 query channels read from shared memory
+// (q: 16-byte aligned) instead of registers; the same operations in the same
+// order, so the same result bit for bit.
+template <typename T>
+__device__ __forceinline__ float int4_dot32_s(const uint4& codes, T s, float m,
+                                              const float* __restrict__ q) {
+  const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+  const uint16_t sb = bits16<T>(s);
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float4 qa = *reinterpret_cast<const float4*>(q + 8 * w);
+    const float4 qb = *reinterpret_cast<const float4*>(q + 8 * w + 4);
+    const uint32_t lo = words[w] & 0x0f0f0f0fu;
+    const uint32_t hi = (words[w] >> 4) & 0x0f0f0f0fu;
+    const uint32_t p0 = code_pair<T>(lo, 0x5140u), p1 = code_pair<T>(lo, 0x5342u);
+    const uint32_t p2 = code_pair<T>(hi, 0x5140u), p3 = code_pair<T>(hi, 0x5342u);
+    acc[0] = __fmaf_rn(fma_mixed<T>((uint16_t)p0, sb, m), qa.x, acc[0]);
+    acc[1] = __fmaf_rn(fma_mixed<T>((uint16_t)p2, sb, m), qa.y, acc[1]);
+    acc[2] = __fmaf_rn(fma_mixed<T>((uint16_t)(p0 >> 16), sb, m), qa.z, acc[2]);
+    acc[3] = __fmaf_rn(fma_mixed<T>((uint16_t)(p2 >> 16), sb, m), qa.w, acc[3]);
+    acc[0] = __fmaf_rn(fma_mixed<T>((uint16_t)p1, sb, m), qb.x, acc[0]);
+    acc[1] = __fmaf_rn(fma_mixed<T>((uint16_t)p3, sb, m), qb.y, acc[1]);
+    acc[2] = __fmaf_rn(fma_mixed<T>((uint16_t)(p1 >> 16), sb, m), qb.z, acc[2]);
+    acc[3] = __fmaf_rn(fma_mixed<T>((uint16_t)(p3 >> 16), sb, m), qb.w, acc[3]);
   }
   return __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
 }

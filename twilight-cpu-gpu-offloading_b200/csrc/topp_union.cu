@@ -527,38 +527,37 @@ int launch_top_p_union(const TopPArgs& args, int groups, cudaStream_t stream) {
   return check_launch();
 }
 
-// ---- whole-layer selection in one launch --------------------------------------------------
-// One thread-block cluster of C CTAs per KV group (C = 16, the largest
-// cluster B200 schedules, when every group's cluster fits at once, else 8)
-// runs the four selection stages with every intermediate in shared memory:
-//  1. Quest scores: all CTAs of the cluster split the candidate pages, 8
-//     threads per page (quest_page_score8); each page's R scores go to the
-//     shared memory of the R row owners (CTA r owns query head r) over
-//     distributed shared memory;
-//  2. top-k pages: each owner radix-selects its row in its own shared memory
-//     (as topk_pages_kernel);
-//  3. INT4 estimate: the row's candidates are split over the C / R
-//     CTAs with rank % R == r; logits go to the owner's shared memory;
-//  4. top-p and the union, as top_p_union_kernel, with the leader (CTA 0)
-//     holding the bitmap;
-//  5. the sorted union is written by all CTAs, each a slice of the leader's
-//     bitmap words.
-// Scores, pages, logits and selections are bit-identical to the per-stage
-// kernels (same arithmetic, select_math.cuh).
-// One further cluster, when the caller asks for it, does work independent of
-// this step's selection while it runs: it appends the new token (position
-// old_length) and stages the protected rows (ProtectedStage).
-constexpr int kSelCluster = 8;      // portable cluster size
-constexpr int kSelClusterWide = 16; // non-portable cluster size
+// ---- whole-layer selection in one launch ---------------------------------------------------
+// One thread-block cluster of C CTAs per query-head row (g, r) of the layer,
+// G*R row clusters in all, runs the four selection stages of its row with
+// every intermediate in the shared memory of its leader CTA (rank 0):
+//  1. Quest scores: the C CTAs split the candidate pages, 4 threads per page
+//     (quest_page_score4); the scores go to the leader over distributed
+//     shared memory;
+//  2. top-k pages: the leader radix-selects the row's B0 pages (as
+//     topk_pages_kernel), ascending;
+//  3. INT4 estimate: the C CTAs split the row's candidates; logits go to the
+//     leader;
+//  4. top-p: the leader counts and marks the row's selection (top_p_row);
+//  5. GQA union: the leader ORs its selected candidates into the group's
+//     bitmap in global memory (one bit per candidate position, bit 0 =
+//     position sink) and counts its row in; the row cluster that counts in
+//     last writes the group's sorted union [0, sink_end) U bitmap U
+//     [recent_start, old_length), then clears the bitmap and the count, so
+//     the merge region is zero again for the next launch.  No row cluster
+//     waits for another, so they need not be resident together.
+// Scores, pages, logits, counts and unions are bit-identical to the
+// per-stage kernels (same arithmetic, select_math.cuh).
+// C is the largest cluster size (<= 8) for which every cluster of the launch
+// is resident at once (one SM per CTA).  One further cluster, when the caller
+// asks for it, does work independent of this step's selection while the row
+// clusters run, with no cluster barrier (so that its host reads never hold
+// up a barrier): it appends the new token (position old_length, beyond every
+// row the selection and the attention read) and stages the protected rows
+// (ProtectedStage) with 16-byte loads.
+constexpr int kSelMaxCluster = 8;  // portable cluster size
 
-// Query heads per group the fused selection serves, and its cluster sizes for
-// them: the largest multiple of R within 8 (portable) or 16 (non-portable),
-// so that every query head's row is shared by the same number of CTAs.
-__host__ __device__ constexpr bool select_fused_r(int R) {
-  return R == 1 || R == 2 || R == 3 || R == 4 || R == 6 || R == 8;
-}
-__host__ __device__ constexpr int select_cluster_narrow(int R) { return R * (kSelCluster / R); }
-__host__ __device__ constexpr int select_cluster_wide(int R) { return R * (kSelClusterWide / R); }
+__host__ __device__ constexpr bool select_fused_r(int R) { return R >= 1 && R <= kMaxHeadsPerGroup; }
 
 struct SelectArgs {
   const void* q;          // [G][R][D], QT
@@ -586,50 +585,159 @@ struct SelectArgs {
   int32_t* head_count;
   int32_t* head_pos;
   int32_t* error_flag;
-  int groups;             // selection clusters; a further cluster stages the
-  ProtectedStage stage;   // protected rows when stage.stage_k is set, and
-  AppendArgs append;      // appends the new token when do_append is set
-  int do_append;
-  int block_shift;        // block == 1 << block_shift, or -1 (not a power of two)
+  int groups;
+  int R;
+  unsigned int* merge_count;  // [G] row clusters counted in (zero between launches)
+  uint32_t* merge_bits;       // [G][merge_words] candidate bitmap (zero between launches)
+  int merge_words;
+  ProtectedStage stage;       // the extra cluster stages the protected rows when
+  AppendArgs append;          // stage.stage_k is set, and appends the new token
+  int do_append;              // when do_append is set
+  int block_shift;            // block == 1 << block_shift, or -1 (not a power of two)
 };
 
-// Dynamic shared memory: scores f32[P] | pages i32[b0] | logits f32[n] (keys
-// alias them) | mass u64[n] | bitmap u32[words] | sel u8[n] | the group's
-// queries as fp32 [kMaxHeadsPerGroup][D].
-__host__ __device__ __forceinline__ size_t select_smem_bytes(int P, int b0, int n, int64_t L) {
-  const size_t words = (size_t)((L + 31) / 32);
-  return align16((size_t)P * 4) + align16((size_t)b0 * 4) + align16((size_t)n * 4) +
-         align16((size_t)n * 8) + align16(words * 4) + align16((size_t)n) +
-         (size_t)kMaxHeadsPerGroup * kHeadDim * 4;
+// Merge region of the selection workspace: the last bytes of the caller's
+// buffer (so that the per-stage kernels' scores and logits at its start never
+// overlap it): count u32[G] at the very end, the bitmap u32[G][words] before.
+__host__ __device__ __forceinline__ int merge_words_of(int n_pages, int block) {
+  return (int)(((int64_t)n_pages * block + 31) / 32);
+}
+size_t merge_region_bytes(int groups, int n_pages, int block) {
+  const size_t bits = (size_t)groups * merge_words_of(n_pages, block) * 4;
+  return ((bits + 255) & ~(size_t)255) + (((size_t)groups * 4 + 255) & ~(size_t)255);
 }
 
-template <typename T, typename QT, int R>
+struct TopKShared {
+  uint32_t hist[256];
+  uint32_t scratch[32];
+  uint32_t prefix, remaining;
+};
+
+// Dynamic shared memory: the top-k state | scores f32[max(P, words)] (keys
+// alias them; the union writer's bitmap words later) | pages i32[b0] | logits
+// f32[n] (keys alias them) | mass u64[n] | sel u8[n] | the row's query as
+// fp32 [D].
+__host__ __device__ __forceinline__ size_t select_smem_bytes(int P, int b0, int n, int words) {
+  return align16(sizeof(TopKShared)) + align16((size_t)max(P, words) * 4) +
+         align16((size_t)b0 * 4) + align16((size_t)n * 4) + align16((size_t)n * 8) +
+         align16((size_t)n) + (size_t)kHeadDim * 4;
+}
+
+// Top-k pages of a row by the leader CTA: keys [P] (order-preserving score
+// keys) -> the B0 = k selected page indices ascending in s_pages and gout:
+// every key above the k-th largest and the lowest-index ties of it, by the
+// 4-pass radix select of topk_pages_kernel.
+__device__ void topk_row(const uint32_t* keys, int P, int k, int32_t* s_pages, int32_t* gout,
+                         TopKShared& sh) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  if (tid == 0) {
+    sh.prefix = 0u;
+    sh.remaining = (uint32_t)k;
+  }
+  __syncthreads();
+  uint32_t mask = 0u;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = tid; b < 256; b += blockDim.x) sh.hist[b] = 0u;
+    __syncthreads();
+    const uint32_t prefix = sh.prefix;
+    for (int i = tid; i < P; i += blockDim.x) {
+      const uint32_t key = keys[i];
+      if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t local[8];
+      uint32_t sum = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        local[j] = sh.hist[8 * lane + j];
+        sum += local[j];
+      }
+      uint32_t suffix = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, off);
+        if (lane + off < 32) suffix += y;
+      }
+      const uint32_t above = suffix - sum;
+      const uint32_t need = sh.remaining;
+      __syncwarp();
+      if (above < need && need <= suffix) {
+        uint32_t acc = above;
+        for (int j = 7; j >= 0; --j) {
+          if (acc + local[j] >= need) {
+            sh.prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
+            sh.remaining = need - acc;
+            break;
+          }
+          acc += local[j];
+        }
+      }
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  const uint32_t kth = sh.prefix;
+  const uint32_t ties = sh.remaining;
+  // keys above kth and the first `ties` keys equal to it, in index order
+  const int seg = (P + blockDim.x - 1) / blockDim.x;
+  const int beg = min(P, tid * seg);
+  const int end = min(P, beg + seg);
+  uint32_t gt = 0u, eq = 0u;
+  for (int i = beg; i < end; ++i) {
+    const uint32_t key = keys[i];
+    gt += key > kth;
+    eq += key == kth;
+  }
+  uint32_t total;
+  const uint32_t eq_before = block_exclusive_scan(eq, sh.scratch, &total);
+  const uint32_t take_eq = (eq_before >= ties) ? 0u : min(eq, ties - eq_before);
+  const uint32_t base = block_exclusive_scan(gt + take_eq, sh.scratch, &total);
+  uint32_t slot = base, eq_seen = 0u;
+  for (int i = beg; i < end; ++i) {
+    const uint32_t key = keys[i];
+    bool take = key > kth;
+    if (key == kth) {
+      take = eq_seen < take_eq;
+      ++eq_seen;
+    }
+    if (take) {
+      s_pages[slot] = i;
+      gout[slot] = i;
+      ++slot;
+    }
+  }
+  __syncthreads();
+}
+
+template <typename T, typename QT>
 __global__ void __launch_bounds__(kTopPThreads)
-select_layer_kernel(SelectArgs a) {
+select_rows_kernel(SelectArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ uint32_t scan_scratch[32];
-  __shared__ uint32_t s_hist[256];
-  __shared__ uint32_t s_prefix, s_remaining;
   __shared__ uint32_t s_woff[kTopPThreads];
-  __shared__ uint32_t s_base;
+  __shared__ uint32_t s_ctotal[kSelMaxCluster];
+  __shared__ uint32_t s_last;
 
   const int C = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
-  const int g = blockIdx.x / C;
-  if (g >= a.groups) {  // the extra cluster: no cluster barrier, no shared memory
-    const int cta = (int)blockIdx.x - a.groups * C;
-    // The new token (independent of this step's selection and attention: it
-    // goes to position old_length, beyond every row they read): group j by
-    // the cluster's threads 128 j .. 128 j + 127.
+  const int R = a.R;
+  const int row = blockIdx.x / C;  // g * R + r
+  if (row >= a.groups * R) {  // the extra cluster: no cluster barrier, no shared memory
+    const int cta = (int)blockIdx.x - a.groups * R * C;
     const int flat = cta * (int)blockDim.x + (int)threadIdx.x;
     if (a.do_append && flat < a.groups * kHeadDim)
       append_token_row<T>(a.append, flat / kHeadDim, flat % kHeadDim);
     if (a.stage.stage_k) stage_protected_rows(a.stage, a.groups, cta, C);
     return;
   }
+  const int g = row / R;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -637,224 +745,135 @@ select_layer_kernel(SelectArgs a) {
   const int P = a.n_pages;
   const int n = a.b0 * a.block;
   const int64_t L = a.old_length;
-  const int words = (int)((L + 31) >> 5);
+  const bool leader = crank == 0;
+  const int words = a.merge_words;
 
   unsigned char* cur = smem_raw;
+  TopKShared& s_topk = *reinterpret_cast<TopKShared*>(cur);
+  cur += align16(sizeof(TopKShared));
   float* s_score = reinterpret_cast<float*>(cur);
-  cur += align16((size_t)P * 4);
+  cur += align16((size_t)max(P, words) * 4);
   int32_t* s_pages = reinterpret_cast<int32_t*>(cur);
   cur += align16((size_t)a.b0 * 4);
   float* s_logit = reinterpret_cast<float*>(cur);
   cur += align16((size_t)n * 4);
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(cur);
   cur += align16((size_t)n * 8);
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(cur);
-  cur += align16((size_t)words * 4);
   unsigned char* sel = cur;
   cur += align16((size_t)n);
   float* s_q = reinterpret_cast<float*>(cur);
 
+  const T* scale = reinterpret_cast<const T*>(a.scale);
+  const T* minimum = reinterpret_cast<const T*>(a.minimum);
+  const int ngroups = kHeadDim / a.group_size;
+  const int64_t tbase = (int64_t)g * a.entry_stride + a.sink;
+  const T* gmin = reinterpret_cast<const T*>(a.pmin) + (int64_t)g * a.meta_stride;
+  const T* gmax = reinterpret_cast<const T*>(a.pmax) + (int64_t)g * a.meta_stride;
+  const int per_cta = (P + C - 1) / C;
+  const int p_beg = min(P, crank * per_cta);
+  const int p_end = min(P, p_beg + per_cta);
+  // This CTA's Quest min / max range is requested from DRAM into L2 before
+  // anything waits on memory, so the score loads below wait on L2 rather than
+  // each on a DRAM round trip.
+  if (tid < 2 && p_end > p_beg)
+    prefetch_l2((tid == 0 ? gmin : gmax) + (int64_t)p_beg * kHeadDim,
+                (size_t)(p_end - p_beg) * kHeadDim * sizeof(T));
   {
-    const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)g * R * kHeadDim;
-    for (int i = tid; i < R * kHeadDim; i += blockDim.x) s_q[i] = to_f32(qg[i]);
+    const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)row * kHeadDim;
+    for (int i = tid; i < kHeadDim; i += blockDim.x) s_q[i] = to_f32(qg[i]);
   }
-  // Leader: clear the bitmap and set the protected sink / recent ranges.
-  if (crank == 0) {
-    const int64_t sink_hi = min(a.sink_end, L);
-    for (int w = tid; w < words; w += blockDim.x) {
-      const int64_t lo = (int64_t)w * 32;
-      bitmap[w] = bits_below(sink_hi, lo) | (bits_below(L, lo) & ~bits_below(a.recent_start, lo));
-    }
-  }
-
   __syncthreads();  // s_q
 
-  // 1. Quest scores of the group's R heads.
+  // 1. Quest scores of the row's query head over the group's candidate pages.
   {
-    const T* gmin = reinterpret_cast<const T*>(a.pmin) + (int64_t)g * a.meta_stride;
-    const T* gmax = reinterpret_cast<const T*>(a.pmax) + (int64_t)g * a.meta_stride;
-    float* owner_scores[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) owner_scores[r] = cluster.map_shared_rank(s_score, r);
-    // CTA crank scores the contiguous pages [p_beg, p_end)
-    const int per_cta = (P + C - 1) / C;
-    const int p_beg = min(P, crank * per_cta);
-    const int p_end = min(P, p_beg + per_cta);
-    // The whole min / max range is requested from DRAM into L2 at once, so
-    // the warps' loads below wait on L2 rather than each on a DRAM round trip.
-    if (tid < 2 && p_end > p_beg)
-      prefetch_l2((tid == 0 ? gmin : gmax) + (int64_t)p_beg * kHeadDim,
-                  (size_t)(p_end - p_beg) * kHeadDim * sizeof(T));
-    // 8 threads per page, 4 pages per warp and pass (the pass index is
-    // warp-uniform: the 8-thread shuffles need the whole warp).
-    const int j8 = lane & 7;
-    const int groups_per_cta = (int)(blockDim.x >> 3);
-    for (int base = p_beg + warp * 4; base < p_end; base += groups_per_cta) {
-      const int p = base + (lane >> 3);
+    float* owner_scores = cluster.map_shared_rank(s_score, 0);
+    const int j4 = lane & 3;
+    const int pages_per_pass = (int)(blockDim.x >> 2);
+    for (int base = p_beg + warp * 8; base < p_end; base += pages_per_pass) {
+      const int p = base + (lane >> 2);  // base is warp-uniform: the 4-lane shuffles
       const bool valid = p < p_end;
-      float sc[R];
-      quest_page_score8<T, R>(s_q, gmin, gmax, valid ? p : p_beg, j8, valid, sc);
-      if (valid && j8 == 0) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) owner_scores[r][p] = sc[r];
-      }
+      const float sc = quest_page_score4<T>(s_q, gmin, gmax, valid ? p : p_beg, j4, valid);
+      if (valid && j4 == 0) owner_scores[p] = sc;
     }
   }
   cluster.sync();
 
-  const bool owner = crank < R;
-  const int row = g * R + crank;
-  // 2. top-k pages of the owner's row (the radix select of topk_pages_kernel).
-  if (owner) {
+  // 2. top-k pages of the row, ascending.
+  if (leader) {
     uint32_t* keys = reinterpret_cast<uint32_t*>(s_score);
     for (int i = tid; i < P; i += blockDim.x) keys[i] = float_key(s_score[i]);
-    if (tid == 0) {
-      s_prefix = 0u;
-      s_remaining = (uint32_t)a.b0;
-    }
     __syncthreads();
-    uint32_t mask = 0u;
-#pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int b = tid; b < 256; b += blockDim.x) s_hist[b] = 0u;
-      __syncthreads();
-      const uint32_t prefix = s_prefix;
-      for (int i = tid; i < P; i += blockDim.x) {
-        const uint32_t key = keys[i];
-        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
-      }
-      __syncthreads();
-      if (warp == 0) {
-        uint32_t local[8];
-        uint32_t sum = 0u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          local[j] = s_hist[8 * lane + j];
-          sum += local[j];
-        }
-        uint32_t suffix = sum;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, off);
-          if (lane + off < 32) suffix += y;
-        }
-        const uint32_t above = suffix - sum;
-        const uint32_t need = s_remaining;
-        __syncwarp();
-        if (above < need && need <= suffix) {
-          uint32_t acc = above;
-          for (int j = 7; j >= 0; --j) {
-            if (acc + local[j] >= need) {
-              s_prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
-              s_remaining = need - acc;
-              break;
-            }
-            acc += local[j];
-          }
-        }
-      }
-      mask |= 255u << shift;
-      __syncthreads();
-    }
-    const uint32_t kth = s_prefix;
-    const uint32_t ties = s_remaining;
-    const int seg = (P + blockDim.x - 1) / blockDim.x;
-    const int beg = min(P, tid * seg);
-    const int end = min(P, beg + seg);
-    uint32_t gt = 0u, eq = 0u;
-    for (int i = beg; i < end; ++i) {
-      const uint32_t key = keys[i];
-      gt += key > kth;
-      eq += key == kth;
-    }
-    uint32_t total;
-    const uint32_t eq_before = block_exclusive_scan(eq, scan_scratch, &total);
-    const uint32_t take_eq = (eq_before >= ties) ? 0u : min(eq, ties - eq_before);
-    const uint32_t base = block_exclusive_scan(gt + take_eq, scan_scratch, &total);
-    int32_t* gout = a.pages_out + (int64_t)row * a.b0;
-    uint32_t slot = base, eq_seen = 0u;
-    for (int i = beg; i < end; ++i) {
-      const uint32_t key = keys[i];
-      bool take = key > kth;
-      if (key == kth) {
-        take = eq_seen < take_eq;
-        ++eq_seen;
-      }
-      if (take) {
-        s_pages[slot] = i;
-        gout[slot] = i;
-        ++slot;
-      }
-    }
+    topk_row(keys, P, a.b0, s_pages, a.pages_out + (int64_t)row * a.b0, s_topk);
   }
   cluster.sync();
 
-  // 3. INT4 estimate: CTAs with rank % R == r share row r's candidates.
+  // 3. INT4 estimate: the C CTAs split the row's candidates.
   {
-    const int r = crank % R;
-    const int part = crank / R;
-    const int parts = C / R;
-    if (!owner) {  // this CTA's copy of row r's pages (the loop reads them per candidate)
-      const int32_t* src = cluster.map_shared_rank(s_pages, r);
+    if (!leader) {  // this CTA's copy of the row's pages (the loop reads them per candidate)
+      const int32_t* src = cluster.map_shared_rank(s_pages, 0);
       for (int i = tid; i < a.b0; i += blockDim.x) s_pages[i] = src[i];
     }
     __syncthreads();
-    const int chunk = (n + parts - 1) / parts;
-    const int c_beg = min(n, part * chunk);
+    const int chunk = (n + C - 1) / C;
+    const int c_beg = min(n, crank * chunk);
     const int c_end = min(n, c_beg + chunk);
     const int sub = lane & 3;
     const int tok = lane >> 2;
     float qr[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) qr[i] = s_q[r * kHeadDim + 32 * sub + i];
-    const int ngroups = kHeadDim / a.group_size;
+    for (int i = 0; i < 32; ++i) qr[i] = s_q[32 * sub + i];
     const int grp = (32 * sub) / a.group_size;
     const int32_t* prow = s_pages;
-    float* lout = cluster.map_shared_rank(s_logit, r);
-    const int64_t tbase = (int64_t)g * a.entry_stride + a.sink;
-    const T* scale = reinterpret_cast<const T*>(a.scale);
-    const T* minimum = reinterpret_cast<const T*>(a.minimum);
+    float* lout = cluster.map_shared_rank(s_logit, 0);
     constexpr int kStep = kTopPThreads / 4;  // candidates per pass of the CTA
-    // Each 4-lane group estimates one candidate per pass; the next pass's
-    // candidate is loaded before this pass's arithmetic, so its loads are in
-    // flight while the group computes.  Candidate i is token
-    // sink + prow[i / block] * block + i % block of the group's entry.
-    uint4 codes_n = make_uint4(0u, 0u, 0u, 0u);
-    T sv_n = from_f32<T>(0.0f);
-    float mv_n = 0.0f;
-    auto load = [&](int i) {
-      if (i < c_end) {
-        int pg, t;
-        if (a.block_shift >= 0) {
-          pg = i >> a.block_shift;
-          t = i & (a.block - 1);
-        } else {
-          pg = i / a.block;
-          t = i - pg * a.block;
-        }
-        const int64_t tr = tbase + (int64_t)prow[pg] * a.block + t;
-        codes_n = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
-        sv_n = scale[tr * ngroups + grp];
-        mv_n = to_f32(minimum[tr * ngroups + grp]);
+    constexpr int kAhead = 2;                // passes whose loads are in flight together
+    // Each 4-lane group estimates one candidate per pass; the codes of kAhead
+    // passes are loaded before their arithmetic, so their latencies overlap.
+    // Candidate i is token sink + prow[i / block] * block + i % block of the
+    // group's entry.
+    auto token_of = [&](int i) -> int64_t {
+      int pg, t;
+      if (a.block_shift >= 0) {
+        pg = i >> a.block_shift;
+        t = i & (a.block - 1);
+      } else {
+        pg = i / a.block;
+        t = i - pg * a.block;
       }
+      return tbase + (int64_t)prow[pg] * a.block + t;
     };
-    // base is warp-uniform (all lanes run every pass: int4_logit shuffles)
-    int base = c_beg + warp * 8;
-    load(base + tok);
-    for (; base < c_end; base += kStep) {
-      const uint4 codes = codes_n;
-      const T sv = sv_n;
-      const float mv = mv_n;
-      load(base + kStep + tok);
-      const float logit = int4_logit(int4_dot32<T>(codes, sv, mv, qr), a.inv_sqrt_d);
-      if (base + tok < c_end && sub == 0) lout[base + tok] = logit;
+    for (int base0 = c_beg + warp * 8; base0 < c_end; base0 += kAhead * kStep) {  // warp-uniform
+      uint4 codes[kAhead];
+      T sv[kAhead];
+      float mv[kAhead];
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) {
+        const int i = base0 + u * kStep + tok;
+        codes[u] = make_uint4(0u, 0u, 0u, 0u);
+        sv[u] = from_f32<T>(0.0f);
+        mv[u] = 0.0f;
+        if (i < c_end) {
+          const int64_t tr = token_of(i);
+          codes[u] = __ldg(reinterpret_cast<const uint4*>(a.packed + tr * (kHeadDim / 2)) + sub);
+          sv[u] = scale[tr * ngroups + grp];
+          mv[u] = to_f32(minimum[tr * ngroups + grp]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) {
+        const int base = base0 + u * kStep;
+        if (base >= c_end) break;  // warp-uniform
+        const float logit = int4_logit(int4_dot32<T>(codes[u], sv[u], mv[u], qr), a.inv_sqrt_d);
+        if (base + tok < c_end && sub == 0) lout[base + tok] = logit;
+      }
     }
   }
   cluster.sync();
 
-  // 4. top-p of the owner's row, then its selection into the leader's bitmap.
-  if (owner) {
+  // 4. top-p of the row; its selection into the group's merge bitmap.
+  unsigned int* gcount = a.merge_count + g;
+  uint32_t* gbits = a.merge_bits + (int64_t)g * words;
+  if (leader) {
     const int count = top_p_row(s_logit, n, a.top_p, reinterpret_cast<uint32_t*>(s_logit), mass, sel);
     if (tid == 0) a.head_count[row] = count;
     if (a.head_pos) {
@@ -864,108 +883,158 @@ select_layer_kernel(SelectArgs a) {
       uint32_t c = 0u;
       for (int i = beg; i < end; ++i) c += sel[i];
       uint32_t total;
-      uint32_t slot = block_exclusive_scan(c, scan_scratch, &total);
+      uint32_t slot = block_exclusive_scan(c, s_topk.scratch, &total);
       int32_t* hp = a.head_pos + (int64_t)row * n;
       for (int i = beg; i < end; ++i)
         if (sel[i]) hp[slot++] = (int32_t)cand_position(s_pages, i, a.block, a.sink);
     }
+    // candidate bit b = page * block + j (position sink + b)
+    bool bad = false;
+    for (int pg = tid; pg < a.b0; pg += blockDim.x) {
+      const int page = s_pages[pg];
+      if (page < 0 || page >= P) {
+        bad = true;
+        continue;
+      }
+      const int64_t b_page = (int64_t)page * a.block;
+      for (int j = 0; j < a.block;) {
+        const int64_t b = b_page + j;
+        const int take = min(a.block - j, 32 - (int)(b & 31));
+        uint32_t m32 = 0u;
+        for (int t = 0; t < take; ++t) m32 |= (uint32_t)sel[pg * a.block + j + t] << t;
+        if (m32) atomicOr(&gbits[b >> 5], m32 << (uint32_t)(b & 31));
+        j += take;
+      }
+    }
+    if (bad && a.error_flag) atomicExch(a.error_flag, TW_ERR_INVALID_INDEX);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned int prev = atomicAdd(gcount, 1u);
+      __threadfence();
+      const uint32_t last = (prev == (unsigned int)R - 1u) ? 1u : 0u;
+      // to every CTA's own copy: after the barrier below no CTA reads the
+      // leader's shared memory, so each may exit on its own
+      for (int c = 0; c < C; ++c) *cluster.map_shared_rank(&s_last, c) = last;
+    }
   }
   cluster.sync();
-  uint32_t* leader_bitmap = cluster.map_shared_rank(bitmap, 0);
-  if (owner && or_selection(leader_bitmap, s_pages, sel, a.b0, a.block, a.sink, L) && a.error_flag)
-    atomicExch(a.error_flag, TW_ERR_INVALID_INDEX);
-  cluster.sync();
 
-  // 5. Sorted union: CTA c writes the positions of words [c*ws, (c+1)*ws).
-  {
+  // 5. The row cluster counted in last writes the group's sorted union.  CTA
+  //    c takes the bitmap words [c*ws, (c+1)*ws) into its shared memory and
+  //    clears them in global memory; the word totals go to every CTA over
+  //    distributed shared memory; CTA 0 also writes the sink range, CTA C-1
+  //    the recent window and the count.
+  if (s_last) {
+    __threadfence();
     const int ws = (words + C - 1) / C;
     const int w_beg = min(words, crank * ws);
     const int w_end = min(words, w_beg + ws);
-    uint32_t before = 0u;
-    for (int w = tid; w < w_beg; w += blockDim.x) before += __popc(leader_bitmap[w]);
-    uint32_t total_before;
-    block_exclusive_scan(before, scan_scratch, &total_before);
-    if (tid == 0) s_base = total_before;
-    __syncthreads();
+    const int nw = w_end - w_beg;
+    uint32_t* s_words = reinterpret_cast<uint32_t*>(s_score);
+    uint32_t mine = 0u;
+    for (int w = tid; w < nw; w += blockDim.x) {
+      const uint32_t x = __ldcg(gbits + w_beg + w);
+      s_words[w] = x;
+      mine += __popc(x);
+      gbits[w_beg + w] = 0u;
+    }
+    uint32_t ctotal;
+    block_exclusive_scan(mine, s_topk.scratch, &ctotal);
+    if (tid == 0)
+      for (int c = 0; c < C; ++c) cluster.map_shared_rank(s_ctotal, c)[crank] = ctotal;
+    cluster.sync();  // totals exchanged; no shared memory of another CTA is read after this
+    uint32_t running = 0u;
+    for (int c = 0; c < crank; ++c) running += s_ctotal[c];
     int32_t* dst = a.union_pos + (int64_t)g * a.pos_stride;
-    uint32_t running = s_base;
-    for (int c0 = w_beg; c0 < w_end; c0 += kTopPThreads) {
+    const int64_t sink_hi = min(a.sink_end, L);
+    if (crank == 0)
+      for (int64_t p = tid; p < sink_hi; p += blockDim.x) dst[p] = (int32_t)p;
+    for (int c0 = 0; c0 < nw; c0 += kTopPThreads) {
       const int w = c0 + tid;
-      const uint32_t bits = w < w_end ? leader_bitmap[w] : 0u;
+      const uint32_t bits = w < nw ? s_words[w] : 0u;
       uint32_t chunk_total;
-      s_woff[tid] = running + block_exclusive_scan((uint32_t)__popc(bits), scan_scratch, &chunk_total);
+      s_woff[tid] = running + block_exclusive_scan((uint32_t)__popc(bits), s_topk.scratch, &chunk_total);
       __syncthreads();
-      const int chunk_words = min(kTopPThreads, w_end - c0);
+      const int chunk_words = min(kTopPThreads, nw - c0);
       for (int j = warp; j < chunk_words; j += nwarps) {
-        const uint32_t word = leader_bitmap[c0 + j];
+        const uint32_t word = s_words[c0 + j];
         if ((word >> lane) & 1u)
-          dst[s_woff[j] + __popc(word & ((1u << lane) - 1u))] = (c0 + j) * 32 + lane;
+          dst[sink_hi + s_woff[j] + __popc(word & ((1u << lane) - 1u))] =
+              (int32_t)(a.sink + (int64_t)(w_beg + c0 + j) * 32 + lane);
       }
       running += chunk_total;
       __syncthreads();
     }
-    if (crank == C - 1 && tid == 0) a.union_count[g] = (int32_t)running;
+    if (crank == C - 1) {
+      const int64_t recent_lo = max(a.recent_start, sink_hi);
+      int32_t* rdst = dst + sink_hi + running;
+      for (int64_t p = recent_lo + tid; p < L; p += blockDim.x) rdst[p - recent_lo] = (int32_t)p;
+      if (tid == 0) a.union_count[g] = (int32_t)(sink_hi + running + (L - recent_lo));
+    }
+    if (crank == 0 && tid == 0) *gcount = 0u;
   }
-  cluster.sync();  // the leader's bitmap is read until here
 }
 
-// Whether the fused selection serves this shape (select_fused_r(R), and
-// the shared memory fitting one CTA).
+// Whether the fused selection serves this shape (shared memory fitting one CTA).
 bool select_fused_supported(int R, int P, int b0, int block, int64_t L, size_t* smem) {
   if (!select_fused_r(R) || b0 <= 0 || P <= 0) return false;
   const int64_t n = (int64_t)b0 * block;
   if (n > 65536 || L > ((int64_t)1 << 30)) return false;
-  *smem = select_smem_bytes(P, b0, (int)n, L);
+  *smem = select_smem_bytes(P, b0, (int)n, merge_words_of(P, block));
   return *smem <= 160 * 1024;
 }
 
-// Wide clusters (16 CTAs; 15 or 12 for R = 3 or 6) when the device can run
-// at least `groups` of them at once (queried once per device and kernel; the
-// kernel needs one SM per CTA at the shared memory the fused selection may
-// use), else narrow ones (8; 6 for R = 3 or 6).
-template <typename T, typename QT, int R>
-int select_cluster_size(int groups) {
-  static int wide_clusters[kMaxDevices];  // 0: not queried, -1: none
+// Cluster size: the largest C <= 8 for which all `clusters` clusters of C
+// CTAs (one SM each, at the shared memory the selection may use) are resident
+// at once on this device, queried once per device and kernel; 1 when none is.
+template <typename T, typename QT>
+int select_cluster_size(int clusters) {
   static std::mutex mu;
+  static int max_active[kMaxDevices][kSelMaxCluster + 1];  // 0: not queried, -1: failed
   int dev = 0;
-  constexpr int narrow = select_cluster_narrow(R), wide = select_cluster_wide(R);
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return narrow;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 1;
   std::lock_guard<std::mutex> lk(mu);
-  if (wide_clusters[dev] == 0) {
-    int n = -1;
-    const void* fn = (const void*)select_layer_kernel<T, QT, R>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
-            cudaSuccess) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(wide, 1, 1);
-      cfg.blockDim = dim3(kTopPThreads, 1, 1);
-      cfg.dynamicSmemBytes = 160 * 1024;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = wide;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int count = 0;
-      if (cudaOccupancyMaxActiveClusters(&count, fn, &cfg) == cudaSuccess && count > 0) n = count;
+  const void* fn = (const void*)select_rows_kernel<T, QT>;
+  for (int c = kSelMaxCluster; c >= 2; --c) {
+    if (max_active[dev][c] == 0) {
+      int count = -1;
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
+          cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c, 1, 1);
+        cfg.blockDim = dim3(kTopPThreads, 1, 1);
+        cfg.dynamicSmemBytes = 160 * 1024;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = c;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int k = 0;
+        if (cudaOccupancyMaxActiveClusters(&k, fn, &cfg) == cudaSuccess && k > 0) count = k;
+      }
+      cudaGetLastError();  // a refused query leaves no error behind
+      max_active[dev][c] = count;
     }
-    cudaGetLastError();  // a refused query leaves no error behind
-    wide_clusters[dev] = n;
+    if (max_active[dev][c] >= clusters) return c;
   }
-  return wide_clusters[dev] >= groups ? wide : narrow;
+  return 1;
 }
 
-template <typename T, typename QT, int R>
-int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t stream) {
+template <typename T, typename QT>
+int launch_select_rows(const SelectArgs& a, size_t smem, cudaStream_t stream) {
   static DynSmemOptIn opt_in;
-  const int clusters = groups + ((a.stage.stage_k || a.do_append) ? 1 : 0);
-  const int cluster = select_cluster_size<T, QT, R>(clusters);
-  const int st = ensure_dyn_smem((const void*)select_layer_kernel<T, QT, R>, opt_in, (int)smem);
+  const int rows = a.groups * a.R;
+  const bool extra = a.stage.stage_k != nullptr || a.do_append;
+  const int cluster = select_cluster_size<T, QT>(rows + (extra ? 1 : 0));
+  if (extra && (int64_t)a.groups * kHeadDim > (int64_t)cluster * kTopPThreads)
+    return TW_ERR_UNSUPPORTED;  // the extra cluster covers 128 threads per group's append
+  const int st = ensure_dyn_smem((const void*)select_rows_kernel<T, QT>, opt_in, (int)smem);
   if (st != TW_OK) return st;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(clusters * cluster, 1, 1);
+  cfg.gridDim = dim3((rows + (extra ? 1 : 0)) * cluster, 1, 1);
   cfg.blockDim = dim3(kTopPThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -978,7 +1047,7 @@ int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t s
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, select_layer_kernel<T, QT, R>, a);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, select_rows_kernel<T, QT>, a);
   if (err != cudaSuccess) {
     set_last_cuda_error(err);
     return TW_ERR_CUDA;
@@ -986,35 +1055,13 @@ int launch_select_r(const SelectArgs& a, int groups, size_t smem, cudaStream_t s
   return check_launch();
 }
 
-template <typename T, typename QT>
-int launch_select_t(const SelectArgs& a, int groups, int R, size_t smem, cudaStream_t stream) {
-  switch (R) {
-    case 1: return launch_select_r<T, QT, 1>(a, groups, smem, stream);
-    case 2: return launch_select_r<T, QT, 2>(a, groups, smem, stream);
-    case 3: return launch_select_r<T, QT, 3>(a, groups, smem, stream);
-    case 4: return launch_select_r<T, QT, 4>(a, groups, smem, stream);
-    case 6: return launch_select_r<T, QT, 6>(a, groups, smem, stream);
-    case 8: return launch_select_r<T, QT, 8>(a, groups, smem, stream);
-    default: return TW_ERR_UNSUPPORTED;
-  }
-}
-
-// The fused selection (q in fp32 or in the K dtype).
-int launch_select_fused(const SelectArgs& a, int groups, int R, int q_dtype, int dtype, size_t smem,
-                        cudaStream_t stream) {
-  if (dtype == TW_F16)
-    return q_dtype == TW_F32 ? launch_select_t<__half, float>(a, groups, R, smem, stream)
-                             : launch_select_t<__half, __half>(a, groups, R, smem, stream);
-  if (dtype == TW_BF16)
-    return q_dtype == TW_F32 ? launch_select_t<__nv_bfloat16, float>(a, groups, R, smem, stream)
-                             : launch_select_t<__nv_bfloat16, __nv_bfloat16>(a, groups, R, smem, stream);
-  return TW_ERR_UNSUPPORTED;
-}
-
 // The whole Twilight selection of one layer in one launch when the shape
-// allows it (select_fused_r(R), shared memory fitting a CTA); returns
-// TW_ERR_UNSUPPORTED otherwise, and the caller runs the per-stage kernels.
-// Same arguments and checks as tw_select_layer's stages; q in fp32 or the K dtype.
+// allows it (shared memory fitting a CTA); returns TW_ERR_UNSUPPORTED
+// otherwise, and the caller runs the per-stage kernels.  Same arguments and
+// checks as tw_select_layer's stages; q in fp32 or the K dtype.  workspace:
+// the caller's selection workspace (its last merge_region_bytes hold the
+// union merge state and must be zero before the first call; every call
+// leaves them zero).
 int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void* pmax,
                        int64_t meta_stride, int n_pages, const uint8_t* packed, const void* scale,
                        const void* minimum, int64_t entry_stride, int groups, int R, int b0,
@@ -1022,8 +1069,9 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
                        int64_t old_length, int64_t sink_end, int64_t recent_start,
                        int32_t* pages_out, int32_t* union_pos, int64_t pos_stride,
                        int32_t* union_count, int32_t* head_count, int32_t* head_pos,
-                       int32_t* error_flag, const ProtectedStage* stage,
-                       const AppendArgs* append, cudaStream_t stream) {
+                       int32_t* error_flag, void* workspace, size_t workspace_bytes,
+                       const ProtectedStage* stage, const AppendArgs* append,
+                       cudaStream_t stream) {
   if (!q || !pmin || !pmax || !packed || !scale || !minimum || !pages_out || !union_pos ||
       !union_count || !head_count || groups <= 0 || groups > (1 << 27) || R <= 0 ||
       n_pages <= 0 || b0 <= 0 || b0 > n_pages || block <= 0 || sink < 0 || old_length < 0 ||
@@ -1034,11 +1082,18 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
   if (group_size != 32 && group_size != 64 && group_size != 128) return TW_ERR_UNSUPPORTED;
   if (dtype != TW_F16 && dtype != TW_BF16) return TW_ERR_UNSUPPORTED;
   if (q_dtype != TW_F32 && q_dtype != dtype) return TW_ERR_BAD_ARG;
+  // candidate positions sink + page * block must lie in [sink_end, recent_start)
+  if ((int64_t)sink + (int64_t)n_pages * block > recent_start || sink < sink_end)
+    return TW_ERR_UNSUPPORTED;
+  if ((int64_t)groups * R * kSelMaxCluster > (int64_t)INT32_MAX / 2) return TW_ERR_UNSUPPORTED;
   size_t smem = 0;
   if (!select_fused_supported(R, n_pages, b0, block, old_length, &smem)) return TW_ERR_UNSUPPORTED;
-  // 8-byte page-row loads (4 channels) in the Quest phase
-  if ((((uintptr_t)pmin | (uintptr_t)pmax) & 7) != 0 || meta_stride % 4 != 0)
+  // 16-byte page-row loads (8 channels) in the Quest phase
+  if ((((uintptr_t)pmin | (uintptr_t)pmax) & 15) != 0 || meta_stride % 8 != 0)
     return TW_ERR_UNSUPPORTED;
+  const size_t merge = merge_region_bytes(groups, n_pages, block);
+  if (!workspace || workspace_bytes < merge || ((uintptr_t)workspace & 3) != 0)
+    return TW_ERR_CAPACITY;
   SelectArgs a{};
   a.q = q;
   a.pmin = pmin;
@@ -1066,6 +1121,15 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
   a.head_pos = head_pos;
   a.error_flag = error_flag;
   a.groups = groups;
+  a.R = R;
+  {
+    // merge region at the end of the caller's buffer (4-byte aligned words)
+    char* end = reinterpret_cast<char*>(workspace) + (workspace_bytes & ~(size_t)3);
+    const size_t count_bytes = ((size_t)groups * 4 + 255) & ~(size_t)255;
+    a.merge_count = reinterpret_cast<unsigned int*>(end - count_bytes);
+    a.merge_words = merge_words_of(n_pages, block);
+    a.merge_bits = reinterpret_cast<uint32_t*>(end - merge);
+  }
   a.block_shift = -1;
   for (int b = 0; b < 31; ++b)
     if (block == (1 << b)) a.block_shift = b;
@@ -1081,14 +1145,14 @@ int select_layer_fused(const void* q, int q_dtype, const void* pmin, const void*
     a.stage = *stage;
   }
   if (append) {
-    // the extra cluster (at least select_cluster_narrow(R) CTAs of kTopPThreads)
-    // covers 128 threads per group
-    if ((int64_t)groups * kHeadDim > (int64_t)select_cluster_narrow(R) * kTopPThreads)
-      return TW_ERR_UNSUPPORTED;
     a.append = *append;
     a.do_append = 1;
   }
-  return launch_select_fused(a, groups, R, q_dtype, dtype, smem, stream);
+  if (dtype == TW_F16)
+    return q_dtype == TW_F32 ? launch_select_rows<__half, float>(a, smem, stream)
+                             : launch_select_rows<__half, __half>(a, smem, stream);
+  return q_dtype == TW_F32 ? launch_select_rows<__nv_bfloat16, float>(a, smem, stream)
+                           : launch_select_rows<__nv_bfloat16, __nv_bfloat16>(a, smem, stream);
 }
 
 }  // namespace tw

@@ -169,7 +169,7 @@ def select_layer(q: torch.Tensor, page_min: torch.Tensor, page_max: torch.Tensor
     if pages is None:
         pages = torch.empty((G, R, b0_pages), device=q.device, dtype=torch.int32)
     ws_bytes = select_layer_workspace_bytes(G, R, n_pages, b0_pages, block_size)
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)  # merge region zero
     _lib.check(lib().tw_select_layer(
         _ptr(q), _ptr(page_min), _ptr(page_max), page_min.shape[1] * D, n_pages, _ptr(packed),
         _ptr(scale), _ptr(minimum), packed.shape[1], G, R, b0_pages, block_size, sink, D,
