@@ -143,16 +143,18 @@ def _timed_ms(fn) -> float:
 
 def link_peaks(tw, slab, device, world: int, reps: int = 6) -> dict:
     """Host-link peaks with every rank probing at the same time (a barrier
-    before each repetition, the slowest rank's time per repetition):
+    before each repetition):
 
     * copy: a 256 MiB pinned host -> device cudaMemcpyAsync (copy engine);
     * mapped: a sequential zero-copy read of this rank's mapped slab (all its
       K and V rows, tw_gather_kv: SM 16-byte loads, the attention kernel's
       access path).
 
-    Per mechanism: the best single-rank GB/s and the best aggregate GB/s
-    (world x bytes / the slowest rank's time).  With world = 1 both are the
-    one GPU's peak."""
+    Per mechanism and repetition the ranks' own rates (bytes / own time) are
+    summed: the aggregate the host delivers while all ranks read (when the
+    host shares its bandwidth unevenly, world x bytes / the slowest rank's
+    time, also reported, is lower).  The best repetition is kept.  With world
+    = 1 all of them are the one GPU's peak."""
     nbytes = 256 << 20
     host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -173,16 +175,26 @@ def link_peaks(tw, slab, device, world: int, reps: int = 6) -> dict:
     for name, (nb, fn) in probes.items():
         fn()  # warm-up
         torch.cuda.synchronize()
-        single = agg = 0.0
+        single = agg = agg_slowest = 0.0
         for _ in range(reps):
             if world > 1:
                 torch.distributed.barrier()
             ms = _timed_ms(fn)
-            slowest = max_over_ranks(ms, device, world)
-            single = max(single, nb / (ms * 1e-3) / 1e9)
-            agg = max(agg, world * nb / (slowest * 1e-3) / 1e9)
+            rate = nb / (ms * 1e-3) / 1e9
+            total = rate
+            slowest = ms
+            if world > 1:
+                t = torch.tensor([rate, ms], dtype=torch.float64, device=device)
+                every = [torch.zeros_like(t) for _ in range(world)]
+                torch.distributed.all_gather(every, t)
+                total = float(sum(x[0].item() for x in every))
+                slowest = float(max(x[1].item() for x in every))
+            single = max(single, rate)
+            agg = max(agg, total)
+            agg_slowest = max(agg_slowest, world * nb / (slowest * 1e-3) / 1e9)
         res[name] = {"single_gbs": round(single, 2), "aggregate_gbs": round(agg, 2),
-                     "per_rank_gbs": round(agg / world, 2)}
+                     "per_rank_gbs": round(agg / world, 2),
+                     "aggregate_slowest_gbs": round(agg_slowest, 2)}
     if int(err.item()) != 0:
         raise RuntimeError("mapped-read probe reported an invalid row")
     del host, dev, out_k, out_v, rows
@@ -486,6 +498,9 @@ def run_ours(args) -> int:
     for i in range(B):
         step.load_query(q_dev[K + i])
         l2_flush(flush)
+        if world > 1:  # every rank's per-stage step at the same time: stages under contention
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
         ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
         step.run(ev)
         for n in names:
@@ -580,7 +595,8 @@ def run_ours(args) -> int:
             "gpu_launches": step.launches_per_step * K * world,
             "kernel_ms": {n: round(float(np.mean(v)), 5) for n, v in kern_ms.items()},
             "kernel_ms_note": f"per-stage CUDA events on {B} further steps (stage boundaries "
-                              "then carry an event, so stages do not overlap there)",
+                              "then carry an event, so stages do not overlap there); with N > 1 "
+                              "all ranks run each of these steps at once (barrier before it)",
             "roofline": {
                 "bound": "host_link",
                 "kernel": ("attention_kernel<UnionRows> (fused zero-copy gather + split-K attention)"
@@ -604,8 +620,9 @@ def run_ours(args) -> int:
                 "link_peaks": peaks_link,
                 "link_peaks_note": ("copy = pinned H2D cudaMemcpyAsync (copy engine); mapped = "
                                     "sequential zero-copy SM reads of the mapped slab (the "
-                                    "attention kernel's access path); aggregate = all ranks at "
-                                    "once, world x bytes / the slowest rank's time"),
+                                    "attention kernel's access path); all ranks at once after a "
+                                    "barrier: aggregate = the sum of the ranks' own rates, "
+                                    "aggregate_slowest = world x bytes / the slowest rank's time"),
             },
             "roofline_step": {
                 "t_roof_us": round(t_roof_ms * 1e3, 2),
@@ -617,6 +634,10 @@ def run_ours(args) -> int:
                 "hbm_peak_source": hbm_src,
                 "host_link_peak_gbs": round(link_peak, 2),
                 "host_link_peak_source": "copy peak per rank with all ranks at once (roofline.link_peaks)",
+                # all ranks together: every rank moves host_bytes per step (replicas)
+                "host_link_aggregate_gbs": round(world * avg["host_bytes"] / (ms_per_step * 1e-3) / 1e9, 2),
+                "host_link_aggregate_frac": round(world * avg["host_bytes"] / (ms_per_step * 1e-3) / 1e9
+                                                  / copy_pk["aggregate_gbs"], 4),
             },
             "e2e": e2e,
         }
