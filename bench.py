@@ -9,8 +9,9 @@ with 8 KV heads x 4 query heads, head_dim 128, 32768 tokens of fp16 K/V in a
 pinned, device-mapped host slab, K ~ N(0,1) with 4 outlier channels per KV
 head scaled by exp(N(0,1)), INT4 group 32, Quest B0 4096 tokens (256 pages of
 16), dynamic top-p 0.95, sink 64, recent 256.  Seeded synthetic data.  A step
-is one layer-step; each timed step uses a fresh query, and L2 is flushed
-(512 MiB write) before every timed step, outside its CUDA events.
+is one layer-step; each timed step uses a fresh query, and the timed steps
+cycle through 12 copies of the layer (own slab, metadata and codes each), so
+that no step finds its data in L2 and no flush runs between steps.
 
 With N > 1 (torchrun) every rank runs its own copy of the request (its own
 slab on its own GPU, the same seeded data): request sharding, no collective
@@ -270,8 +271,10 @@ class DeviceStep:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         ws = tw.ops.select_layer_workspace_bytes(G, R, self.cand_pages, self.b0, block)
         self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)  # zero before the first call
-        self.flat_k = torch.empty((self.rows_cap, 128), dtype=torch.float16, device=device)
-        self.flat_v = torch.empty_like(self.flat_k)
+        # the staged twin's gathered rows (the fused path reads rows in place)
+        self.flat_k = (torch.empty((self.rows_cap, 128), dtype=torch.float16, device=device)
+                       if not fused else None)
+        self.flat_v = torch.empty_like(self.flat_k) if not fused else None
         self.cu = torch.zeros(G + 1, dtype=torch.int32, device=device)
         aws = tw.ops.decode_attention_workspace_bytes(G, R, self.per_group_cap)
         self.attn_ws = torch.zeros(aws, dtype=torch.uint8, device=device)
@@ -452,14 +455,24 @@ def run_ours(args) -> int:
     layer, queries = build_workload(tw, device, seed=0, n_queries=K + W + B, rho=rho)
     step = DeviceStep(tw, layer, device, fused=not args.staged, reuse=args.reuse,
                       n_steps=K + W + B + 1, numa=args.numa)
+    # Timed steps cycle through `cycle` copies of the layer (each its own slab,
+    # metadata and codes), so that a step finds none of its data in L2 without
+    # a flush between steps: with N > 1 a flush would leave each rank's host
+    # link idle for its duration and hand that bandwidth to the other ranks.
+    # Row reuse needs one layer's consecutive steps and keeps the flush.
+    cycle = 1 if args.reuse else max(1, args.layer_copies)
+    steps = [step] + [DeviceStep(tw, layer, device, fused=not args.staged, reuse=False,
+                                 n_steps=1, numa=args.numa) for _ in range(cycle - 1)]
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     torch.cuda.synchronize()
 
     for i in range(W):
-        step.load_query(queries[i].to(device))
-        step.run()
+        st = steps[i % cycle]
+        st.load_query(queries[i].to(device))
+        st.run()
     torch.cuda.synchronize()
-    step.err.zero_()
+    for st in steps:
+        st.err.zero_()
 
     names = ("select", "attention") if step.fused else ("select", "gather", "attention")
     per_step = []
@@ -473,15 +486,19 @@ def run_ours(args) -> int:
     # Timed steps: events only around the whole step, so that nothing sits
     # between the step's kernels (they overlap by programmatic dependent launch).
     for i in range(K):
-        step.load_query(q_dev[i])
-        l2_flush(flush)
+        st = steps[(W + i) % cycle]
+        st.load_query(q_dev[i])
+        if cycle == 1:
+            l2_flush(flush)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        step.run()
+        st.run()
         e.record()
         per_step.append((s, e))
-        byte_log.append((step.last_union_count.clone(), step.pages.clone()))
+        byte_log.append((st.last_union_count.clone(), st.pages.clone()))
     torch.cuda.synchronize()
+    if any(int(st.err.item()) != 0 for st in steps):
+        raise RuntimeError("device-side check failed in a timed step")
     if world > 1:
         torch.distributed.barrier()
     clocks = sampler.stop()
@@ -557,7 +574,8 @@ def run_ours(args) -> int:
         torch.distributed.barrier()
     slab_numa = {"requested": args.numa, "bound_node": step.slab.numa_node,
                  "page_node": step.slab.page_node(0)}
-    step.close()
+    for st in steps:
+        st.close()
 
     if rank == 0:
         peaks = measured_peaks()
@@ -589,7 +607,7 @@ def run_ours(args) -> int:
             "vs_baseline": None,
             "dtype": DTYPE_NOTE,
             "data": DATA_NOTE,
-            "config": cfg2_config(world, fused=step.fused, reuse=step.reuse, rho=rho),
+            "config": cfg2_config(world, fused=step.fused, reuse=step.reuse, rho=rho, cycle=cycle),
             "workload_stats": {"mean_union_rows": avg["union_rows"], "slab_numa": slab_numa},
             "clocks": clocks,
             "gpu_launches": step.launches_per_step * K * world,
@@ -664,14 +682,18 @@ DTYPE_NOTE = "fp16 K/V, fp32 math"
 DATA_NOTE = "synthetic (seeded splitmix64 normals; cfg2 shapes)"
 
 
-def cfg2_config(world: int, fused: bool = True, reuse: bool = False, rho: float = 0.0) -> dict:
+def cfg2_config(world: int, fused: bool = True, reuse: bool = False, rho: float = 0.0,
+                cycle: int = 12) -> dict:
     """The workload's config object, identical in both arms."""
     return {
         "workload": "cfg2: one layer, 8 KV x 4 Q heads, D 128, ctx 32768, fp16 K/V "
                     "in a pinned mapped host slab, 4 lognormal outlier channels, INT4 g32, "
                     "Quest B0 4096 tok, top-p 0.95, sink 64, recent 256",
-        "l2": "flushed before every timed step (512 MiB device write, then read back so "
-              "the remaining lines are clean; outside the events)",
+        "l2": (f"inputs larger than L2: the timed steps cycle through {cycle} copies of the "
+               "layer (own slab, metadata and INT4 codes each: ~200 MB of device data and "
+               "1.6 GB of host rows in the cycle), no flush" if cycle > 1 else
+               "flushed before every timed step (512 MiB device write, then read back so "
+               "the remaining lines are clean; outside the events)"),
         "parallelism": f"request-sharded replicas x{world}",
         "path": ("fused gather+attention" if fused else "staged gather then attention")
                 + (" + previous-token row reuse" if reuse else ""),
@@ -968,7 +990,7 @@ def run_reference(args) -> int:
         "vs_baseline": None,
         "dtype": DTYPE_NOTE,
         "data": DATA_NOTE,
-        "config": cfg2_config(world),
+        "config": cfg2_config(world, cycle=max(1, args.layer_copies)),
         "reference_execution": "rank 0 only, on all its host cores (CPU); the other ranks exit",
         "cpu_baseline": {"value": round(value, 4), "unit": "layer-steps/s",
                          "cores": torch.get_num_threads(), "kind": path.kind,
@@ -1450,6 +1472,10 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
+    ap.add_argument("--layer-copies", type=int, default=12,
+                    help="copies of the cfg2 layer the timed steps cycle through (inputs larger "
+                         "than L2, no flush between steps); 1 = one layer with an L2 flush "
+                         "before every timed step")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the cfg5 (head-sharded) and cfg4 (request-sharded batch) sub-runs "
                          "of the default workload")
