@@ -151,11 +151,13 @@ def link_peaks(tw, slab, device, world: int, reps: int = 6) -> dict:
       K and V rows, tw_gather_kv: SM 16-byte loads, the attention kernel's
       access path).
 
-    Per mechanism and repetition the ranks' own rates (bytes / own time) are
-    summed: the aggregate the host delivers while all ranks read (when the
-    host shares its bandwidth unevenly, world x bytes / the slowest rank's
-    time, also reported, is lower).  The best repetition is kept.  With world
-    = 1 all of them are the one GPU's peak."""
+    Per mechanism and repetition: aggregate = world x bytes / the slowest
+    rank's time, the rate at which every rank completes an equal transfer
+    (what a step of equal work per rank can use; it ends with its slowest
+    rank), and aggregate_sum_of_rates = the sum of the ranks' own rates, the
+    momentary total while all read (higher when the host shares its
+    bandwidth unevenly).  The best repetition is kept.  With world = 1 all of
+    them are the one GPU's peak."""
     nbytes = 256 << 20
     host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -193,9 +195,9 @@ def link_peaks(tw, slab, device, world: int, reps: int = 6) -> dict:
             single = max(single, rate)
             agg = max(agg, total)
             agg_slowest = max(agg_slowest, world * nb / (slowest * 1e-3) / 1e9)
-        res[name] = {"single_gbs": round(single, 2), "aggregate_gbs": round(agg, 2),
-                     "per_rank_gbs": round(agg / world, 2),
-                     "aggregate_slowest_gbs": round(agg_slowest, 2)}
+        res[name] = {"single_gbs": round(single, 2), "aggregate_gbs": round(agg_slowest, 2),
+                     "per_rank_gbs": round(agg_slowest / world, 2),
+                     "aggregate_sum_of_rates_gbs": round(agg, 2)}
     if int(err.item()) != 0:
         raise RuntimeError("mapped-read probe reported an invalid row")
     del host, dev, out_k, out_v, rows
@@ -639,8 +641,10 @@ def run_ours(args) -> int:
                 "link_peaks_note": ("copy = pinned H2D cudaMemcpyAsync (copy engine); mapped = "
                                     "sequential zero-copy SM reads of the mapped slab (the "
                                     "attention kernel's access path); all ranks at once after a "
-                                    "barrier: aggregate = the sum of the ranks' own rates, "
-                                    "aggregate_slowest = world x bytes / the slowest rank's time"),
+                                    "barrier, equal bytes each: aggregate = world x bytes / the "
+                                    "slowest rank's time (per_rank = aggregate / world, the "
+                                    "roofline denominator); aggregate_sum_of_rates = the sum of "
+                                    "the ranks' own rates"),
             },
             "roofline_step": {
                 "t_roof_us": round(t_roof_ms * 1e3, 2),
