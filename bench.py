@@ -578,6 +578,9 @@ def run_ours(args) -> int:
                  "page_node": step.slab.page_node(0)}
     for st in steps:
         st.close()
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extra_workloads:
+        extras = run_single_extras(tw, device, K, W, peaks_link["copy"]["per_rank_gbs"])
 
     if rank == 0:
         peaks = measured_peaks()
@@ -674,6 +677,7 @@ def run_ours(args) -> int:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         line.update(sharded)
+        line.update(extras)
         print(json.dumps(line), flush=True)
         if parity is not None and not parity["ok"]:
             raise RuntimeError(f"parity check failed: {parity}")
@@ -1248,6 +1252,150 @@ def run_sharded(args, tw, device, world: int, rank: int, link_peak: float | None
     return out
 
 
+def measure_cfg1(tw, device, K: int, W: int, link_peak: float | None) -> dict:
+    """cfg1, per-query-head Quest on one layer (32 / 8 heads, D 128, context 4096
+    fp16, 8 needle blocks per head, block 16, top-k 64 blocks, every row in
+    pinned host memory), through the reference's call sequence for that cache
+    (hi/mp.py:420-473): prepare_layer_selection, update_layer_flat_ragged (the
+    per-head gather and the append) and the varlen attention call.  Each step's
+    query is the layer's query plus seeded noise (0.25 N(0,1)), so that the
+    selections vary; L2 is flushed before every step, outside its events.  The
+    steps are timed twice: with the host waiting for each step, and issued
+    back to back behind a GPU sleep (device time per step, and the host's own
+    issue time per step)."""
+    from oracle import synth  # seeded synthetic inputs (test infrastructure)
+
+    G, R, L, sink, recent, block = 8, 4, 4096, 64, 256, 16
+    d = synth.make_layer(groups=G, heads_per_group=R, length=L, dtype="float16", seed=1,
+                         workload="needles", sink=sink, recent=recent, block=block, n_needles=8)
+    fraction = 0.27  # ceil(0.27 * 3777 eligible tokens / 16) = 64 pages (hi/quest_offload_cache.py:330-338)
+    cache = tw.QuestTopKOffloadedCache(
+        num_cache_entries=G, max_cache_len=L + 2 * K + W + 8, head_dim=128, num_query_heads_per_kv=R,
+        dtype=torch.float16, device=device, sink_tokens=sink, recent_tokens=recent, block_size=block,
+        budget_fraction=fraction, layer_batched_selection=True, layer_flat_ragged_execution=True)
+    entries = list(range(G))
+    cache.prefill_layer(key_states=d.keys.to(device), value_states=d.values.to(device), entries=entries)
+    gq = torch.Generator().manual_seed(29)
+    q_all = (d.queries.float()[None] + 0.25 * torch.randn(W + 2 * K, G, R, 128, generator=gq))
+    q_all = q_all.to(torch.float16).to(device)
+    ks = [d.key_new[g].view(1, 1, 1, 128).to(device) for g in range(G)]
+    vs = [d.value_new[g].view(1, 1, 1, 128).to(device) for g in range(G)]
+    cu_q = torch.arange(G * R + 1, dtype=torch.int32, device=device)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+
+    def one_step(i):
+        qs = [q_all[i, g].view(1, R, 1, 128) for g in range(G)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        cache.prepare_layer_selection(entries=entries, queries=qs)
+        ev[1].record()
+        k, v, cu, max_k, lengths = cache.update_layer_flat_ragged(
+            key_states=ks, value_states=vs, queries=qs, entries=entries)
+        ev[2].record()
+        tw.flash_attention_varlen_forward(q_all[i].reshape(G * R, 1, 128), k, v, cu_q, cu, 1, max_k)
+        ev[3].record()
+        return ev, sum(lengths) - G * R  # every row but the current token's
+
+    # (a) synchronous: the host waits for each step before issuing the next
+    sync_ms, sync_wall = [], 0.0
+    for i in range(W + K):
+        l2_flush(flush)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ev, _ = one_step(i)
+        ev[3].synchronize()
+        if i >= W:
+            sync_wall += time.perf_counter() - t0
+            sync_ms.append(ev[0].elapsed_time(ev[3]))
+    # (b) pipelined, as a decode loop issues its layers: no host wait between
+    # steps, the L2 flush queued on the stream before each step's first event
+    steps, host_rows = [], []
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e6 * K))  # ~1 ms of GPU time per step queued first: the host never waits
+    t0 = time.perf_counter()
+    issue_s = 0.0
+    for i in range(W + K, W + 2 * K):
+        l2_flush(flush)
+        t1 = time.perf_counter()
+        ev, n_rows = one_step(i)
+        issue_s += time.perf_counter() - t1
+        steps.append(ev)
+        host_rows.append(n_rows)
+    torch.cuda.synchronize()
+    dev_ms = [ev[0].elapsed_time(ev[3]) for ev in steps]
+    parts = [[ev[j].elapsed_time(ev[j + 1]) for j in range(3)] for ev in steps]
+    qs = [q_all[W + 2 * K - 1, g].view(1, R, 1, 128) for g in range(G)]
+    cache.synchronize()
+    # distinct rows of the last timed step's selection: per group the union of
+    # its heads' pages plus the sink and recent rows (what the gather reads)
+    cache.enable_selection_trace()
+    cache.prepare_layer_selection(entries=entries, queries=qs)
+    trace = cache.selection_trace()
+    step_id = max(t["decode_step"] for t in trace)
+    union = {}
+    for t in trace:
+        if t["decode_step"] == step_id:
+            union.setdefault(t["entry"], set()).update(t["selected_page_indices"])
+    n_prot = sink + (recent - 1)
+    distinct_rows = sum(len(u) * block + n_prot for u in union.values())
+    cache.close()
+    del flush
+    us = float(np.mean(dev_ms)) * 1e3
+    host_us = issue_s / K * 1e6
+    layout_bytes = float(np.mean(host_rows)) * 2 * 128 * 2
+    host_bytes = float(distinct_rows) * 2 * 128 * 2
+    gbs = host_bytes / (us * 1e-6) / 1e9
+    return {
+        "workload": ("cfg1: one layer, 32 / 8 heads, D 128, context 4096 fp16 with 8 needle blocks "
+                     "per head, per-query-head Quest top-k 64 blocks of 16, sink 64, recent 256, "
+                     "every row in pinned host memory"),
+        "calls": "prepare_layer_selection + update_layer_flat_ragged + flash_attention_varlen_forward",
+        "steps": K, "warmup": W,
+        "us_per_layer_step": round(us, 2),
+        "us_per_layer_step_note": "device time of a step issued without a host wait before it "
+                                  "(CUDA events from before the first call to after the "
+                                  "attention, mean over steps)",
+        "host_issue_us_per_layer_step": round(host_us, 2),
+        "host_issue_note": "host time to issue one step's three calls (the GPU busy meanwhile); "
+                           "a decode loop of such layers runs at max(device, host)",
+        "synchronous_us_per_layer_step": round(float(np.mean(sync_ms)) * 1e3, 2),
+        "synchronous_wall_us_per_layer_step": round(sync_wall / K * 1e6, 2),
+        "synchronous_note": "the host waits for each step before issuing the next, so the "
+                            "calls' host-side work is on the device timeline",
+        "host_bytes_per_step": host_bytes,
+        "host_bytes_note": "rows read over the host link: per group the union of its 4 heads' "
+                           "pages plus the sink and recent rows, each once (from the selection "
+                           "of one further step)",
+        "host_link_gbs": round(gbs, 2),
+        "frac_of_copy_peak": round(gbs / link_peak, 4) if link_peak else None,
+        "per_head_layout_bytes_per_step": layout_bytes,
+        "per_head_layout_note": "K + V rows written to the 32 per-head segments that "
+                                "update_layer_flat_ragged returns (each head's sink and recent "
+                                "rows and shared pages once per head)",
+        "calls_us": {n: round(float(np.mean([p[j] for p in parts])) * 1e3, 2)
+                     for j, n in enumerate(("prepare_layer_selection", "update_layer_flat_ragged",
+                                            "flash_attention_varlen_forward"))},
+        "timing": "CUDA events around the three calls of each step, L2 flushed before it "
+                  "(outside the events)",
+    }
+
+
+def run_single_extras(tw, device, K: int, W: int, link_peak: float | None) -> dict:
+    """cfg1 and cfg3 beside the 1-GPU headline line; a failure is recorded, not raised."""
+    out = {}
+    try:
+        out["cfg1"] = measure_cfg1(tw, device, min(K, 20), W, link_peak)
+    except Exception as exc:  # recorded in the line: the headline stands on its own
+        out["cfg1"] = {"error": f"{type(exc).__name__}: {exc}"}
+    try:
+        c3 = measure_cfg3(tw, device, "cfg3", reuse=False)
+        c3.pop("metric", None)
+        out["cfg3"] = c3
+    except Exception as exc:
+        out["cfg3"] = {"error": f"{type(exc).__name__}: {exc}"}
+    return out
+
+
 CFG3 = dict(layers=32, hidden=4096, heads=32, kv_heads=8, intermediate=14336, vocab=128256,
             length=32768, b0_tokens=2048, top_p=0.95, int4_group=32, resident_heads=(0, 1),
             rope_theta=500000.0, tokens=32)
@@ -1357,24 +1505,18 @@ class Llama8BDecoder:
         return logits.argmax().view(1)
 
 
-def run_cfg3(args) -> int:
-    """Full-model decode TPOT (cfg3: Llama-3-8B shape, 25 % of KV heads resident) on one GPU, timed as the
-    reference times it (scripts/run_ruler_partial_h2d_tpot_case_v1.py:1303-1323):
-    decode step D1 is the warm-up, then a synchronized wall over D2..D32."""
-    _, rank, local = dist_env()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if rank != 0:
-        return 0
-    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
-    ref3b = args.workload == "ref3b"
+def measure_cfg3(tw, device, workload: str = "cfg3", reuse: bool = False) -> dict:
+    """Full-model decode TPOT (cfg3: Llama-3-8B shape, 25 % of KV heads resident; or ref3b) on one GPU,
+    timed as the reference times it (scripts/run_ruler_partial_h2d_tpot_case_v1.py:1303-1323):
+    decode step D1 is the warm-up, then a synchronized wall over D2..D32.  Returns the JSON line."""
+    ref3b = workload == "ref3b"
     C = CFG_REF3B if ref3b else CFG3
     n_tok = C["tokens"]
-    model = Llama8BDecoder(tw, device, reuse=args.reuse, extra_tokens=n_tok + 4, cfg=C)
+    model = Llama8BDecoder(tw, device, reuse=reuse, extra_tokens=n_tok + 4, cfg=C)
     token = torch.zeros(1, dtype=torch.int64, device=device)
     token = model.step(token)  # D1
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(device.index)
     sampler.start()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
@@ -1418,7 +1560,7 @@ def run_cfg3(args) -> int:
     hbm_peak = peaks.get("hbm_gbs") or 6650.0
     del flush
     line = {
-        "metric": METRIC, "workload": args.workload,
+        "metric": METRIC, "workload": workload,
         "value": round(steps / wall, 3), "unit": "tokens/s",
         "ms_per_token": round(wall / steps * 1e3, 4),
         "device_ms_per_token": round(dev_ms / steps, 4),
@@ -1435,7 +1577,7 @@ def run_cfg3(args) -> int:
                                 "cfg3: 32 layers, 32/8 heads, D 128, hidden 4096, MLP 14336, ctx 32768, "
                                 "2 of 8 KV heads per layer GPU-resident, B0 2048, top-p 0.95, INT4 g32"),
                    "timing": "D1 warm-up, synchronized wall over D2..D32 (the reference's TPOT protocol)",
-                   "row_reuse": bool(args.reuse),
+                   "row_reuse": bool(reuse),
                    "model_gemms": "torch / cuBLAS (o_proj, MLP, LM head); q/k/v projection + RoPE is "
                                   "tw_qkv_rope"},
         "clocks": clocks,
@@ -1457,13 +1599,25 @@ def run_cfg3(args) -> int:
                     "not this hardware: resident zero-copy stack 69.137 ms/token (exact INT4 path), "
                     "55.939 ms/token (direct INT4 QK), 30.098 ms/token (its latest preset, source not "
                     "in the mirror)"}
-    if args.reuse:
+    if reuse:
         rows = model.cache.resident_reuse_trace()
         rows = [r for r in rows if r["decode_step"] > 1]
         hist = sum(r["history_rows"] for r in rows)
         line["row_reuse_hit_ratio"] = round(sum(r["hit_rows"] for r in rows) / max(1, hist), 4)
-    print(json.dumps(line), flush=True)
     model.cache.close()
+    del model
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_cfg3(args) -> int:
+    _, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if rank != 0:
+        return 0
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    print(json.dumps(measure_cfg3(tw, device, args.workload, args.reuse)), flush=True)
     return 0
 
 
@@ -1483,6 +1637,9 @@ def main() -> int:
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the cfg5 (head-sharded) and cfg4 (request-sharded batch) sub-runs "
                          "of the default workload")
+    ap.add_argument("--no-extra-workloads", action="store_true",
+                    help="skip the cfg1 (per-head Quest layer) and cfg3 (full-model decode) "
+                         "sub-runs of the 1-GPU line")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5", "ref3b"], default="cfg2",
                     help="cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
                          "decode, TPOT), cfg4 (request-sharded batch of 16 requests), cfg5 "

@@ -266,6 +266,10 @@ int tw_gather_union(const void* slab_k, const void* slab_v, const uint64_t* entr
  * [recent_start, old_length) then the group's current token, each head one
  * segment of the flat layout (segment s = g*R + r, equal lengths
  * seg_len = sink_end + k*block_size + (old_length - recent_start) + 1).
+ * Each distinct source row of a group (its sink and recent rows, and a page
+ * named by several heads or twice by one) is read once and written to every
+ * segment holding it; pages may come in any order.  A page id < 0 or a row at
+ * or beyond old_length sets TW_ERR_INVALID_INDEX in error_flag and writes zeros.
  * Replaces _selected_positions + update_layer_flat_ragged packing
  * (hi/quest_offload_cache.py:403-511, :724-987) and the per-entry pack of update
  * (:578-630). */

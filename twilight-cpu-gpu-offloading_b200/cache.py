@@ -408,8 +408,9 @@ class QuestTopKOffloadedCache:
         first = _contiguous_entries(entries)
         if budget == 0:
             return None, 0, w
-        q = torch.stack([query[0, :, 0] for query in queries], dim=0).float().contiguous()
         G = len(entries)
+        # [1, R, 1, D] each (validated) -> [G, R, D] fp32
+        q = torch.cat(queries, dim=0).view(G, self.num_query_heads_per_kv, HEAD_DIM).float()
         start = self._phase_start()
         scores = ops.quest_score(q, self._page_min[first:first + G], self._page_max[first:first + G],
                                  candidate_pages)
@@ -538,17 +539,28 @@ class QuestTopKOffloadedCache:
         first = entries[0]
         G = len(entries)
         pages, budget, w = self._quest_pages_for(entries, queries, old_length)
-        k_new = torch.cat([k[0, 0] for k in key_states], dim=0)
-        v_new = torch.cat([v[0, 0] for v in value_states], dim=0)
+        k_new = torch.cat(key_states, dim=0).view(G, HEAD_DIM)
+        v_new = torch.cat(value_states, dim=0).view(G, HEAD_DIM)
         out_k, out_v, seg_len = self._quest_gather(first, G, pages, budget, w, old_length, k_new, v_new)
         self._append_rows(first, G, old_length, k_new, v_new)
         R = self.num_query_heads_per_kv
         total = seg_len * G * R
-        cu = torch.arange(0, G * R + 1, dtype=torch.int32, device=self.device) * seg_len
+        cu = self._equal_cu_seqlens(G * R, seg_len)
         lengths = tuple([seg_len] * (G * R))
         for g, entry in enumerate(entries):
             self._last_query_head_lengths[entry] = tuple([seg_len] * R)
         return out_k.view(total, 1, HEAD_DIM), out_v.view(total, 1, HEAD_DIM), cu, seg_len, lengths
+
+    def _equal_cu_seqlens(self, segments: int, seg_len: int) -> torch.Tensor:
+        """arange(segments + 1) * seg_len as int32 on the device, kept for the
+        next call with the same shape (segment lengths stay fixed once the
+        recent window is full)."""
+        key = (segments, seg_len)
+        cached = getattr(self, "_cu_cache", None)
+        if cached is None or cached[0] != key:
+            cu = torch.arange(0, segments + 1, dtype=torch.int32, device=self.device) * seg_len
+            self._cu_cache = (key, cu)
+        return self._cu_cache[1]
 
     def _advance_layer(self, entries: list[int]) -> int:
         olds = []

@@ -367,55 +367,84 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
   __threadfence();
 
   // Last split: per-head max and normaliser (warp per head), then the
-  // weighted sum of the partial outputs (threads over (head, channel)).
+  // weighted sum of the partial outputs.  A thread owns one float4 column
+  // (head r, channels 4*d4..4*d4+3) and every kTpp-th split; the kTpp threads
+  // of a column are adjacent lanes, summed by a shuffle tree at the end.
   const float* ml = ws.part_ml + (int64_t)s * max_splits * R * 2;
   const float* po_all = ws.part_o + (int64_t)s * max_splits * R * kHeadDim;
-  for (int r = warp; r < R; r += kWarps) {
-    float M = -CUDART_INF_F;
-    for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(ml + ((int64_t)j * R + r) * 2));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.0f;
-    for (int j = lane; j < nsplit; j += 32) {
-      const float* e = ml + ((int64_t)j * R + r) * 2;
-      L += __ldcg(e + 1) * weight(__ldcg(e), M);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    if (lane == 0) {
-      s_M[r] = M;
-      s_L[r] = L;
-    }
-  }
-  __syncthreads();
-  // Weighted sum of the partial outputs.  A thread owns one float4 column
-  // (head r, channels 4*d4..4*d4+3) and every kTpp-th split of a chunk; the
-  // split weights of the chunk are computed once into shared memory, and the
-  // unrolled loop keeps 8 independent partial loads in flight per thread.  The
-  // kTpp threads of a column are adjacent lanes, summed by a shuffle tree.
   constexpr int kPairs = R * (kHeadDim / 4);
   constexpr int kTpp = kAttnThreads / kPairs >= 8 ? 8
                        : kAttnThreads / kPairs >= 4 ? 4
                        : kAttnThreads / kPairs >= 2 ? 2 : 1;
   static_assert(kPairs <= kAttnThreads, "one float4 column per thread at most");
+  static_assert(R <= kWarps, "one warp per head in the merge");
   const int pair = tid / kTpp;
   const int sub = tid % kTpp;
   const bool has_pair = pair < kPairs;
   const int pr = has_pair ? pair / (kHeadDim / 4) : 0;
   const int d4 = pair % (kHeadDim / 4);
+  const int64_t jstride = (int64_t)R * kHeadDim / 4;
   float4 acc4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  for (int j0 = 0; j0 < nsplit; j0 += kMergeChunk) {
-    const int n = min(kMergeChunk, nsplit - j0);
-    for (int idx = tid; idx < n * R; idx += kAttnThreads) {
-      const int jj = idx / R, rr = idx % R;
-      s_wt[jj][rr] = weight(__ldcg(ml + ((int64_t)(j0 + jj) * R + rr) * 2), s_M[rr]);
+  if (nsplit <= kMergeChunk) {
+    // One pass (every split's weight fits s_wt): each thread issues its first
+    // kMergeAhead partial loads, then warp r reads head r's (m, l) pairs once
+    // into registers for the max, the normaliser and the weights, while those
+    // loads are in flight.  Same arithmetic and order as the chunked path.
+    constexpr int kMergeAhead = 8;
+    constexpr int kPerLane = kMergeChunk / 32;
+    const float4* col = reinterpret_cast<const float4*>(po_all + (int64_t)pr * kHeadDim) + d4;
+    float4 pre[kMergeAhead];
+#pragma unroll
+    for (int u = 0; u < kMergeAhead; ++u) {
+      const int jj = sub + u * kTpp;
+      pre[u] = (has_pair && jj < nsplit) ? __ldcg(col + jj * jstride) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    if (warp < R) {
+      const int r = warp;
+      float2 e[kPerLane];
+#pragma unroll
+      for (int k = 0; k < kPerLane; ++k) {
+        const int j = lane + 32 * k;
+        e[k] = j < nsplit ? __ldcg(reinterpret_cast<const float2*>(ml + ((int64_t)j * R + r) * 2))
+                          : make_float2(-CUDART_INF_F, 0.0f);
+      }
+      float M = -CUDART_INF_F;
+#pragma unroll
+      for (int k = 0; k < kPerLane; ++k) M = fmaxf(M, e[k].x);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kPerLane; ++k) {
+        const int j = lane + 32 * k;
+        const float w = weight(e[k].x, M);
+        if (j < nsplit) {
+          L += e[k].y * w;
+          s_wt[j][r] = w;
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane == 0) {
+        s_M[r] = M;
+        s_L[r] = L;
+      }
     }
     __syncthreads();
     if (has_pair) {
-      const float4* col = reinterpret_cast<const float4*>(po_all + ((int64_t)j0 * R + pr) * kHeadDim) + d4;
-      const int64_t jstride = (int64_t)R * kHeadDim / 4;
+#pragma unroll
+      for (int u = 0; u < kMergeAhead; ++u) {
+        const int jj = sub + u * kTpp;
+        if (jj < nsplit) {
+          const float w = s_wt[jj][pr];
+          acc4.x = fmaf(w, pre[u].x, acc4.x);
+          acc4.y = fmaf(w, pre[u].y, acc4.y);
+          acc4.z = fmaf(w, pre[u].z, acc4.z);
+          acc4.w = fmaf(w, pre[u].w, acc4.w);
+        }
+      }
 #pragma unroll 8
-      for (int jj = sub; jj < n; jj += kTpp) {
+      for (int jj = sub + kMergeAhead * kTpp; jj < nsplit; jj += kTpp) {
         const float w = s_wt[jj][pr];
         const float4 o = __ldcg(col + jj * jstride);
         acc4.x = fmaf(w, o.x, acc4.x);
@@ -424,7 +453,48 @@ attention_kernel(Rows rows, const T* __restrict__ q, float scale_log2, int max_s
         acc4.w = fmaf(w, o.w, acc4.w);
       }
     }
+  } else {
+    for (int r = warp; r < R; r += kWarps) {
+      float M = -CUDART_INF_F;
+      for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(ml + ((int64_t)j * R + r) * 2));
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.0f;
+      for (int j = lane; j < nsplit; j += 32) {
+        const float* e = ml + ((int64_t)j * R + r) * 2;
+        L += __ldcg(e + 1) * weight(__ldcg(e), M);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane == 0) {
+        s_M[r] = M;
+        s_L[r] = L;
+      }
+    }
     __syncthreads();
+    // Chunks of kMergeChunk splits: their weights are computed once into
+    // shared memory; the unrolled loop keeps 8 partial loads in flight.
+    for (int j0 = 0; j0 < nsplit; j0 += kMergeChunk) {
+      const int n = min(kMergeChunk, nsplit - j0);
+      for (int idx = tid; idx < n * R; idx += kAttnThreads) {
+        const int jj = idx / R, rr = idx % R;
+        s_wt[jj][rr] = weight(__ldcg(ml + ((int64_t)(j0 + jj) * R + rr) * 2), s_M[rr]);
+      }
+      __syncthreads();
+      if (has_pair) {
+        const float4* col = reinterpret_cast<const float4*>(po_all + ((int64_t)j0 * R + pr) * kHeadDim) + d4;
+#pragma unroll 8
+        for (int jj = sub; jj < n; jj += kTpp) {
+          const float w = s_wt[jj][pr];
+          const float4 o = __ldcg(col + jj * jstride);
+          acc4.x = fmaf(w, o.x, acc4.x);
+          acc4.y = fmaf(w, o.y, acc4.y);
+          acc4.z = fmaf(w, o.z, acc4.z);
+          acc4.w = fmaf(w, o.w, acc4.w);
+        }
+      }
+      __syncthreads();
+    }
   }
 #pragma unroll
   for (int off = kTpp / 2; off > 0; off >>= 1) {

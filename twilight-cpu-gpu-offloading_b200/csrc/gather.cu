@@ -200,62 +200,139 @@ gather_union_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ 
 
 // Quest per-query-head layout: segment s = g*R + r has seg_len rows:
 // [0, sink_end) then the k pages' rows then [recent_start, old_length) then the
-// current token of group g.
+// current token of group g.  The R heads of a group share their sink and
+// recent rows and many of their pages, so each distinct source row is read
+// over the host link once per group and written to every segment holding it.
+// One warp per work item of a group (two rows per 16-byte load, 16 rows in
+// flight per warp):
+//  - page slot (r, j), item r*k + j: the warp reads the group's R*k page ids
+//    and owns the page when no earlier slot names it; the owner loads the
+//    page's rows once and writes them to every slot naming it (pages in any
+//    order, repeats included);
+//  - a chunk of 16 protected rows (the sink rows, then the recent window):
+//    loaded once, written to the R segments;
+//  - the current token: written to the R segments.
+// A group with more than kQuestShareMax page slots does not share pages (each
+// slot loads its own).  A page id < 0 or a row at or beyond old_length sets
+// TW_ERR_INVALID_INDEX and writes zeros.
+constexpr int kQuestShareMax = 1024;
+constexpr int kQuestWarps = kGatherThreads / 32;
+
 template <int kVec>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_quest_kernel(const uint4* __restrict__ slab_k, const uint4* __restrict__ slab_v,
                     const unsigned long long* __restrict__ dirs, int64_t n_entries,
-                    int64_t max_len, int first_entry, int R, int64_t old_length, int64_t sink_end,
-                    int64_t recent_start, int sink, int block, const int32_t* __restrict__ pages,
-                    int k_pages, const uint4* __restrict__ cur_k, const uint4* __restrict__ cur_v,
+                    int64_t max_len, int first_entry, int groups, int R, int64_t old_length,
+                    int64_t sink_end, int64_t recent_start, int sink, int block,
+                    const int32_t* __restrict__ pages, int k_pages,
+                    const uint4* __restrict__ cur_k, const uint4* __restrict__ cur_v,
                     uint4* __restrict__ out_k, uint4* __restrict__ out_v, int64_t seg_len,
-                    int64_t total, int32_t* error_flag) {
-  constexpr int rows_per_cta = kGatherThreads / kVec;
-  const int sub_row = threadIdx.x / kVec;
-  const int col = threadIdx.x % kVec;
-  const int64_t stride = (int64_t)gridDim.x * rows_per_cta;
+                    int32_t* error_flag) {
+  static_assert(kVec == 16, "a half-warp moves one row per load");
+  constexpr int kPairs = 8;  // row pairs in flight per warp
+  const int lane = threadIdx.x & 31;
+  const int half = lane >> 4;
+  const int l16 = lane & 15;
   const int64_t sel = (int64_t)k_pages * block;
-  for (int64_t base = (int64_t)blockIdx.x * rows_per_cta + sub_row; base < total;
-       base += stride * kGatherUnroll) {
-    uint4 kv[kGatherUnroll], vv[kGatherUnroll];
-    int64_t t[kGatherUnroll];
+  const int64_t n_prot = sink_end + (old_length - recent_start);
+  const int64_t n_chunks = (n_prot + 2 * kPairs - 1) / (2 * kPairs);
+  const int64_t slots = (int64_t)R * k_pages;
+  const int64_t per_group = slots + n_chunks + 1;
+  const int64_t item = (int64_t)blockIdx.x * kQuestWarps + (threadIdx.x >> 5);
+  if (item >= per_group * groups) return;
+  const int g = (int)(item / per_group);
+  const int64_t w = item - (int64_t)g * per_group;
+  const int64_t seg0 = (int64_t)g * R;
+  const uint4 *kb, *vb;
+  entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec, kb, vb);
+
+  if (w == per_group - 1) {  // the current token
+    const uint4 ck = cur_k[(int64_t)g * kVec + l16];
+    const uint4 cv = cur_v[(int64_t)g * kVec + l16];
+    for (int r = half; r < R; r += 2) {
+      const int64_t t = (seg0 + r) * seg_len + seg_len - 1;
+      out_k[t * kVec + l16] = ck;
+      out_v[t * kVec + l16] = cv;
+    }
+    return;
+  }
+  uint4 kv[kPairs], vv[kPairs];
+  if (w >= slots) {  // protected rows: chunk c covers protected rows [16c, 16c + 16)
+    const int64_t t0 = (w - slots) * 2 * kPairs;
 #pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      t[u] = base + u * stride;
-      if (t[u] >= total) continue;
-      const int64_t s = t[u] / seg_len;
-      const int64_t i = t[u] - s * seg_len;
-      const int g = (int)(s / R);
-      int64_t pos;
-      if (i < sink_end) {
-        pos = i;
-      } else if (i < sink_end + sel) {
-        const int64_t j = i - sink_end;
-        pos = (int64_t)sink + (int64_t)pages[s * k_pages + j / block] * block + (j % block);
-      } else if (i < seg_len - 1) {
-        pos = recent_start + (i - sink_end - sel);
-      } else {
-        pos = -1;  // current token
-      }
-      if (pos < 0) {
-        kv[u] = cur_k[(int64_t)g * kVec + col];
-        vv[u] = cur_v[(int64_t)g * kVec + col];
-      } else if (pos >= old_length) {
-        if (error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
-        kv[u] = make_uint4(0, 0, 0, 0);
-        vv[u] = kv[u];
-      } else {
-        const uint4 *kb, *vb;
-        entry_rows(slab_k, slab_v, dirs, n_entries, max_len, (int64_t)first_entry + g, kVec, kb, vb);
-        kv[u] = __ldcs(kb + pos * kVec + col);
-        vv[u] = __ldcs(vb + pos * kVec + col);
+    for (int q = 0; q < kPairs; ++q) {
+      const int64_t t = t0 + 2 * q + half;
+      if (t < n_prot) {
+        const int64_t pos = t < sink_end ? t : recent_start + (t - sink_end);
+        kv[q] = __ldcs(kb + pos * kVec + l16);
+        vv[q] = __ldcs(vb + pos * kVec + l16);
       }
     }
+    for (int r = 0; r < R; ++r) {
 #pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      if (t[u] >= total) continue;
-      out_k[t[u] * kVec + col] = kv[u];
-      out_v[t[u] * kVec + col] = vv[u];
+      for (int q = 0; q < kPairs; ++q) {
+        const int64_t t = t0 + 2 * q + half;
+        if (t < n_prot) {
+          const int64_t i = t < sink_end ? t : t + sel;
+          const int64_t o = ((seg0 + r) * seg_len + i) * kVec + l16;
+          out_k[o] = kv[q];
+          out_v[o] = vv[q];
+        }
+      }
+    }
+    return;
+  }
+
+  // page slot w = (r, j) of the group
+  const int32_t* gp = pages + seg0 * k_pages;
+  const int32_t page = gp[w];
+  const bool share = slots <= kQuestShareMax;
+  if (share) {
+    for (int64_t f0 = 0; f0 < w; f0 += 32) {  // an earlier slot naming the page owns it
+      const int64_t f = f0 + lane;
+      if (__any_sync(0xffffffffu, f < w && gp[f] == page)) return;
+    }
+  }
+  const int64_t pos0 = (int64_t)sink + (int64_t)page * block;
+  for (int b0 = 0; b0 < block; b0 += 2 * kPairs) {
+    bool bad = false;
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) {
+      const int row = b0 + 2 * q + half;
+      kv[q] = make_uint4(0, 0, 0, 0);
+      vv[q] = kv[q];
+      if (row < block) {
+        const int64_t pos = pos0 + row;
+        if (page >= 0 && pos < old_length) {
+          kv[q] = __ldcs(kb + pos * kVec + l16);
+          vv[q] = __ldcs(vb + pos * kVec + l16);
+        } else {
+          bad = true;
+        }
+      }
+    }
+    if (bad && error_flag) atomicExch(error_flag, TW_ERR_INVALID_INDEX);
+    // every slot from w on naming the page (w itself included)
+    for (int64_t f0 = share ? w : 0; f0 < (share ? slots : 1); f0 += 32) {
+      const int64_t f = f0 + lane;
+      unsigned m = share ? __ballot_sync(0xffffffffu, f < slots && gp[f] == page) : 1u;
+      while (m) {
+        const int bit = __ffs(m) - 1;
+        m &= m - 1;
+        const int64_t ff = share ? f0 + bit : w;
+        const int64_t rr = ff / k_pages;
+        const int64_t jj = ff - rr * k_pages;
+        const int64_t base = (seg0 + rr) * seg_len + sink_end + jj * block + b0;
+#pragma unroll
+        for (int q = 0; q < kPairs; ++q) {
+          const int row = 2 * q + half;
+          if (b0 + row < block) {
+            const int64_t o = (base + row) * kVec + l16;
+            out_k[o] = kv[q];
+            out_v[o] = vv[q];
+          }
+        }
+      }
     }
   }
 }
@@ -373,13 +450,16 @@ extern "C" int tw_gather_quest_heads(const void* slab_k, const void* slab_v,
     return TW_ERR_BAD_ARG;
   const int64_t seg_len =
       sink_end + (int64_t)k_pages * block_size + (old_length - recent_start) + 1;
-  const int64_t total = seg_len * groups * heads_per_group;
   constexpr int kVec = kHeadDim * 2 / 16;
-  const int grid = gather_grid(total, kGatherThreads / kVec);
-  gather_quest_kernel<kVec><<<grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
+  const int64_t n_prot = sink_end + (old_length - recent_start);
+  const int64_t per_group = (int64_t)heads_per_group * k_pages + (n_prot + 15) / 16 + 1;
+  const int64_t items = per_group * groups;
+  const int64_t grid = (items + kQuestWarps - 1) / kQuestWarps;
+  if (grid > 0x7fffffffLL) return TW_ERR_UNSUPPORTED;
+  gather_quest_kernel<kVec><<<(unsigned)grid, kGatherThreads, 0, (cudaStream_t)stream>>>(
       (const uint4*)slab_k, (const uint4*)slab_v, (const unsigned long long*)entry_dirs, n_entries,
-      max_len, first_entry, heads_per_group,
-      old_length, sink_end, recent_start, sink, block_size, pages, k_pages, (const uint4*)cur_k,
-      (const uint4*)cur_v, (uint4*)out_k, (uint4*)out_v, seg_len, total, error_flag);
+      max_len, first_entry, groups, heads_per_group, old_length, sink_end, recent_start, sink,
+      block_size, pages, k_pages, (const uint4*)cur_k, (const uint4*)cur_v, (uint4*)out_k,
+      (uint4*)out_v, seg_len, error_flag);
   return check_launch();
 }
