@@ -1380,6 +1380,38 @@ def measure_cfg1(tw, device, K: int, W: int, link_peak: float | None) -> dict:
     }
 
 
+def copy_peak_gbs(device, reps: int = 6) -> float:
+    """Pinned host -> device cudaMemcpyAsync of 256 MiB, best of reps (GB/s)."""
+    nbytes = 256 << 20
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    best = max(nbytes / (_timed_ms(lambda: dev.copy_(host, non_blocking=True)) * 1e-3) / 1e9
+               for _ in range(reps))
+    del host, dev
+    return best
+
+
+def run_cfg1(args) -> int:
+    """cfg1 alone on one GPU: the per-query-head Quest layer-step (measure_cfg1)."""
+    _, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if rank != 0:
+        return 0
+    tw = importlib.import_module("twilight-cpu-gpu-offloading_b200")
+    peak = copy_peak_gbs(device)
+    res = measure_cfg1(tw, device, args.steps, args.warmup, peak)
+    line = {"metric": METRIC, "workload": "cfg1", "value": round(1e6 / res["us_per_layer_step"], 3),
+            "unit": "layer-steps/s", "n_gpus": 1, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "fp16 K/V, fp32 math",
+            "data": "synthetic (seeded splitmix64 normals with needle blocks; cfg1 shapes)",
+            "copy_peak_gbs": round(peak, 2), **res}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_single_extras(tw, device, K: int, W: int, link_peak: float | None) -> dict:
     """cfg1 and cfg3 beside the 1-GPU headline line; a failure is recorded, not raised."""
     out = {}
@@ -1640,8 +1672,10 @@ def main() -> int:
     ap.add_argument("--no-extra-workloads", action="store_true",
                     help="skip the cfg1 (per-head Quest layer) and cfg3 (full-model decode) "
                          "sub-runs of the 1-GPU line")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5", "ref3b"], default="cfg2",
-                    help="cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "ref3b"],
+                    default="cfg2",
+                    help="cfg1 (per-query-head Quest layer, 4096 tokens), "
+                         "cfg2 (default, the metric's configuration), cfg3 (full Llama-3-8B-shaped "
                          "decode, TPOT), cfg4 (request-sharded batch of 16 requests), cfg5 "
                          "(head-sharded 70B layer) or ref3b (the same decode loop on the "
                          "reference's own published setup: Llama-3.2-3B shape, B0 8192, top-p 0.9)")
@@ -1659,6 +1693,8 @@ def main() -> int:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "cfg1":
+        return run_cfg1(args)
     if args.workload == "cfg5":
         return run_cfg5(args)
     if args.workload in ("cfg3", "ref3b"):
