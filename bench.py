@@ -233,8 +233,6 @@ class DeviceStep:
         self.tw = tw
         self.fused = fused
         self.reuse = reuse
-        if reuse and not fused:
-            raise ValueError("row reuse is timed on the fused path")
         self.lib = tw.load_library()
         G, R, L = CFG["groups"], CFG["heads"], CFG["length"]
         self.G, self.R, self.L = G, R, L
@@ -273,10 +271,11 @@ class DeviceStep:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         ws = tw.ops.select_layer_workspace_bytes(G, R, self.cand_pages, self.b0, block)
         self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)  # zero before the first call
-        # the staged twin's gathered rows (the fused path reads rows in place)
+        # the staged twin's gathered rows (the fused path reads rows in place;
+        # with row reuse the staged gather writes into the kept-row slot)
         self.flat_k = (torch.empty((self.rows_cap, 128), dtype=torch.float16, device=device)
-                       if not fused else None)
-        self.flat_v = torch.empty_like(self.flat_k) if not fused else None
+                       if not fused and not reuse else None)
+        self.flat_v = torch.empty_like(self.flat_k) if self.flat_k is not None else None
         self.cu = torch.zeros(G + 1, dtype=torch.int32, device=device)
         aws = tw.ops.decode_attention_workspace_bytes(G, R, self.per_group_cap)
         self.attn_ws = torch.zeros(aws, dtype=torch.uint8, device=device)
@@ -351,8 +350,13 @@ class DeviceStep:
             log = self.row_log[min(self.t, self.row_log.shape[0] - 1)]
             kw = {} if self.t == 0 else dict(prev_tag=self.t, prev_k=self.rows2[prv, 0],
                                              prev_v=self.rows2[prv, 1])
-            reuse = tw.ops.row_reuse(self.row_map, self.t + 1, next_k=self.rows2[cur, 0],
-                                     next_v=self.rows2[cur, 1], row_counts=log, **kw)
+            if self.fused:
+                reuse = tw.ops.row_reuse(self.row_map, self.t + 1, next_k=self.rows2[cur, 0],
+                                         next_v=self.rows2[cur, 1], row_counts=log, **kw)
+            else:  # the staged gather's output rows are the kept rows
+                reuse = tw.ops.row_reuse(self.row_map, self.t + 1, row_counts=log, **kw)
+                self.flat_k = self.rows2[cur, 0].view(self.rows_cap, 128)
+                self.flat_v = self.rows2[cur, 1].view(self.rows_cap, 128)
             self.t += 1
         self.last_union_count = union_count
         if self.fused and not ev:
@@ -391,8 +395,8 @@ class DeviceStep:
                 self.L,
                 self.union_pos.data_ptr(), self.max_len, self.union_count.data_ptr(),
                 self.k_new.data_ptr(), self.v_new.data_ptr(), 128, 0, self.flat_k.data_ptr(),
-                self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(), None,
-                st), "gather_union")
+                self.flat_v.data_ptr(), self.rows_cap, self.cu.data_ptr(), self.err.data_ptr(),
+                None if reuse is None else ctypes.byref(reuse), st), "gather_union")
             if "gather" in ev:
                 ev["gather"][1].record()
                 ev["attention"][0].record()
