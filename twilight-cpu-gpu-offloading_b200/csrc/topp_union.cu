@@ -610,7 +610,7 @@ size_t merge_region_bytes(int groups, int n_pages, int block) {
 struct TopKShared {
   uint32_t hist[256];
   uint32_t scratch[32];
-  uint32_t prefix, remaining;
+  uint32_t prefix, remaining, resolved;
 };
 
 // Dynamic shared memory: the top-k state | scores f32[max(P, words)] (keys
@@ -635,9 +635,13 @@ __device__ void topk_row(const uint32_t* keys, int P, int k, int32_t* s_pages, i
   if (tid == 0) {
     sh.prefix = 0u;
     sh.remaining = (uint32_t)k;
+    sh.resolved = 0u;
   }
   __syncthreads();
   uint32_t mask = 0u;
+  // A pass whose crossing bin holds exactly the keys still needed resolves
+  // the selection: every key whose masked prefix is at or above it is taken
+  // (k keys in all), the set the remaining passes would also give.
 #pragma unroll 1
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
@@ -672,6 +676,7 @@ __device__ void topk_row(const uint32_t* keys, int P, int k, int32_t* s_pages, i
           if (acc + local[j] >= need) {
             sh.prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
             sh.remaining = need - acc;
+            sh.resolved = (local[j] == need - acc) ? 1u : 0u;
             break;
           }
           acc += local[j];
@@ -680,16 +685,18 @@ __device__ void topk_row(const uint32_t* keys, int P, int k, int32_t* s_pages, i
     }
     mask |= 255u << shift;
     __syncthreads();
+    if (sh.resolved) break;
   }
   const uint32_t kth = sh.prefix;
   const uint32_t ties = sh.remaining;
-  // keys above kth and the first `ties` keys equal to it, in index order
+  // masked keys above kth and the first `ties` masked keys equal to it, in
+  // index order (mask covers the passes run)
   const int seg = (P + blockDim.x - 1) / blockDim.x;
   const int beg = min(P, tid * seg);
   const int end = min(P, beg + seg);
   uint32_t gt = 0u, eq = 0u;
   for (int i = beg; i < end; ++i) {
-    const uint32_t key = keys[i];
+    const uint32_t key = keys[i] & mask;
     gt += key > kth;
     eq += key == kth;
   }
@@ -699,7 +706,7 @@ __device__ void topk_row(const uint32_t* keys, int P, int k, int32_t* s_pages, i
   const uint32_t base = block_exclusive_scan(gt + take_eq, sh.scratch, &total);
   uint32_t slot = base, eq_seen = 0u;
   for (int i = beg; i < end; ++i) {
-    const uint32_t key = keys[i];
+    const uint32_t key = keys[i] & mask;
     bool take = key > kth;
     if (key == kth) {
       take = eq_seen < take_eq;
@@ -940,7 +947,10 @@ select_rows_kernel(SelectArgs a) {
       gbits[w_beg + w] = 0u;
     }
     uint32_t ctotal;
-    block_exclusive_scan(mine, s_topk.scratch, &ctotal);
+    {
+      const uint32_t excl = block_exclusive_scan(mine, s_topk.scratch, &ctotal);
+      if (nw <= (int)blockDim.x) s_woff[tid] = excl;  // word tid is thread tid's only word
+    }
     if (tid == 0)
       for (int c = 0; c < C; ++c) cluster.map_shared_rank(s_ctotal, c)[crank] = ctotal;
     cluster.sync();  // totals exchanged; no shared memory of another CTA is read after this
@@ -951,16 +961,18 @@ select_rows_kernel(SelectArgs a) {
     if (crank == 0)
       for (int64_t p = tid; p < sink_hi; p += blockDim.x) dst[p] = (int32_t)p;
     for (int c0 = 0; c0 < nw; c0 += kTopPThreads) {
-      const int w = c0 + tid;
-      const uint32_t bits = w < nw ? s_words[w] : 0u;
-      uint32_t chunk_total;
-      s_woff[tid] = running + block_exclusive_scan((uint32_t)__popc(bits), s_topk.scratch, &chunk_total);
-      __syncthreads();
       const int chunk_words = min(kTopPThreads, nw - c0);
+      uint32_t chunk_total = ctotal;
+      if (nw > (int)blockDim.x) {  // several words per thread: offsets of this chunk
+        const int w = c0 + tid;
+        const uint32_t bits = w < nw ? s_words[w] : 0u;
+        s_woff[tid] = block_exclusive_scan((uint32_t)__popc(bits), s_topk.scratch, &chunk_total);
+        __syncthreads();
+      }
       for (int j = warp; j < chunk_words; j += nwarps) {
         const uint32_t word = s_words[c0 + j];
         if ((word >> lane) & 1u)
-          dst[sink_hi + s_woff[j] + __popc(word & ((1u << lane) - 1u))] =
+          dst[sink_hi + running + s_woff[j] + __popc(word & ((1u << lane) - 1u))] =
               (int32_t)(a.sink + (int64_t)(w_beg + c0 + j) * 32 + lane);
       }
       running += chunk_total;
