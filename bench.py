@@ -1417,18 +1417,19 @@ def run_cfg1(args) -> int:
 
 
 def run_single_extras(tw, device, K: int, W: int, link_peak: float | None) -> dict:
-    """cfg1 and cfg3 beside the 1-GPU headline line; a failure is recorded, not raised."""
+    """cfg1, cfg3 and ref3b beside the 1-GPU headline line; a failure is recorded, not raised."""
     out = {}
     try:
         out["cfg1"] = measure_cfg1(tw, device, min(K, 20), W, link_peak)
     except Exception as exc:  # recorded in the line: the headline stands on its own
         out["cfg1"] = {"error": f"{type(exc).__name__}: {exc}"}
-    try:
-        c3 = measure_cfg3(tw, device, "cfg3", reuse=False)
-        c3.pop("metric", None)
-        out["cfg3"] = c3
-    except Exception as exc:
-        out["cfg3"] = {"error": f"{type(exc).__name__}: {exc}"}
+    for name in ("cfg3", "ref3b"):
+        try:
+            line = measure_cfg3(tw, device, name, reuse=False)
+            line.pop("metric", None)
+            out[name] = line
+        except Exception as exc:
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"}
     return out
 
 
@@ -1674,8 +1675,8 @@ def main() -> int:
                     help="skip the cfg5 (head-sharded) and cfg4 (request-sharded batch) sub-runs "
                          "of the default workload")
     ap.add_argument("--no-extra-workloads", action="store_true",
-                    help="skip the cfg1 (per-head Quest layer) and cfg3 (full-model decode) "
-                         "sub-runs of the 1-GPU line")
+                    help="skip the cfg1 (per-head Quest layer), cfg3 and ref3b (full-model "
+                         "decode) sub-runs of the 1-GPU line")
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "ref3b"],
                     default="cfg2",
                     help="cfg1 (per-query-head Quest layer, 4096 tokens), "
