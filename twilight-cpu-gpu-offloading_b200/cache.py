@@ -552,15 +552,15 @@ class QuestTopKOffloadedCache:
         return out_k.view(total, 1, HEAD_DIM), out_v.view(total, 1, HEAD_DIM), cu, seg_len, lengths
 
     def _equal_cu_seqlens(self, segments: int, seg_len: int) -> torch.Tensor:
-        """arange(segments + 1) * seg_len as int32 on the device, kept for the
-        next call with the same shape (segment lengths stay fixed once the
-        recent window is full)."""
+        """arange(segments + 1) * seg_len as int32 on the device.  The values are
+        kept for the next call with the same shape (segment lengths stay fixed
+        once the recent window is full); each call returns its own copy."""
         key = (segments, seg_len)
         cached = getattr(self, "_cu_cache", None)
         if cached is None or cached[0] != key:
             cu = torch.arange(0, segments + 1, dtype=torch.int32, device=self.device) * seg_len
             self._cu_cache = (key, cu)
-        return self._cu_cache[1]
+        return self._cu_cache[1].clone()
 
     def _advance_layer(self, entries: list[int]) -> int:
         olds = []
