@@ -731,6 +731,10 @@ select_rows_kernel(SelectArgs a) {
   __shared__ uint32_t s_woff[kTopPThreads];
   __shared__ uint32_t s_ctotal[kSelMaxCluster];
   __shared__ uint32_t s_last;
+  // The query again for the INT4 phase, each 4-lane group's 32-channel slice
+  // rotated by 4 * slice: the four slices' 16-byte loads of one step then fall
+  // in four different bank groups (no bank conflict).
+  __shared__ __align__(16) float s_qx[kHeadDim];
 
   const int C = (int)cluster.num_blocks();
   const int crank = (int)cluster.block_rank();
@@ -787,9 +791,14 @@ select_rows_kernel(SelectArgs a) {
                 (size_t)(p_end - p_beg) * kHeadDim * sizeof(T));
   {
     const QT* qg = reinterpret_cast<const QT*>(a.q) + (int64_t)row * kHeadDim;
-    for (int i = tid; i < kHeadDim; i += blockDim.x) s_q[i] = to_f32(qg[i]);
+    for (int i = tid; i < kHeadDim; i += blockDim.x) {
+      const float v = to_f32(qg[i]);
+      s_q[i] = v;
+      const int slice = i >> 5;
+      s_qx[32 * slice + (((i & 31) + 4 * slice) & 31)] = v;
+    }
   }
-  __syncthreads();  // s_q
+  __syncthreads();  // s_q, s_qx
 
   // 1. Quest scores of the row's query head over the group's candidate pages.
   {
@@ -828,7 +837,13 @@ select_rows_kernel(SelectArgs a) {
     const int tok = lane >> 2;
     float qr[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) qr[i] = s_q[32 * sub + i];
+    for (int j = 0; j < 8; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(s_qx + 32 * sub + ((4 * j + 4 * sub) & 31));
+      qr[4 * j] = v.x;
+      qr[4 * j + 1] = v.y;
+      qr[4 * j + 2] = v.z;
+      qr[4 * j + 3] = v.w;
+    }
     const int grp = (32 * sub) / a.group_size;
     const int32_t* prow = s_pages;
     float* lout = cluster.map_shared_rank(s_logit, 0);
