@@ -79,14 +79,25 @@ __device__ __forceinline__ unsigned long long target_of(unsigned long long z, do
 constexpr int kTopPBins = 2048;
 constexpr int kTopPSmallBin = 256;
 
-// Top-p count and selection of one row, by the whole CTA (kTopPThreads threads).
-// lrow: the row's n logits (global or shared memory); keys may alias lrow
-// (each thread overwrites only the logits it has read).  On return sel[i] = 1
-// for the selected candidates; returns the count.
-__device__ int top_p_row(const float* lrow, int n, double top_p, uint32_t* keys,
-                         unsigned long long* mass, unsigned char* sel) {
-  __shared__ unsigned long long bin_mass[kTopPBins];
-  __shared__ uint32_t bin_cnt[kTopPBins];
+// The binned fixed-point mass histogram of a row's candidates: bin b of
+// candidate i is min(kTopPBins - 1, (lmax - logit_i) * kTopPBins / span).
+__device__ __forceinline__ float top_p_inv_width(float lmax, float lmin) {
+  const float span = __fsub_rn(lmax, lmin);
+  return span > 0.0f ? __fdiv_rn((float)kTopPBins, span) : 0.0f;
+}
+__device__ __forceinline__ int top_p_bin(float d, float inv_w) {
+  return min(kTopPBins - 1, (int)__fmul_rn(-d, inv_w));
+}
+
+// Top-p count and selection of one row from its keys, masses and mass
+// histogram, by the whole CTA (kTopPThreads threads).  keys [n]: the
+// order-preserving keys of the logits; mass [n]: mass_of(det_exp(logit - lmax));
+// bin_mass / bin_cnt [kTopPBins] (16-byte aligned): the histogram, whose total
+// is the row's total mass.  On return sel[i] = 1 for the selected candidates;
+// returns the count.
+__device__ int top_p_select(const uint32_t* keys, const unsigned long long* mass,
+                            unsigned char* sel, int n, double top_p, float lmax, float inv_w,
+                            const unsigned long long* bin_mass, const uint32_t* bin_cnt) {
   __shared__ unsigned long long list[kTopPSmallBin];
   __shared__ unsigned long long ranked[kTopPSmallBin];
   __shared__ unsigned long long hist_mass[256];
@@ -94,93 +105,53 @@ __device__ int top_p_row(const float* lrow, int n, double top_p, uint32_t* keys,
   __shared__ uint32_t scan_scratch[32];
   __shared__ unsigned long long scan64[32];
   __shared__ unsigned long long stage[kTopPThreads / 32][32];
-  __shared__ uint32_t s_prefix, s_cnt_gt, s_kmax, s_kmin, s_list_n;
+  __shared__ uint32_t s_prefix, s_cnt_gt, s_list_n, s_bcnt;
   __shared__ unsigned long long s_mass_gt, s_target;
   __shared__ int s_bstar, s_count;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int nwarps = blockDim.x >> 5;
-  for (int b = tid; b < kTopPBins; b += blockDim.x) {
-    bin_mass[b] = 0ull;
-    bin_cnt[b] = 0u;
-  }
   if (tid == 0) {
-    s_kmax = 0u;
-    s_kmin = 0xffffffffu;
     s_list_n = 0u;
     s_bstar = -1;
   }
-  __syncthreads();
-
-  // 1. keys, row max and min.
-  uint32_t kmax = 0u, kmin = 0xffffffffu;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const uint32_t k = float_key(lrow[i]);
-    keys[i] = k;
-    kmax = max(kmax, k);
-    kmin = min(kmin, k);
-  }
-  for (int off = 16; off > 0; off >>= 1) {
-    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
-    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
-  }
-  if (lane == 0) {
-    atomicMax(&s_kmax, kmax);
-    atomicMin(&s_kmin, kmin);
-  }
-  __syncthreads();
-  const float lmax = key_float(s_kmax);
-  const float span = __fsub_rn(lmax, key_float(s_kmin));
-  const float inv_w = span > 0.0f ? __fdiv_rn((float)kTopPBins, span) : 0.0f;
-
-  // 2. masses, their exact total and the binned mass histogram.
-  unsigned long long part = 0ull;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const float d = __fsub_rn(key_float(keys[i]), lmax);
-    const unsigned long long m = mass_of(det_exp((double)d));
-    mass[i] = m;
-    part += m;
-    const int b = min(kTopPBins - 1, (int)__fmul_rn(-d, inv_w));
-    atomicAdd(&bin_mass[b], m);
-    atomicAdd(&bin_cnt[b], 1u);
-  }
-  unsigned long long z;
-  block_exclusive_scan_u64(part, scan64, &z);
-  const unsigned long long target = target_of(z, top_p);
 
   // 3. crossing bin: bins in order (highest logits first), two per thread.
   constexpr int kBinsPerThread = kTopPBins / kTopPThreads;
-  unsigned long long bm_local = 0ull;
-  uint32_t bc_local = 0u;
-#pragma unroll
-  for (int j = 0; j < kBinsPerThread; ++j) {
-    bm_local += bin_mass[kBinsPerThread * tid + j];
-    bc_local += bin_cnt[kBinsPerThread * tid + j];
-  }
+  static_assert(kBinsPerThread == 2, "bins are read in pairs");
+  const ulonglong2 bm2 = reinterpret_cast<const ulonglong2*>(bin_mass)[tid];
+  const uint2 bc2 = reinterpret_cast<const uint2*>(bin_cnt)[tid];
+  const unsigned long long bm[kBinsPerThread] = {bm2.x, bm2.y};
+  const uint32_t bc[kBinsPerThread] = {bc2.x, bc2.y};
+  const unsigned long long bm_local = bm[0] + bm[1];
+  const uint32_t bc_local = bc[0] + bc[1];
+  unsigned long long z;
   unsigned long long mrun = block_exclusive_scan_u64(bm_local, scan64, &z);
   uint32_t ctotal;
   uint32_t crun = block_exclusive_scan(bc_local, scan_scratch, &ctotal);
+  const unsigned long long target = target_of(z, top_p);
 #pragma unroll
   for (int j = 0; j < kBinsPerThread; ++j) {
     const int b = kBinsPerThread * tid + j;
-    if (mrun < target && target <= mrun + bin_mass[b]) {
+    if (mrun < target && target <= mrun + bm[j]) {
       s_bstar = b;
+      s_bcnt = bc[j];
       s_mass_gt = mrun;
       s_cnt_gt = crun;
     }
-    mrun += bin_mass[b];
-    crun += bin_cnt[b];
+    mrun += bm[j];
+    crun += bc[j];
   }
   __syncthreads();
   const int bstar = s_bstar;
 
   int count;
-  if (bstar >= 0 && bin_cnt[bstar] <= (uint32_t)kTopPSmallBin) {
+  if (bstar >= 0 && s_bcnt <= (uint32_t)kTopPSmallBin) {
     // 4a. rank the crossing bin's candidates exactly and walk their masses.
     for (int i = tid; i < n; i += blockDim.x) {
       const float d = __fsub_rn(key_float(keys[i]), lmax);
-      const int b = min(kTopPBins - 1, (int)__fmul_rn(-d, inv_w));
+      const int b = top_p_bin(d, inv_w);
       sel[i] = b < bstar ? 1 : 0;
       if (b == bstar) list[atomicAdd(&s_list_n, 1u)] = rank_key(keys[i], i);
     }
@@ -344,6 +315,60 @@ __device__ int top_p_row(const float* lrow, int n, double top_p, uint32_t* keys,
   __syncthreads();
 
   return count;
+}
+
+// Top-p count and selection of one row, by the whole CTA (kTopPThreads threads).
+// lrow: the row's n logits (global or shared memory); keys may alias lrow
+// (each thread overwrites only the logits it has read).  On return sel[i] = 1
+// for the selected candidates; returns the count.
+__device__ int top_p_row(const float* lrow, int n, double top_p, uint32_t* keys,
+                         unsigned long long* mass, unsigned char* sel) {
+  __shared__ __align__(16) unsigned long long bin_mass[kTopPBins];
+  __shared__ __align__(16) uint32_t bin_cnt[kTopPBins];
+  __shared__ uint32_t s_kmax, s_kmin;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  for (int b = tid; b < kTopPBins; b += blockDim.x) {
+    bin_mass[b] = 0ull;
+    bin_cnt[b] = 0u;
+  }
+  if (tid == 0) {
+    s_kmax = 0u;
+    s_kmin = 0xffffffffu;
+  }
+  __syncthreads();
+
+  // 1. keys, row max and min.
+  uint32_t kmax = 0u, kmin = 0xffffffffu;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint32_t k = float_key(lrow[i]);
+    keys[i] = k;
+    kmax = max(kmax, k);
+    kmin = min(kmin, k);
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, off));
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
+  }
+  if (lane == 0) {
+    atomicMax(&s_kmax, kmax);
+    atomicMin(&s_kmin, kmin);
+  }
+  __syncthreads();
+  const float lmax = key_float(s_kmax);
+  const float inv_w = top_p_inv_width(lmax, key_float(s_kmin));
+
+  // 2. masses and the binned mass histogram.
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float d = __fsub_rn(key_float(keys[i]), lmax);
+    const unsigned long long m = mass_of(det_exp((double)d));
+    mass[i] = m;
+    const int b = top_p_bin(d, inv_w);
+    atomicAdd(&bin_mass[b], m);
+    atomicAdd(&bin_cnt[b], 1u);
+  }
+  __syncthreads();
+  return top_p_select(keys, mass, sel, n, top_p, lmax, inv_w, bin_mass, bin_cnt);
 }
 
 // ORs the row's selected positions (sel over its candidate pages prow) into
