@@ -126,10 +126,9 @@ __device__ int top_p_select(const uint32_t* keys, const unsigned long long* mass
   const uint32_t bc[kBinsPerThread] = {bc2.x, bc2.y};
   const unsigned long long bm_local = bm[0] + bm[1];
   const uint32_t bc_local = bc[0] + bc[1];
-  unsigned long long z;
-  unsigned long long mrun = block_exclusive_scan_u64(bm_local, scan64, &z);
-  uint32_t ctotal;
-  uint32_t crun = block_exclusive_scan(bc_local, scan_scratch, &ctotal);
+  unsigned long long z, mrun;
+  uint32_t ctotal, crun;
+  block_exclusive_scan_pair(bm_local, bc_local, scan64, scan_scratch, &mrun, &crun, &z, &ctotal);
   const unsigned long long target = target_of(z, top_p);
 #pragma unroll
   for (int j = 0; j < kBinsPerThread; ++j) {

@@ -353,6 +353,54 @@ __device__ __forceinline__ unsigned long long block_exclusive_scan_u64(
   return warp_base + x - v;
 }
 
+// block_exclusive_scan_u64 and block_exclusive_scan of two values at once (one
+// set of block barriers; scratch64 / scratch32: 32 entries each).
+__device__ __forceinline__ void block_exclusive_scan_pair(
+    unsigned long long v, uint32_t c, unsigned long long* scratch64, uint32_t* scratch32,
+    unsigned long long* prefix, uint32_t* cprefix, unsigned long long* total,
+    uint32_t* ctotal) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  unsigned long long x = v;
+  uint32_t xc = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, x, off);
+    const uint32_t yc = __shfl_up_sync(0xffffffffu, xc, off);
+    if (lane >= off) {
+      x += y;
+      xc += yc;
+    }
+  }
+  if (lane == 31) {
+    scratch64[warp] = x;
+    scratch32[warp] = xc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    unsigned long long w = (lane < nwarps) ? scratch64[lane] : 0ull;
+    uint32_t wc = (lane < nwarps) ? scratch32[lane] : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, w, off);
+      const uint32_t yc = __shfl_up_sync(0xffffffffu, wc, off);
+      if (lane >= off) {
+        w += y;
+        wc += yc;
+      }
+    }
+    scratch64[lane] = w;
+    scratch32[lane] = wc;
+  }
+  __syncthreads();
+  *prefix = ((warp > 0) ? scratch64[warp - 1] : 0ull) + x - v;
+  *cprefix = ((warp > 0) ? scratch32[warp - 1] : 0u) + xc - c;
+  *total = scratch64[nwarps - 1];
+  *ctotal = scratch32[nwarps - 1];
+  __syncthreads();
+}
+
 // In-place bitonic sort, descending, of n (a power of two) 64-bit keys in
 // shared memory by the whole block.  The caller synchronises before the call;
 // the sorted keys are visible to all threads on return.
